@@ -1,0 +1,99 @@
+"""Model shapes the engine runs (a runtime struct rather than the reference's hard-coded constants,
+foidfinder/backends/cuda/reference.py:12-17).
+
+- EVA02_L: BASELINE config 0/3, "PixAI-shaped EVA02-L/14": 448 px, patch 14, 1024 patches + class token,
+  24 blocks, dim 1024, 16 heads of 64, SwiGLU hidden 2730 with the EVA02 hidden LayerNorm, 2-D RoPE,
+  final LayerNorm, class-token linear head to 30,877 tags, pixel mean/std 0.5.
+- EVA02_B: the Haruka backbone shape (foidfinder/haruka.py:13-27): dim 768, 12 blocks, 12 heads,
+  hidden 2048, ImageNet mean/std, 98,782 tags.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, replace
+
+IMAGENET_MEAN = (0.485, 0.456, 0.406)
+IMAGENET_STD = (0.229, 0.224, 0.225)
+
+
+def _ceil(a: int, b: int) -> int:
+    return (a + b - 1) // b * b
+
+
+@dataclass(frozen=True)
+class ModelConfig:
+    name: str
+    image_size: int = 448
+    patch: int = 14
+    dim: int = 1024
+    depth: int = 24
+    heads: int = 16
+    mlp_hidden: int = 2730
+    num_tags: int = 30877
+    rope_ref_grid: int = 16
+    ln_eps: float = 1e-6
+    mean: tuple[float, float, float] = (0.5, 0.5, 0.5)
+    std: tuple[float, float, float] = (0.5, 0.5, 0.5)
+    rot_block_dim: int = 1024  # Hadamard block of the dim-wide GEMM inputs (qkv, proj, fc1)
+    rot_block_hidden: int = 128  # Hadamard block of the hidden-wide GEMM input (fc2)
+    topk: int = 50
+
+    @property
+    def grid(self) -> int:
+        return self.image_size // self.patch
+
+    @property
+    def patches(self) -> int:
+        return self.grid * self.grid
+
+    @property
+    def tokens(self) -> int:
+        return self.patches + 1
+
+    @property
+    def head_dim(self) -> int:
+        return self.dim // self.heads
+
+    @property
+    def mlp_hidden_pad(self) -> int:
+        return _ceil(self.mlp_hidden, 128)
+
+    @property
+    def num_tags_pad(self) -> int:
+        return _ceil(self.num_tags, 256)
+
+    @property
+    def k_patch(self) -> int:
+        return self.patch * self.patch * 3
+
+    @property
+    def k_pad(self) -> int:
+        return _ceil(self.k_patch, 64)
+
+    def gemm_ops_per_image(self, padded: bool = False) -> int:
+        """Int8 multiply-adds x 2 of the four block GEMMs per image (qkv, proj, gate|up, down)."""
+        h = self.mlp_hidden_pad if padded else self.mlp_hidden
+        per_token = self.dim * 3 * self.dim + self.dim * self.dim + self.dim * 2 * h + h * self.dim
+        return 2 * self.tokens * self.depth * per_token
+
+    def attention_flops_per_image(self) -> int:
+        return 4 * self.heads * self.tokens * self.tokens * self.head_dim * self.depth
+
+    def with_(self, **kw) -> ModelConfig:
+        return replace(self, **kw)
+
+
+EVA02_L = ModelConfig("eva02-l-448")
+EVA02_B = ModelConfig(
+    "eva02-b-448",
+    dim=768,
+    depth=12,
+    heads=12,
+    mlp_hidden=2048,
+    num_tags=98782,
+    mean=IMAGENET_MEAN,
+    std=IMAGENET_STD,
+    rot_block_dim=256,
+)
+
+CONFIGS = {c.name: c for c in (EVA02_L, EVA02_B)}

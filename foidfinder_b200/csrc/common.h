@@ -1,0 +1,38 @@
+// Host-side helpers shared by the C-ABI translation units: status codes, the thread-local error
+// string, device properties and TMA descriptor encoding through the driver entry point.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "../../include/foidfinder_b200.h"
+
+namespace ff {
+
+void set_error(const char* fmt, ...);
+
+// Returns FF_ERR_LAUNCH (and records the CUDA error) when the last launch failed.
+int check_launch(const char* what);
+
+int sm_count();  // of the current device
+
+// Per-device error word that kernels with bounded waits write (allocated on first use, held until exit).
+int* device_error_word();
+
+// 2-D tensor map over a row-major [outer, inner] matrix, 128-byte swizzle, box {box_inner, box_outer}.
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elt_bytes, uint64_t inner,
+                 uint64_t outer, uint32_t box_inner, uint32_t box_outer);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace ff
+
+#define FF_REQUIRE(cond, ...)         \
+  do {                                \
+    if (!(cond)) {                    \
+      ::ff::set_error(__VA_ARGS__);   \
+      return FF_ERR_INVALID_ARGUMENT; \
+    }                                 \
+  } while (0)

@@ -1,0 +1,391 @@
+// Whole-model int8 engine behind the C ABI: one object per device, activation buffers and a CUDA graph
+// per batch size, weights owned by the caller.
+//
+// The layer loop follows PixAICuda._forward (foidfinder/backends/cuda/engine.py:142-161) with the EVA02
+// block of foidfinder/backends/mlx/haruka.py:86-99:
+//   per block: LN1+H(dim)+q8 -> QKV GEMM (+bias, 2-D RoPE) -> attention -> H(dim)+q8 -> proj GEMM
+//              (+bias, residual) -> LN2+H(dim)+q8 -> gate|up GEMM (+bias, SwiGLU) -> mlp LN+H128+q8 ->
+//              down GEMM (+bias, residual)
+// followed by the final LayerNorm of the class tokens, the fp16 tag head and a device top-k.
+// Graph capture per batch size replaces the torch.cuda.graph capture of engine.py:163-184.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <map>
+#include <mutex>
+#include <vector>
+
+#include "common.h"
+#include "gemm.h"
+#include "kernels.h"
+
+struct ff_engine {
+  struct Batch {
+    int B = 0;
+    void* block = nullptr;  // one allocation for every activation buffer below
+    uint8_t* images = nullptr;
+    __half* patches = nullptr;
+    __half* x = nullptr;
+    int8_t* a8 = nullptr;
+    float* rs = nullptr;
+    __half* qkv = nullptr;
+    __half* o = nullptr;
+    __half* h = nullptr;
+    __half* cls = nullptr;
+    float* logits = nullptr;
+    int32_t* top_idx = nullptr;
+    float* top_val = nullptr;
+    ff::GemmPlan stem, head;
+    std::vector<ff::GemmPlan> qkv_p, proj_p, fc1_p, fc2_p;
+    cudaGraphExec_t exec = nullptr;
+    cudaStream_t capture_stream = nullptr;
+  };
+  ff_model_config cfg{};
+  ff_model_weights w{};
+  std::vector<ff_layer_weights> layers;
+  int device = 0;
+  int grid = 0, patches = 0, tokens = 0, k_pad = 0;
+  std::map<int, Batch*> batches;
+  std::mutex mu;
+};
+
+namespace ff {
+namespace {
+
+struct DeviceScope {
+  int prev = 0;
+  explicit DeviceScope(int dev) {
+    cudaGetDevice(&prev);
+    cudaSetDevice(dev);
+  }
+  ~DeviceScope() { cudaSetDevice(prev); }
+};
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+struct Layout {
+  size_t images, patches, x, a8, rs, qkv, o, h, cls, logits, top_idx, top_val, total;
+};
+
+Layout layout_for(const ff_model_config& c, int B) {
+  const size_t G = c.image_size / c.patch, P = G * G, T = P + 1, M = static_cast<size_t>(B) * T;
+  const size_t kpad = align_up(static_cast<size_t>(c.patch) * c.patch * 3, 64);
+  const size_t wide = std::max<size_t>(c.dim, c.mlp_hidden_pad);
+  Layout l{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = align_up(off + bytes, 1024);
+    return at;
+  };
+  l.images = take(static_cast<size_t>(B) * c.image_size * c.image_size * 3);
+  l.patches = take(static_cast<size_t>(B) * P * kpad * 2);
+  l.x = take(M * c.dim * 2);
+  l.a8 = take(M * wide);
+  l.rs = take(M * 4);
+  l.qkv = take(M * 3 * c.dim * 2);
+  l.o = take(M * c.dim * 2);
+  l.h = take(M * c.mlp_hidden_pad * 2);
+  l.cls = take(static_cast<size_t>(B) * c.dim * 2);
+  l.logits = take(static_cast<size_t>(B) * c.num_tags * 4);
+  l.top_idx = take(static_cast<size_t>(B) * (c.topk > 0 ? c.topk : 1) * 4);
+  l.top_val = take(static_cast<size_t>(B) * (c.topk > 0 ? c.topk : 1) * 4);
+  l.total = off;
+  return l;
+}
+
+int validate(const ff_model_config& c) {
+  FF_REQUIRE(c.patch >= 1 && c.image_size % c.patch == 0, "engine: image_size %d not a multiple of patch %d", c.image_size, c.patch);
+  FF_REQUIRE(c.dim == 768 || c.dim == 1024, "engine: dim %d (supported: 768, 1024)", c.dim);
+  FF_REQUIRE(c.heads * 64 == c.dim, "engine: heads * 64 must equal dim");
+  FF_REQUIRE(c.depth >= 1, "engine: depth %d", c.depth);
+  FF_REQUIRE(c.mlp_hidden >= 1 && c.mlp_hidden <= c.mlp_hidden_pad && c.mlp_hidden_pad % 128 == 0,
+             "engine: mlp_hidden %d / pad %d", c.mlp_hidden, c.mlp_hidden_pad);
+  FF_REQUIRE(c.mlp_hidden_pad == 2048 || c.mlp_hidden_pad == 2816 || c.mlp_hidden_pad == 4096,
+             "engine: mlp_hidden_pad %d has no rotation kernel", c.mlp_hidden_pad);
+  FF_REQUIRE(c.num_tags >= 1 && c.num_tags <= c.num_tags_pad && c.num_tags_pad % 256 == 0,
+             "engine: num_tags %d / pad %d", c.num_tags, c.num_tags_pad);
+  FF_REQUIRE(c.dim % c.rot_block_dim == 0 && c.mlp_hidden_pad % c.rot_block_hidden == 0, "engine: rotation blocks");
+  FF_REQUIRE(c.topk >= 0 && c.topk <= 64 && c.topk <= c.num_tags, "engine: topk %d", c.topk);
+  return FF_OK;
+}
+
+int build_batch(ff_engine* e, int B, ff_engine::Batch** out) {
+  const ff_model_config& c = e->cfg;
+  const Layout l = layout_for(c, B);
+  auto* b = new ff_engine::Batch();
+  b->B = B;
+  if (cudaMalloc(&b->block, l.total) != cudaSuccess) {
+    delete b;
+    cudaGetLastError();
+    set_error("engine: cudaMalloc of %zu bytes for batch %d failed", l.total, B);
+    return FF_ERR_OUT_OF_MEMORY;
+  }
+  uint8_t* base = static_cast<uint8_t*>(b->block);
+  b->images = base + l.images;
+  b->patches = reinterpret_cast<__half*>(base + l.patches);
+  b->x = reinterpret_cast<__half*>(base + l.x);
+  b->a8 = reinterpret_cast<int8_t*>(base + l.a8);
+  b->rs = reinterpret_cast<float*>(base + l.rs);
+  b->qkv = reinterpret_cast<__half*>(base + l.qkv);
+  b->o = reinterpret_cast<__half*>(base + l.o);
+  b->h = reinterpret_cast<__half*>(base + l.h);
+  b->cls = reinterpret_cast<__half*>(base + l.cls);
+  b->logits = reinterpret_cast<float*>(base + l.logits);
+  b->top_idx = reinterpret_cast<int32_t*>(base + l.top_idx);
+  b->top_val = reinterpret_cast<float*>(base + l.top_val);
+  cudaMemset(b->block, 0, l.total);
+
+  const int M = B * e->tokens, D = c.dim, H = c.mlp_hidden_pad;
+  int rc = FF_OK;
+  {
+    GemmProblem p{};
+    p.A = b->patches;
+    p.W = e->w.patch_w;
+    p.out = b->x;
+    p.M = B * e->patches;
+    p.N = D;
+    p.K = e->k_pad;
+    p.epi = EPI_STEM;
+    p.f16 = true;
+    p.args.ldo = D;
+    p.args.pos_bias = e->w.pos_bias;
+    p.args.patches = e->patches;
+    p.args.tokens = e->tokens;
+    rc = gemm_prepare(p, &b->stem);
+  }
+  if (rc == FF_OK) {
+    GemmProblem p{};
+    p.A = b->cls;
+    p.W = e->w.head_w;
+    p.out = b->logits;
+    p.M = B;
+    p.N = c.num_tags_pad;
+    p.K = D;
+    p.epi = EPI_LOGITS;
+    p.f16 = true;
+    p.args.bias = e->w.head_b;
+    p.args.ldo = c.num_tags;
+    p.args.n_valid = c.num_tags;
+    rc = gemm_prepare(p, &b->head);
+  }
+  b->qkv_p.resize(c.depth);
+  b->proj_p.resize(c.depth);
+  b->fc1_p.resize(c.depth);
+  b->fc2_p.resize(c.depth);
+  for (int i = 0; i < c.depth && rc == FF_OK; ++i) {
+    const ff_layer_weights& lw = e->layers[i];
+    auto prep = [&](GemmPlan* plan, const int8_t* W, const float* s, const float* bias, void* out, int N, int K, int epi) {
+      GemmProblem p{};
+      p.A = b->a8;
+      p.W = W;
+      p.out = out;
+      p.M = M;
+      p.N = N;
+      p.K = K;
+      p.epi = epi;
+      p.f16 = false;
+      p.args.row_scale = b->rs;
+      p.args.col_scale = s;
+      p.args.bias = bias;
+      p.args.ldo = epi == EPI_SWIGLU ? N / 2 : N;
+      p.args.rope_cos = e->w.rope_cos;
+      p.args.rope_sin = e->w.rope_sin;
+      p.args.rope_cols = epi == EPI_QKV_ROPE ? 2 * D : 0;
+      p.args.tokens = e->tokens;
+      return gemm_prepare(p, plan);
+    };
+    rc = prep(&b->qkv_p[i], lw.qkv_w, lw.qkv_s, lw.qkv_b, b->qkv, 3 * D, D, EPI_QKV_ROPE);
+    if (rc == FF_OK) rc = prep(&b->proj_p[i], lw.proj_w, lw.proj_s, lw.proj_b, b->x, D, D, EPI_RESIDUAL);
+    if (rc == FF_OK) rc = prep(&b->fc1_p[i], lw.fc1_w, lw.fc1_s, lw.fc1_b, b->h, 2 * H, D, EPI_SWIGLU);
+    if (rc == FF_OK) rc = prep(&b->fc2_p[i], lw.fc2_w, lw.fc2_s, lw.fc2_b, b->x, D, H, EPI_RESIDUAL);
+  }
+  if (rc != FF_OK) {
+    cudaFree(b->block);
+    delete b;
+    return rc;
+  }
+  *out = b;
+  return FF_OK;
+}
+
+#define FF_TRY(expr)             \
+  do {                           \
+    const int rc_ = (expr);      \
+    if (rc_ != FF_OK) return rc_; \
+  } while (0)
+
+// Every launch of one forward of batch b on stream s.
+int run_forward(ff_engine* e, ff_engine::Batch* b, cudaStream_t s) {
+  const ff_model_config& c = e->cfg;
+  const int B = b->B, M = B * e->tokens, D = c.dim, H = c.mlp_hidden_pad;
+  FF_TRY(patchify(b->images, B, c.image_size, c.patch, c.mean, c.std, b->patches, e->k_pad, s));
+  FF_TRY(gemm_launch(b->stem, s));
+  FF_TRY(fill_cls(e->w.cls_row, b->x, B, e->tokens, D, s));
+  for (int i = 0; i < c.depth; ++i) {
+    const ff_layer_weights& lw = e->layers[i];
+    FF_TRY(rot_q8(b->x, lw.norm1_w, lw.norm1_b, c.ln_eps, M, D, D, c.rot_block_dim, b->a8, b->rs, s));
+    FF_TRY(gemm_launch(b->qkv_p[i], s));
+    FF_TRY(attention(b->qkv, b->o, B, e->tokens, c.heads, nullptr, nullptr, 1.f, s));
+    FF_TRY(rot_q8(b->o, nullptr, nullptr, 0.f, M, D, D, c.rot_block_dim, b->a8, b->rs, s));
+    FF_TRY(gemm_launch(b->proj_p[i], s));
+    FF_TRY(rot_q8(b->x, lw.norm2_w, lw.norm2_b, c.ln_eps, M, D, D, c.rot_block_dim, b->a8, b->rs, s));
+    FF_TRY(gemm_launch(b->fc1_p[i], s));
+    FF_TRY(rot_q8(b->h, lw.mlp_norm_w, lw.mlp_norm_b, c.ln_eps, M, H, c.mlp_hidden, c.rot_block_hidden, b->a8, b->rs, s));
+    FF_TRY(gemm_launch(b->fc2_p[i], s));
+  }
+  FF_TRY(layernorm(b->x, static_cast<int64_t>(e->tokens) * D, e->w.norm_w, e->w.norm_b, c.ln_eps, B, D, b->cls, s));
+  FF_TRY(gemm_launch(b->head, s));
+  if (c.topk > 0) FF_TRY(topk(b->logits, B, c.num_tags, c.topk, b->top_idx, b->top_val, s));
+  return FF_OK;
+}
+
+int copy_out(ff_engine* e, ff_engine::Batch* b, float* logits, int32_t* top_idx, float* top_val, cudaStream_t s) {
+  const ff_model_config& c = e->cfg;
+  const int B = b->B;
+  if (logits && cudaMemcpyAsync(logits, b->logits, static_cast<size_t>(B) * c.num_tags * 4, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+    return check_launch("engine: logits copy");
+  if (c.topk > 0 && top_idx &&
+      cudaMemcpyAsync(top_idx, b->top_idx, static_cast<size_t>(B) * c.topk * 4, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+    return check_launch("engine: top-k index copy");
+  if (c.topk > 0 && top_val &&
+      cudaMemcpyAsync(top_val, b->top_val, static_cast<size_t>(B) * c.topk * 4, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+    return check_launch("engine: top-k value copy");
+  return FF_OK;
+}
+
+int get_batch(ff_engine* e, int B, ff_engine::Batch** out) {
+  auto it = e->batches.find(B);
+  if (it != e->batches.end()) {
+    *out = it->second;
+    return FF_OK;
+  }
+  ff_engine::Batch* b = nullptr;
+  FF_TRY(build_batch(e, B, &b));
+  e->batches[B] = b;
+  *out = b;
+  return FF_OK;
+}
+
+int check_inputs(ff_engine* e, const uint8_t* images, int B, float* logits, int32_t* top_idx) {
+  FF_REQUIRE(e != nullptr, "engine: NULL handle");
+  FF_REQUIRE(images != nullptr && B >= 1, "engine: need images and B >= 1");
+  FF_REQUIRE(logits != nullptr || top_idx != nullptr, "engine: no output requested");
+  FF_REQUIRE(top_idx == nullptr || e->cfg.topk > 0, "engine: top-k requested but cfg.topk is 0");
+  return FF_OK;
+}
+
+}  // namespace
+}  // namespace ff
+
+using namespace ff;
+
+extern "C" int64_t ff_engine_workspace_bytes(const ff_model_config* cfg, int B) {
+  if (cfg == nullptr || B < 1) return -1;
+  return static_cast<int64_t>(layout_for(*cfg, B).total);
+}
+
+extern "C" int ff_engine_create(const ff_model_config* cfg, const ff_model_weights* w, int device, ff_engine** out) {
+  FF_REQUIRE(cfg && w && out, "ff_engine_create: NULL argument");
+  FF_TRY(validate(*cfg));
+  FF_REQUIRE(w->patch_w && w->pos_bias && w->cls_row && w->rope_cos && w->rope_sin && w->layers && w->norm_w &&
+                 w->norm_b && w->head_w && w->head_b,
+             "ff_engine_create: a model weight pointer is NULL");
+  for (int i = 0; i < cfg->depth; ++i) {
+    const ff_layer_weights& l = w->layers[i];
+    FF_REQUIRE(l.norm1_w && l.norm1_b && l.qkv_w && l.qkv_s && l.qkv_b && l.proj_w && l.proj_s && l.proj_b &&
+                   l.norm2_w && l.norm2_b && l.fc1_w && l.fc1_s && l.fc1_b && l.mlp_norm_w && l.mlp_norm_b && l.fc2_w &&
+                   l.fc2_s && l.fc2_b,
+               "ff_engine_create: layer %d has a NULL weight pointer", i);
+  }
+  int ndev = 0;
+  cudaGetDeviceCount(&ndev);
+  FF_REQUIRE(device >= 0 && device < ndev, "ff_engine_create: device %d of %d", device, ndev);
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess || prop.major != 10) {
+    set_error("ff_engine_create: device %d is not sm_100 (compute capability %d.%d)", device, prop.major, prop.minor);
+    return FF_ERR_UNSUPPORTED_DEVICE;
+  }
+  auto* e = new ff_engine();
+  e->cfg = *cfg;
+  e->w = *w;
+  e->layers.assign(w->layers, w->layers + cfg->depth);
+  e->w.layers = e->layers.data();
+  e->device = device;
+  e->grid = cfg->image_size / cfg->patch;
+  e->patches = e->grid * e->grid;
+  e->tokens = e->patches + 1;
+  e->k_pad = static_cast<int>(align_up(static_cast<size_t>(cfg->patch) * cfg->patch * 3, 64));
+  *out = e;
+  return FF_OK;
+}
+
+extern "C" int ff_engine_forward_eager(ff_engine* e, const uint8_t* images, int B, float* logits, int32_t* top_idx,
+                                       float* top_val, void* stream) {
+  FF_TRY(check_inputs(e, images, B, logits, top_idx));
+  std::lock_guard<std::mutex> lock(e->mu);
+  DeviceScope scope(e->device);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ff_engine::Batch* b = nullptr;
+  FF_TRY(get_batch(e, B, &b));
+  const size_t in_bytes = static_cast<size_t>(B) * e->cfg.image_size * e->cfg.image_size * 3;
+  if (cudaMemcpyAsync(b->images, images, in_bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+    return check_launch("engine: image copy");
+  FF_TRY(run_forward(e, b, s));
+  return copy_out(e, b, logits, top_idx, top_val, s);
+}
+
+extern "C" int ff_engine_forward(ff_engine* e, const uint8_t* images, int B, float* logits, int32_t* top_idx,
+                                 float* top_val, void* stream) {
+  FF_TRY(check_inputs(e, images, B, logits, top_idx));
+  std::lock_guard<std::mutex> lock(e->mu);
+  DeviceScope scope(e->device);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ff_engine::Batch* b = nullptr;
+  FF_TRY(get_batch(e, B, &b));
+  if (b->exec == nullptr) {
+    // Warm up outside capture (kernel attributes, module loading), then capture on a private stream.
+    if (cudaStreamCreateWithFlags(&b->capture_stream, cudaStreamNonBlocking) != cudaSuccess)
+      return check_launch("engine: stream create");
+    FF_TRY(run_forward(e, b, b->capture_stream));
+    if (cudaStreamSynchronize(b->capture_stream) != cudaSuccess) return check_launch("engine: warm-up forward");
+    cudaGraph_t graph = nullptr;
+    if (cudaStreamBeginCapture(b->capture_stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+      return check_launch("engine: begin capture");
+    const int rc = run_forward(e, b, b->capture_stream);
+    const cudaError_t ce = cudaStreamEndCapture(b->capture_stream, &graph);
+    if (rc != FF_OK) {
+      if (graph) cudaGraphDestroy(graph);
+      return rc;
+    }
+    if (ce != cudaSuccess) return check_launch("engine: end capture");
+    const cudaError_t ie = cudaGraphInstantiate(&b->exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ie != cudaSuccess) {
+      b->exec = nullptr;
+      return check_launch("engine: graph instantiate");
+    }
+  }
+  const size_t in_bytes = static_cast<size_t>(B) * e->cfg.image_size * e->cfg.image_size * 3;
+  if (cudaMemcpyAsync(b->images, images, in_bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+    return check_launch("engine: image copy");
+  if (cudaGraphLaunch(b->exec, s) != cudaSuccess) return check_launch("engine: graph launch");
+  return copy_out(e, b, logits, top_idx, top_val, s);
+}
+
+extern "C" int ff_engine_destroy(ff_engine* e) {
+  if (e == nullptr) return FF_OK;
+  {
+    DeviceScope scope(e->device);
+    cudaDeviceSynchronize();
+    for (auto& kv : e->batches) {
+      ff_engine::Batch* b = kv.second;
+      if (b->exec) cudaGraphExecDestroy(b->exec);
+      if (b->capture_stream) cudaStreamDestroy(b->capture_stream);
+      cudaFree(b->block);
+      delete b;
+    }
+  }
+  delete e;
+  return FF_OK;
+}

@@ -1,0 +1,167 @@
+// Host side of the tcgen05 GEMM: argument checks, TMA descriptors, tile-shape choice and launch.
+#include "common.h"
+#include "gemm.h"
+#include "gemm_tc.cuh"
+
+namespace ff {
+
+namespace {
+
+template <int BN, int STAGES, bool F16IN, int EPI>
+int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, cudaStream_t stream) {
+  using C = GemmCfg<BN, STAGES>;
+  auto kernel = gemm_tc_kernel<BN, STAGES, F16IN, EPI>;
+  static bool configured[64] = {};  // per instantiation and device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+      return check_launch("gemm: cudaFuncSetAttribute");
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  const int tiles = a.tiles_m * (a.N / BN);
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  kernel<<<grid, 192, C::SMEM, stream>>>(ta, tb, a);
+  return check_launch("gemm_tc_kernel");
+}
+
+template <int BN, bool F16IN>
+int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, cudaStream_t s) {
+  constexpr int STAGES = BN == 256 ? 4 : 6;
+  if constexpr (F16IN) {
+    switch (epi) {
+      case EPI_STEM: return launch_one<BN, STAGES, true, EPI_STEM>(ta, tb, a, s);
+      case EPI_LOGITS: return launch_one<BN, STAGES, true, EPI_LOGITS>(ta, tb, a, s);
+    }
+  } else {
+    switch (epi) {
+      case EPI_QKV_ROPE: return launch_one<BN, STAGES, false, EPI_QKV_ROPE>(ta, tb, a, s);
+      case EPI_RESIDUAL: return launch_one<BN, STAGES, false, EPI_RESIDUAL>(ta, tb, a, s);
+      case EPI_SWIGLU: return launch_one<BN, STAGES, false, EPI_SWIGLU>(ta, tb, a, s);
+      case EPI_BIAS: return launch_one<BN, STAGES, false, EPI_BIAS>(ta, tb, a, s);
+      case EPI_S32: return launch_one<BN, STAGES, false, EPI_S32>(ta, tb, a, s);
+    }
+  }
+  set_error("gemm: epilogue %d is not available for %s inputs", epi, F16IN ? "fp16" : "int8");
+  return FF_ERR_INVALID_ARGUMENT;
+}
+
+}  // namespace
+
+int choose_tile_n(int M, int N) {
+  // Prefer 256-wide tiles; drop to 128 when 256 would leave most SMs idle (small M) or N needs it.
+  if (N % 256 != 0) return 128;
+  const int tiles256 = ((M + 127) / 128) * (N / 256);
+  return tiles256 * 2 <= sm_count() ? 128 : 256;
+}
+
+int gemm_prepare(const GemmProblem& p, GemmPlan* plan) {
+  const bool f16 = p.f16;
+  const int elt = f16 ? 2 : 1;
+  FF_REQUIRE(p.A != nullptr && p.W != nullptr && p.out != nullptr, "gemm: NULL operand");
+  FF_REQUIRE(p.M >= 1 && p.N >= 1 && p.K >= 1, "gemm: bad shape M=%d N=%d K=%d", p.M, p.N, p.K);
+  FF_REQUIRE((static_cast<int64_t>(p.K) * elt) % 128 == 0, "gemm: K*%d bytes must be a multiple of 128 (K=%d)", elt, p.K);
+  FF_REQUIRE(aligned16(p.A) && aligned16(p.W), "gemm: A and W must be 16-byte aligned");
+  int bn = p.tile_n == 0 ? choose_tile_n(p.M, p.N) : p.tile_n;
+  FF_REQUIRE(bn == 128 || bn == 256, "gemm: tile_n must be 0, 128 or 256 (got %d)", p.tile_n);
+  FF_REQUIRE(p.N % bn == 0, "gemm: N=%d must be a multiple of the tile width %d", p.N, bn);
+  const CUtensorMapDataType dt = f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const uint32_t box_k = 128 / elt;
+  int rc = make_tmap_2d(&plan->ta, p.A, dt, elt, static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.M), box_k, 128);
+  if (rc != FF_OK) return rc;
+  rc = make_tmap_2d(&plan->tb, p.W, dt, elt, static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.N), box_k,
+                    static_cast<uint32_t>(bn));
+  if (rc != FF_OK) return rc;
+  plan->args = p.args;
+  plan->args.M = p.M;
+  plan->args.N = p.N;
+  plan->args.K = p.K;
+  plan->args.num_kb = static_cast<int>((static_cast<int64_t>(p.K) * elt) / 128);
+  plan->args.tiles_m = (p.M + 127) / 128;
+  plan->args.out = p.out;
+  plan->args.err = device_error_word();
+  FF_REQUIRE(plan->args.err != nullptr, "gemm: no device error word");
+  plan->bn = bn;
+  plan->f16 = f16;
+  plan->epi = p.epi;
+  return FF_OK;
+}
+
+int gemm_launch(const GemmPlan& plan, cudaStream_t stream) {
+  if (plan.f16)
+    return plan.bn == 256 ? dispatch_epi<256, true>(plan.epi, plan.ta, plan.tb, plan.args, stream)
+                          : dispatch_epi<128, true>(plan.epi, plan.ta, plan.tb, plan.args, stream);
+  return plan.bn == 256 ? dispatch_epi<256, false>(plan.epi, plan.ta, plan.tb, plan.args, stream)
+                        : dispatch_epi<128, false>(plan.epi, plan.ta, plan.tb, plan.args, stream);
+}
+
+}  // namespace ff
+
+using namespace ff;
+
+extern "C" int ff_gemm_s8(const int8_t* A, const int8_t* W, const float* row_scale, const float* col_scale,
+                          const float* bias, void* out, int M, int N, int K, int epi, const float* rope_cos,
+                          const float* rope_sin, int rope_cols, int tokens, int tile_n, void* stream) {
+  FF_REQUIRE(epi == EPI_QKV_ROPE || epi == EPI_RESIDUAL || epi == EPI_SWIGLU || epi == EPI_BIAS || epi == EPI_S32,
+             "ff_gemm_s8: unknown epilogue %d", epi);
+  if (epi != EPI_S32) FF_REQUIRE(row_scale && col_scale && bias, "ff_gemm_s8: scales and bias are required");
+  FF_REQUIRE(N % 128 == 0, "ff_gemm_s8: N=%d must be a multiple of 128", N);
+  if (epi == EPI_QKV_ROPE) {
+    FF_REQUIRE(rope_cos && rope_sin && tokens >= 1, "ff_gemm_s8: QKV epilogue needs RoPE tables and tokens");
+    FF_REQUIRE(rope_cols % 64 == 0 && rope_cols >= 0 && rope_cols <= N, "ff_gemm_s8: bad rope_cols %d", rope_cols);
+  }
+  GemmProblem p{};
+  p.A = A;
+  p.W = W;
+  p.out = out;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.epi = epi;
+  p.tile_n = tile_n;
+  p.f16 = false;
+  p.args.row_scale = row_scale;
+  p.args.col_scale = col_scale;
+  p.args.bias = bias;
+  p.args.ldo = epi == EPI_SWIGLU ? N / 2 : N;
+  p.args.rope_cos = rope_cos;
+  p.args.rope_sin = rope_sin;
+  p.args.rope_cols = epi == EPI_QKV_ROPE ? rope_cols : 0;
+  p.args.tokens = tokens > 0 ? tokens : 1;
+  GemmPlan plan;
+  int rc = gemm_prepare(p, &plan);
+  if (rc != FF_OK) return rc;
+  return gemm_launch(plan, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ff_gemm_f16(const uint16_t* A, const uint16_t* W, const float* bias, void* out, int M, int N, int K,
+                           int epi, int ldo, int n_valid, const float* pos_bias, int patches, int tokens, int tile_n,
+                           void* stream) {
+  FF_REQUIRE(epi == EPI_STEM || epi == EPI_LOGITS, "ff_gemm_f16: unknown epilogue %d", epi);
+  if (epi == EPI_STEM) {
+    FF_REQUIRE(pos_bias != nullptr && patches >= 1 && tokens >= patches + 1, "ff_gemm_f16: stem needs pos_bias, patches, tokens");
+    FF_REQUIRE(ldo >= N && ldo % 8 == 0, "ff_gemm_f16: stem ldo %d", ldo);
+  } else {
+    FF_REQUIRE(bias != nullptr && n_valid >= 1 && n_valid <= N && ldo >= n_valid, "ff_gemm_f16: logits need bias, n_valid <= N, ldo >= n_valid");
+  }
+  GemmProblem p{};
+  p.A = A;
+  p.W = W;
+  p.out = out;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.epi = epi;
+  p.tile_n = tile_n;
+  p.f16 = true;
+  p.args.bias = bias;
+  p.args.ldo = ldo;
+  p.args.n_valid = n_valid;
+  p.args.pos_bias = pos_bias;
+  p.args.patches = patches;
+  p.args.tokens = tokens;
+  GemmPlan plan;
+  int rc = gemm_prepare(p, &plan);
+  if (rc != FF_OK) return rc;
+  return gemm_launch(plan, static_cast<cudaStream_t>(stream));
+}

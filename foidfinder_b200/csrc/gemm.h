@@ -1,0 +1,34 @@
+// Internal GEMM planning API: the engine encodes TMA descriptors once per buffer (gemm_prepare) and
+// replays the launch (gemm_launch) inside its CUDA graph.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "gemm_args.h"
+
+namespace ff {
+
+struct GemmProblem {
+  const void* A;
+  const void* W;
+  void* out;
+  int M, N, K;
+  int epi;
+  int tile_n;  // 0 = automatic
+  bool f16;
+  GemmArgs args;  // epilogue fields; M/N/K/num_kb/tiles_m/out/err are filled in by gemm_prepare
+};
+
+struct GemmPlan {
+  CUtensorMap ta, tb;
+  GemmArgs args;
+  int bn;
+  bool f16;
+  int epi;
+};
+
+int choose_tile_n(int M, int N);
+int gemm_prepare(const GemmProblem& p, GemmPlan* plan);
+int gemm_launch(const GemmPlan& plan, cudaStream_t stream);
+
+}  // namespace ff

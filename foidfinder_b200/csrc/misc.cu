@@ -1,0 +1,234 @@
+// Stem input preparation, the final LayerNorm and the device top-k of the tag logits.
+#include "common.h"
+#include "ptx.cuh"
+
+namespace ff {
+
+// ---------------------------------------------------------------- patchify
+// images [B, S, S, 3] uint8 -> patches [B * G * G, k_pad] fp16, column k = (kh * p + kw) * 3 + c
+// (the (kh, kw, c) order of reference.py:103-107 and mlx/haruka.py:78), value (px / 255 - mean) / std.
+__global__ void patchify_kernel(const uint8_t* __restrict__ img, int B, int S, int p, float m0, float m1, float m2,
+                                float is0, float is1, float is2, __half* __restrict__ out, int k_pad) {
+  const int G = S / p, P = G * G, kreal = p * p * 3;
+  const int64_t total = static_cast<int64_t>(B) * P * k_pad;
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int k = static_cast<int>(t % k_pad);
+    const int64_t row = t / k_pad;
+    float v = 0.f;
+    if (k < kreal) {
+      const int b = static_cast<int>(row / P), pi = static_cast<int>(row % P);
+      const int py = pi / G, px = pi % G;
+      const int kh = k / (p * 3), rem = k % (p * 3);
+      const int y = py * p + kh;
+      const int c = rem % 3;
+      const uint8_t u = img[(static_cast<int64_t>(b) * S + y) * S * 3 + static_cast<int64_t>(px) * p * 3 + rem];
+      const float mean = c == 0 ? m0 : (c == 1 ? m1 : m2);
+      const float istd = c == 0 ? is0 : (c == 1 ? is1 : is2);
+      v = (static_cast<float>(u) * (1.f / 255.f) - mean) * istd;
+    }
+    out[t] = __float2half_rn(v);
+  }
+}
+
+__global__ void fill_cls_kernel(const __half* __restrict__ cls, __half* __restrict__ x, int B, int tokens, int dim) {
+  const int b = blockIdx.x;
+  for (int c = threadIdx.x; c < dim; c += blockDim.x) x[static_cast<size_t>(b) * tokens * dim + c] = cls[c];
+}
+
+// ---------------------------------------------------------------- LayerNorm (one warp per row)
+__global__ void layernorm_kernel(const __half* __restrict__ x, int64_t stride, const float* __restrict__ g,
+                                 const float* __restrict__ b, float eps, int rows, int cols, __half* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const __half* xr = x + row * stride;
+  float s = 0.f;
+  for (int c = lane; c < cols; c += 32) s += __half2float(xr[c]);
+  const float mean = warp_sum(s) / static_cast<float>(cols);
+  float q = 0.f;
+  for (int c = lane; c < cols; c += 32) {
+    const float d = __half2float(xr[c]) - mean;
+    q += d * d;
+  }
+  const float rstd = rsqrtf(warp_sum(q) / static_cast<float>(cols) + eps);
+  __half* orow = out + static_cast<size_t>(row) * cols;
+  for (int c = lane; c < cols; c += 32) orow[c] = __float2half_rn((__half2float(xr[c]) - mean) * rstd * g[c] + b[c]);
+}
+
+// ---------------------------------------------------------------- top-k per row
+// One CTA per row. The row's keys (order-preserving uint32 of the f32 logits) are staged in shared
+// memory, a 4-pass 8-bit radix select finds the k-th largest key, then the winners are gathered
+// (ties at the threshold taken in index order) and ranked by (value desc, index asc).
+constexpr int kTopkThreads = 1024;
+constexpr int kTopkMax = 64;
+
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__global__ void __launch_bounds__(kTopkThreads) topk_kernel(const float* __restrict__ logits, int n, int k,
+                                                            int32_t* __restrict__ idx_out, float* __restrict__ val_out) {
+  extern __shared__ uint32_t keys[];  // [n]
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t s_prefix, s_remaining;
+  __shared__ uint32_t s_sel_key[kTopkMax];
+  __shared__ int s_sel_idx[kTopkMax];
+  __shared__ int s_count_gt, s_warp_ties[kTopkThreads / 32];
+  const int row = blockIdx.x, tid = threadIdx.x;
+  const float* lr = logits + static_cast<size_t>(row) * n;
+  for (int i = tid; i < n; i += kTopkThreads) keys[i] = order_key(lr[i]);
+  if (tid == 0) {
+    s_prefix = 0;
+    s_remaining = static_cast<uint32_t>(k);
+    s_count_gt = 0;
+  }
+  __syncthreads();
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = tid; i < 256; i += kTopkThreads) hist[i] = 0;
+    __syncthreads();
+    const uint32_t prefix = s_prefix;
+    const uint32_t hmask = shift == 24 ? 0u : (0xffffffffu << (shift + 8));
+    for (int i = tid; i < n; i += kTopkThreads) {
+      const uint32_t key = keys[i];
+      if ((key & hmask) == (prefix & hmask)) atomicAdd(&hist[(key >> shift) & 0xffu], 1u);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      uint32_t rem = s_remaining, cum = 0;
+      int d = 255;
+      for (; d > 0; --d) {
+        if (cum + hist[d] >= rem) break;
+        cum += hist[d];
+      }
+      s_prefix = prefix | (static_cast<uint32_t>(d) << shift);
+      s_remaining = rem - cum;
+    }
+    __syncthreads();
+  }
+  const uint32_t thr = s_prefix;
+  const uint32_t ties_needed = s_remaining;  // how many keys equal to thr are taken
+  // Gather: keys > thr (unordered), and the first `ties_needed` keys == thr in index order. Each thread
+  // owns a contiguous index range so a block scan of tie counts preserves index order.
+  const int per = (n + kTopkThreads - 1) / kTopkThreads;
+  const int lo = tid * per, hi = min(n, lo + per);
+  int my_ties = 0;
+  for (int i = lo; i < hi; ++i) my_ties += keys[i] == thr;
+  // exclusive scan of my_ties over the block
+  const int lane = tid & 31, warp = tid >> 5;
+  int incl = my_ties;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) s_warp_ties[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < kTopkThreads / 32 ? s_warp_ties[lane] : 0;
+    int wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += t;
+    }
+    if (lane < kTopkThreads / 32) s_warp_ties[lane] = wi - w;  // exclusive warp offsets
+  }
+  __syncthreads();
+  int tie_rank = s_warp_ties[warp] + incl - my_ties;
+  const int n_gt = k - static_cast<int>(ties_needed);
+  for (int i = lo; i < hi; ++i) {
+    const uint32_t key = keys[i];
+    if (key > thr) {
+      const int slot = atomicAdd(&s_count_gt, 1);
+      s_sel_key[slot] = key;
+      s_sel_idx[slot] = i;
+    } else if (key == thr) {
+      if (tie_rank < static_cast<int>(ties_needed)) {
+        s_sel_key[n_gt + tie_rank] = key;
+        s_sel_idx[n_gt + tie_rank] = i;
+      }
+      ++tie_rank;
+    }
+  }
+  __syncthreads();
+  if (tid < k) {
+    const uint32_t mk = s_sel_key[tid];
+    const int mi = s_sel_idx[tid];
+    int rank = 0;
+    for (int j = 0; j < k; ++j) {
+      const uint32_t ok = s_sel_key[j];
+      const int oi = s_sel_idx[j];
+      rank += (ok > mk) || (ok == mk && oi < mi);
+    }
+    idx_out[static_cast<size_t>(row) * k + rank] = mi;
+    if (val_out != nullptr) val_out[static_cast<size_t>(row) * k + rank] = lr[mi];
+  }
+}
+
+int topk(const float* logits, int B, int n, int k, int32_t* idx, float* val, cudaStream_t s) {
+  FF_REQUIRE(logits && idx, "ff_topk: NULL pointer");
+  FF_REQUIRE(k >= 1 && k <= kTopkMax && n >= k, "ff_topk: need 1 <= k <= %d and k <= n (k=%d n=%d)", kTopkMax, k, n);
+  const size_t smem = static_cast<size_t>(n) * sizeof(uint32_t);
+  FF_REQUIRE(smem <= 200 * 1024, "ff_topk: row of %d logits exceeds the shared-memory stage", n);
+  if (B == 0) return FF_OK;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    if (cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess)
+      return check_launch("ff_topk: cudaFuncSetAttribute");
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  topk_kernel<<<B, kTopkThreads, smem, s>>>(logits, n, k, idx, val);
+  return check_launch("topk_kernel");
+}
+
+int patchify(const uint8_t* img, int B, int S, int p, const float* mean, const float* stdv, void* out, int k_pad,
+             cudaStream_t s) {
+  FF_REQUIRE(img && out && mean && stdv, "ff_patchify: NULL pointer");
+  FF_REQUIRE(p >= 1 && S % p == 0 && k_pad >= p * p * 3, "ff_patchify: bad geometry S=%d p=%d k_pad=%d", S, p, k_pad);
+  if (B == 0) return FF_OK;
+  const int64_t total = static_cast<int64_t>(B) * (S / p) * (S / p) * k_pad;
+  const int grid = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 16));
+  patchify_kernel<<<grid, 256, 0, s>>>(img, B, S, p, mean[0], mean[1], mean[2], 1.f / stdv[0], 1.f / stdv[1],
+                                       1.f / stdv[2], static_cast<__half*>(out), k_pad);
+  return check_launch("patchify_kernel");
+}
+
+int fill_cls(const void* cls, void* x, int B, int tokens, int dim, cudaStream_t s) {
+  FF_REQUIRE(cls && x && tokens >= 1 && dim >= 1, "ff_fill_cls: bad arguments");
+  if (B == 0) return FF_OK;
+  fill_cls_kernel<<<B, 256, 0, s>>>(static_cast<const __half*>(cls), static_cast<__half*>(x), B, tokens, dim);
+  return check_launch("fill_cls_kernel");
+}
+
+int layernorm(const void* x, int64_t stride, const float* g, const float* b, float eps, int rows, int cols, void* out,
+              cudaStream_t s) {
+  FF_REQUIRE(x && g && b && out && cols >= 1 && stride >= cols, "ff_layernorm: bad arguments");
+  if (rows == 0) return FF_OK;
+  layernorm_kernel<<<(rows + 7) / 8, 256, 0, s>>>(static_cast<const __half*>(x), stride, g, b, eps, rows, cols,
+                                                  static_cast<__half*>(out));
+  return check_launch("layernorm_kernel");
+}
+
+}  // namespace ff
+
+extern "C" int ff_patchify(const uint8_t* images, int B, int image_size, int patch, const float* mean3,
+                           const float* std3, uint16_t* patches, int k_pad, void* stream) {
+  return ff::patchify(images, B, image_size, patch, mean3, std3, patches, k_pad, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ff_fill_cls(const uint16_t* cls_row, uint16_t* x, int B, int tokens, int dim, void* stream) {
+  return ff::fill_cls(cls_row, x, B, tokens, dim, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ff_layernorm(const uint16_t* x, int64_t row_stride, const float* gamma, const float* beta, float eps,
+                            int rows, int cols, uint16_t* out, void* stream) {
+  return ff::layernorm(x, row_stride, gamma, beta, eps, rows, cols, out, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ff_topk(const float* logits, int B, int n, int k, int32_t* idx_out, float* val_out, void* stream) {
+  return ff::topk(logits, B, n, k, idx_out, val_out, static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,129 @@
+"""`Engine`: the whole int8 forward on one B200, through the C ABI's engine object.
+
+Replaces `PixAICuda` (foidfinder/backends/cuda/engine.py:65-184): `engine(images)` returns fp32 logits
+[B, num_tags], the first call for a batch size allocates that size's activation buffers and captures the
+forward in a CUDA graph (engine.py:163-184), later calls replay it. Weights stay owned by this object
+(torch tensors) and are handed to the library as device pointers.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib
+from .config import ModelConfig
+from .weights import synthetic
+
+_LAYER_KEYS = {
+    "norm1_w": "norm1.weight",
+    "norm1_b": "norm1.bias",
+    "qkv_w": "qkv.qweight",
+    "qkv_s": "qkv.wscale",
+    "qkv_b": "qkv.bias",
+    "proj_w": "proj.qweight",
+    "proj_s": "proj.wscale",
+    "proj_b": "proj.bias",
+    "norm2_w": "norm2.weight",
+    "norm2_b": "norm2.bias",
+    "fc1_w": "fc1.qweight",
+    "fc1_s": "fc1.wscale",
+    "fc1_b": "fc1.bias",
+    "mlp_norm_w": "mlp_norm.weight",
+    "mlp_norm_b": "mlp_norm.bias",
+    "fc2_w": "fc2.qweight",
+    "fc2_s": "fc2.wscale",
+    "fc2_b": "fc2.bias",
+}
+
+
+def c_config(cfg: ModelConfig) -> _lib.ModelConfig:
+    c = _lib.ModelConfig()
+    c.image_size, c.patch, c.dim, c.depth, c.heads = cfg.image_size, cfg.patch, cfg.dim, cfg.depth, cfg.heads
+    c.mlp_hidden, c.mlp_hidden_pad = cfg.mlp_hidden, cfg.mlp_hidden_pad
+    c.num_tags, c.num_tags_pad = cfg.num_tags, cfg.num_tags_pad
+    c.rot_block_dim, c.rot_block_hidden, c.topk, c.ln_eps = cfg.rot_block_dim, cfg.rot_block_hidden, cfg.topk, cfg.ln_eps
+    c.mean = (C.c_float * 3)(*cfg.mean)
+    c.std = (C.c_float * 3)(*cfg.std)
+    return c
+
+
+class Engine:
+    def __init__(self, cfg: ModelConfig, weights: dict[str, torch.Tensor] | None = None, *, device: int | str = 0,
+                 seed: int = 0):
+        """weights: the output of `weights.convert` (any device; moved here). None = seeded random init."""
+        self.cfg = cfg
+        self.device = torch.device("cuda", torch.device(device).index if isinstance(device, str) else device)
+        if weights is None:
+            weights = synthetic(cfg, seed, self.device)
+        self.w = {k: v.to(self.device).contiguous() for k, v in weights.items()}
+        L = self.w
+        self._c_cfg = c_config(cfg)
+        self._layers = (_lib.LayerWeights * cfg.depth)()
+        for i in range(cfg.depth):
+            for field, key in _LAYER_KEYS.items():
+                setattr(self._layers[i], field, L[f"blocks.{i}.{key}"].data_ptr())
+        mw = _lib.ModelWeights()
+        mw.patch_w, mw.pos_bias, mw.cls_row = L["patch_w"].data_ptr(), L["pos_bias"].data_ptr(), L["cls_row"].data_ptr()
+        mw.rope_cos, mw.rope_sin = L["rope_cos"].data_ptr(), L["rope_sin"].data_ptr()
+        mw.layers = C.cast(self._layers, C.POINTER(_lib.LayerWeights))
+        mw.norm_w, mw.norm_b = L["norm.weight"].data_ptr(), L["norm.bias"].data_ptr()
+        mw.head_w, mw.head_b = L["head.weight"].data_ptr(), L["head.bias"].data_ptr()
+        self._c_w = mw
+        handle = C.c_void_p()
+        _lib.check(
+            _lib.lib().ff_engine_create(C.byref(self._c_cfg), C.byref(mw), self.device.index, C.byref(handle)),
+            "ff_engine_create",
+        )
+        self._h = handle
+
+    def workspace_bytes(self, B: int) -> int:
+        return int(_lib.lib().ff_engine_workspace_bytes(C.byref(self._c_cfg), B))
+
+    @torch.no_grad()
+    def forward(
+        self,
+        images: torch.Tensor,
+        *,
+        logits: torch.Tensor | None = None,
+        topk: bool = True,
+        graph: bool = True,
+    ) -> tuple[torch.Tensor, torch.Tensor | None, torch.Tensor | None]:
+        """images [B, S, S, 3] uint8 -> (logits [B, tags] f32, top-k indices [B, k] int32, values [B, k] f32)."""
+        cfg = self.cfg
+        if images.dtype != torch.uint8 or images.dim() != 4 or tuple(images.shape[1:]) != (cfg.image_size,) * 2 + (3,):
+            raise ValueError(f"images must be uint8 [B, {cfg.image_size}, {cfg.image_size}, 3]")
+        images = images.to(self.device, non_blocking=True).contiguous()
+        B = images.shape[0]
+        if logits is None:
+            logits = torch.empty(B, cfg.num_tags, device=self.device, dtype=torch.float32)
+        idx = torch.empty(B, cfg.topk, device=self.device, dtype=torch.int32) if topk and cfg.topk else None
+        val = torch.empty(B, cfg.topk, device=self.device, dtype=torch.float32) if idx is not None else None
+        fn = _lib.lib().ff_engine_forward if graph else _lib.lib().ff_engine_forward_eager
+        with torch.cuda.device(self.device):
+            stream = torch.cuda.current_stream(self.device).cuda_stream
+            _lib.check(
+                fn(self._h, images.data_ptr(), B, logits.data_ptr(), idx.data_ptr() if idx is not None else None,
+                   val.data_ptr() if val is not None else None, stream),
+                "ff_engine_forward",
+            )
+        return logits, idx, val
+
+    def __call__(self, images: torch.Tensor) -> torch.Tensor:
+        """images [B, S, S, 3] uint8 -> logits [B, num_tags] f32 (PixAICuda.__call__, engine.py:163-184)."""
+        return self.forward(images, topk=False)[0]
+
+    def device_error(self) -> int:
+        return _lib.device_error(self.device.index, clear=True)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            _lib.lib().ff_engine_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,202 @@
+"""Per-kernel entry points on torch CUDA tensors, mirroring the reference's `torch.ops.foidfinder` ops
+(foidfinder/backends/cuda/csrc/kernels.cu:267-281): outputs are caller-allocated and written in place,
+shape/dtype violations raise, and every launch goes on the current CUDA stream. Each call goes through
+the C ABI of `libfoidfinder_b200.so`; torch is only the memory and stream plumbing.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib
+from ._lib import EPI_BIAS, EPI_LOGITS, EPI_QKV_ROPE, EPI_RESIDUAL, EPI_S32, EPI_STEM, EPI_SWIGLU, check, lib
+
+__all__ = [
+    "EPI_QKV_ROPE", "EPI_RESIDUAL", "EPI_SWIGLU", "EPI_BIAS", "EPI_S32", "EPI_STEM", "EPI_LOGITS",
+    "gemm_s8", "gemm_f16", "rot_q8", "rot_q8_1024", "rot_q8_h128", "attention", "patchify", "fill_cls",
+    "layernorm", "topk",
+]
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _need(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _cuda(*ts: torch.Tensor | None) -> None:
+    for t in ts:
+        if t is not None:
+            _need(t.is_cuda and t.is_contiguous(), "expected contiguous CUDA tensors")
+
+
+def gemm_s8(
+    A: torch.Tensor,
+    W: torch.Tensor,
+    row_scale: torch.Tensor | None,
+    col_scale: torch.Tensor | None,
+    bias: torch.Tensor | None,
+    out: torch.Tensor,
+    epi: int,
+    tile_n: int = 0,
+    rope_cos: torch.Tensor | None = None,
+    rope_sin: torch.Tensor | None = None,
+    rope_cols: int = 0,
+    tokens: int = 1,
+) -> None:
+    """A [M, K] int8 x W [N, K] int8 -> epilogue into out (see include/foidfinder_b200.h)."""
+    _cuda(A, W, row_scale, col_scale, bias, out, rope_cos, rope_sin)
+    _need(A.dtype == torch.int8 and W.dtype == torch.int8, "gemm_s8: A and W must be int8")
+    M, K = A.shape
+    N = W.shape[0]
+    _need(W.shape[1] == K, "gemm_s8: K mismatch")
+    if epi == EPI_S32:
+        _need(out.dtype == torch.int32 and tuple(out.shape) == (M, N), "gemm_s8: S32 out must be int32 [M, N]")
+    else:
+        cols = N // 2 if epi == EPI_SWIGLU else N
+        _need(out.dtype == torch.float16 and tuple(out.shape) == (M, cols), f"gemm_s8: out must be fp16 [{M}, {cols}]")
+        _need(row_scale.numel() == M and col_scale.numel() == N and bias.numel() == N, "gemm_s8: scale/bias sizes")
+    with torch.cuda.device(A.device):
+        check(
+            lib().ff_gemm_s8(
+                _ptr(A), _ptr(W), _ptr(row_scale), _ptr(col_scale), _ptr(bias), _ptr(out), M, N, K, epi,
+                _ptr(rope_cos), _ptr(rope_sin), rope_cols, tokens, tile_n, _stream(A),
+            ),
+            "gemm_s8",
+        )
+
+
+def gemm_f16(
+    A: torch.Tensor,
+    W: torch.Tensor,
+    out: torch.Tensor,
+    epi: int,
+    bias: torch.Tensor | None = None,
+    n_valid: int | None = None,
+    pos_bias: torch.Tensor | None = None,
+    patches: int = 0,
+    tokens: int = 0,
+    tile_n: int = 0,
+) -> None:
+    """fp16 A [M, K] x W [N, K] with f32 accumulation: EPI_STEM into the token rows of x, EPI_LOGITS into f32."""
+    _cuda(A, W, out, bias, pos_bias)
+    _need(A.dtype == torch.float16 and W.dtype == torch.float16, "gemm_f16: A and W must be fp16")
+    M, K = A.shape
+    N = W.shape[0]
+    ldo = out.shape[-1]
+    nv = n_valid if n_valid is not None else min(N, ldo)
+    with torch.cuda.device(A.device):
+        check(
+            lib().ff_gemm_f16(
+                _ptr(A), _ptr(W), _ptr(bias), _ptr(out), M, N, K, epi, ldo, nv, _ptr(pos_bias), patches, tokens,
+                tile_n, _stream(A),
+            ),
+            "gemm_f16",
+        )
+
+
+def rot_q8(
+    x: torch.Tensor,
+    gamma: torch.Tensor | None,
+    beta: torch.Tensor | None,
+    out: torch.Tensor,
+    row_scale: torch.Tensor,
+    *,
+    block: int,
+    eps: float = 1e-6,
+    valid_cols: int | None = None,
+) -> None:
+    """x [T, C] fp16 -> (LayerNorm) -> block Hadamard -> int8 codes out [T, C] + row_scale [T]."""
+    _cuda(x, gamma, beta, out, row_scale)
+    _need(x.dtype == torch.float16 and out.dtype == torch.int8 and out.shape == x.shape, "rot_q8: dtypes/shapes")
+    T, Ccols = x.shape
+    with torch.cuda.device(x.device):
+        check(
+            lib().ff_rot_q8(
+                _ptr(x), _ptr(gamma), _ptr(beta), eps, T, Ccols, valid_cols or Ccols, block, _ptr(out),
+                _ptr(row_scale), _stream(x),
+            ),
+            "rot_q8",
+        )
+
+
+def rot_q8_1024(x, gamma, beta, out, row_scale) -> None:
+    """Reference signature (kernels.cu:220): LayerNorm eps 1e-5 if gamma is given, H1024, int8."""
+    rot_q8(x, gamma, beta, out, row_scale, block=1024, eps=1e-5)
+
+
+def rot_q8_h128(x, out, row_scale) -> None:
+    """Reference signature (kernels.cu:238): block-H128 rotation and int8, no norm."""
+    rot_q8(x, None, None, out, row_scale, block=128)
+
+
+def attention(
+    qkv: torch.Tensor,
+    out: torch.Tensor,
+    seq_len: int,
+    heads: int | None = None,
+    rope: tuple[torch.Tensor, torch.Tensor] | None = None,
+    scale: float = 1.0,
+) -> None:
+    """qkv [S * seq_len, 3 * heads * 64] fp16 -> out [S * seq_len, heads * 64] fp16 (non-causal)."""
+    _cuda(qkv, out)
+    _need(qkv.dtype == torch.float16 and out.dtype == torch.float16, "attention: fp16 tensors expected")
+    heads = heads or qkv.shape[1] // 192
+    _need(qkv.shape[1] == 3 * heads * 64 and out.shape[1] == heads * 64, "attention: column sizes")
+    _need(qkv.shape[0] % seq_len == 0 and out.shape[0] == qkv.shape[0], "attention: row sizes")
+    cos, sin = rope if rope is not None else (None, None)
+    _cuda(cos, sin)
+    with torch.cuda.device(qkv.device):
+        check(
+            lib().ff_attention(
+                _ptr(qkv), _ptr(out), qkv.shape[0] // seq_len, seq_len, heads, _ptr(cos), _ptr(sin), scale,
+                _stream(qkv),
+            ),
+            "attention",
+        )
+
+
+def patchify(images: torch.Tensor, patch: int, mean, std, out: torch.Tensor) -> None:
+    _cuda(images, out)
+    _need(images.dtype == torch.uint8 and images.dim() == 4, "patchify: uint8 [B, S, S, 3] expected")
+    B, S = images.shape[:2]
+    m = (C.c_float * 3)(*map(float, mean))
+    s = (C.c_float * 3)(*map(float, std))
+    with torch.cuda.device(images.device):
+        check(lib().ff_patchify(_ptr(images), B, S, patch, m, s, _ptr(out), out.shape[1], _stream(images)), "patchify")
+
+
+def fill_cls(cls_row: torch.Tensor, x: torch.Tensor, B: int, tokens: int) -> None:
+    _cuda(cls_row, x)
+    with torch.cuda.device(x.device):
+        check(lib().ff_fill_cls(_ptr(cls_row), _ptr(x), B, tokens, x.shape[-1], _stream(x)), "fill_cls")
+
+
+def layernorm(x: torch.Tensor, row_stride: int, rows: int, cols: int, gamma, beta, eps: float, out: torch.Tensor) -> None:
+    _cuda(x, gamma, beta, out)
+    with torch.cuda.device(x.device):
+        check(
+            lib().ff_layernorm(_ptr(x), row_stride, _ptr(gamma), _ptr(beta), eps, rows, cols, _ptr(out), _stream(x)),
+            "layernorm",
+        )
+
+
+def topk(logits: torch.Tensor, k: int, idx: torch.Tensor, val: torch.Tensor | None = None) -> None:
+    _cuda(logits, idx, val)
+    B, n = logits.shape
+    with torch.cuda.device(logits.device):
+        check(lib().ff_topk(_ptr(logits), B, n, k, _ptr(idx), _ptr(val), _stream(logits)), "topk")
+
+
+def device_error(device: int = 0, clear: bool = True) -> int:
+    """Error code left by a kernel whose bounded wait ran out (0 = none); synchronises the device."""
+    return _lib.device_error(device, clear)

@@ -1,0 +1,181 @@
+"""Checkpoint handling: synthetic EVA02 weights, RoPE tables, and the int8 conversion the kernels read.
+
+`convert` plays the role of the reference's `convert_checkpoint` (foidfinder/backends/cuda/engine.py:49-62):
+each block linear becomes `<name>.qweight` (int8, W' = W · blockdiag(H_n)), `<name>.wscale` (f32 per
+output channel, `quantize_rows_int8`, engine.py:37-41) and `<name>.bias` (f32). On top of the reference
+it lays the weights out for the sm_100a kernels:
+- gate|up rows interleaved in groups of 64 ([gate 64 | up 64] per 128 rows) so one GEMM tile holds
+  matching gate and up columns and the SwiGLU runs in the epilogue;
+- the SwiGLU width padded (2730 -> 2816) with zero rows/columns so every GEMM K is a multiple of 128;
+- head rows padded to a multiple of 256 tags; patch-embedding columns padded to a multiple of 64.
+
+The raw layout is the folded one foidfinder/haruka.py:fold writes (q rows and bias pre-scaled by
+head_dim**-0.5, zero k bias, fused qkv and gate|up matrices, patch bias + position embedding).
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+from .config import ModelConfig
+
+LINEARS = ("qkv", "proj", "fc1", "fc2")
+
+
+def rope_tables(grid: int, ref_grid: int, head_dim: int = 64) -> tuple[torch.Tensor, torch.Tensor]:
+    """EVA02 2-D RoPE (timm RotaryEmbeddingCat as restated in foidfinder/backends/mlx/haruka.py:22-33):
+    axial bands, positions t / grid * ref_grid, y bands then x bands, interleaved pairs, class token
+    (row 0) unrotated. Returns per-pair cos/sin [1 + grid*grid, head_dim/2] f32."""
+    nb = head_dim // 4
+    bands = 1.0 / (10000.0 ** (np.arange(nb, dtype=np.float32) / nb))
+    t = np.arange(grid, dtype=np.float32) / grid * ref_grid
+    ty, tx = np.meshgrid(t, t, indexing="ij")
+    ang = np.concatenate([ty.reshape(-1, 1) * bands, tx.reshape(-1, 1) * bands], axis=1)  # [N, head_dim/2]
+    cos = np.concatenate([np.ones((1, head_dim // 2), np.float32), np.cos(ang)]).astype(np.float32)
+    sin = np.concatenate([np.zeros((1, head_dim // 2), np.float32), np.sin(ang)]).astype(np.float32)
+    return torch.from_numpy(cos), torch.from_numpy(sin)
+
+
+def random_raw(cfg: ModelConfig, seed: int = 0, device: str | torch.device = "cpu") -> dict[str, torch.Tensor]:
+    """Seeded random-init weights in the folded layout: linear weights, position/class embeddings and
+    biases ~ N(0, 0.02); LayerNorm weight 1 + N(0, 0.02), bias N(0, 0.02)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    D, H, P = cfg.dim, cfg.mlp_hidden, cfg.patches
+
+    def n(*shape, std=0.02):
+        return torch.randn(*shape, generator=g, device=device) * std
+
+    raw = {
+        "patch_w": n(D, cfg.k_patch),
+        "patch_b": n(D),
+        "pos_embed": n(P + 1, D),
+        "cls_token": n(D),
+        "norm.weight": 1.0 + n(D),
+        "norm.bias": n(D),
+        "head.weight": n(cfg.num_tags, D),
+        "head.bias": n(cfg.num_tags),
+    }
+    q_scale = cfg.head_dim**-0.5
+    for i in range(cfg.depth):
+        p = f"blocks.{i}."
+        qkv_w, qkv_b = n(3 * D, D), n(3 * D)
+        qkv_w[:D] *= q_scale  # attention scale folded into q (haruka.py:48-57)
+        qkv_b[:D] *= q_scale
+        qkv_b[D : 2 * D] = 0.0
+        raw.update(
+            {
+                p + "norm1.weight": 1.0 + n(D),
+                p + "norm1.bias": n(D),
+                p + "qkv.weight": qkv_w,
+                p + "qkv.bias": qkv_b,
+                p + "proj.weight": n(D, D),
+                p + "proj.bias": n(D),
+                p + "norm2.weight": 1.0 + n(D),
+                p + "norm2.bias": n(D),
+                p + "fc1.weight": n(2 * H, D),  # gate rows then up rows (haruka.py:58-59)
+                p + "fc1.bias": n(2 * H),
+                p + "mlp_norm.weight": 1.0 + n(H),
+                p + "mlp_norm.bias": n(H),
+                p + "fc2.weight": n(D, H),
+                p + "fc2.bias": n(D),
+            }
+        )
+    return raw
+
+
+def fwht_rows(w: torch.Tensor, block: int) -> torch.Tensor:
+    """w [N, K] -> w · blockdiag(H_block) with the normalised Sylvester H (engine.py:29-34), computed as a
+    fast Walsh-Hadamard transform of each row in float64."""
+    N, K = w.shape
+    x = w.double().reshape(N, K // block, block)
+    h = 1
+    while h < block:
+        x = x.reshape(N, K // block, block // (2 * h), 2, h)
+        a, b = x[:, :, :, 0, :], x[:, :, :, 1, :]
+        x = torch.stack([a + b, a - b], dim=3)
+        h *= 2
+    return (x.reshape(N, K) / math.sqrt(block)).float()
+
+
+def quantize_rows_int8(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Symmetric per-output-channel int8 (engine.py:37-41)."""
+    scale = w.abs().amax(1).clamp_min(1e-12) / 127.0
+    q = torch.round(w / scale[:, None]).clamp(-127, 127).to(torch.int8)
+    return q.contiguous(), scale.float().contiguous()
+
+
+def interleave_gate_up(w: torch.Tensor, hidden: int, hidden_pad: int) -> torch.Tensor:
+    """[gate (hidden) ; up (hidden)] rows -> [gate 64 | up 64] groups over hidden_pad (zero padding)."""
+    rest = w.shape[1:]
+    gate = torch.zeros(hidden_pad, *rest, dtype=w.dtype, device=w.device)
+    up = torch.zeros_like(gate)
+    gate[:hidden], up[:hidden] = w[:hidden], w[hidden:]
+    return torch.stack([gate.view(hidden_pad // 64, 64, *rest), up.view(hidden_pad // 64, 64, *rest)], 1).reshape(
+        2 * hidden_pad, *rest
+    )
+
+
+def convert(raw: dict[str, torch.Tensor], cfg: ModelConfig, device: str | torch.device | None = None) -> dict[str, torch.Tensor]:
+    """Folded fp32 weights -> the engine format on `device` (default: where raw lives)."""
+    dev = torch.device(device) if device is not None else raw["patch_w"].device
+    D, H, Hp = cfg.dim, cfg.mlp_hidden, cfg.mlp_hidden_pad
+    out: dict[str, torch.Tensor] = {}
+
+    def put(name: str, t: torch.Tensor) -> None:
+        out[name] = t.to(dev).contiguous()
+
+    pw = torch.zeros(D, cfg.k_pad, device=raw["patch_w"].device)
+    pw[:, : cfg.k_patch] = raw["patch_w"].float()
+    put("patch_w", pw.half())
+    pos = raw["pos_embed"].float()
+    put("pos_bias", raw["patch_b"].float()[None, :] + pos[1:])
+    put("cls_row", (raw["cls_token"].float() + pos[0]).half())
+    cos, sin = rope_tables(cfg.grid, cfg.rope_ref_grid, cfg.head_dim)
+    put("rope_cos", cos)
+    put("rope_sin", sin)
+    put("norm.weight", raw["norm.weight"].float())
+    put("norm.bias", raw["norm.bias"].float())
+    hw = torch.zeros(cfg.num_tags_pad, D, device=raw["head.weight"].device)
+    hw[: cfg.num_tags] = raw["head.weight"].float()
+    hb = torch.zeros(cfg.num_tags_pad, device=hw.device)
+    hb[: cfg.num_tags] = raw["head.bias"].float()
+    put("head.weight", hw.half())
+    put("head.bias", hb)
+    for i in range(cfg.depth):
+        p = f"blocks.{i}."
+        for n in ("norm1", "norm2"):
+            put(p + n + ".weight", raw[p + n + ".weight"].float())
+            put(p + n + ".bias", raw[p + n + ".bias"].float())
+        mw = torch.zeros(Hp, device=hw.device)
+        mb = torch.zeros(Hp, device=hw.device)
+        mw[:H], mb[:H] = raw[p + "mlp_norm.weight"].float(), raw[p + "mlp_norm.bias"].float()
+        put(p + "mlp_norm.weight", mw)
+        put(p + "mlp_norm.bias", mb)
+        lin = {
+            "qkv": (raw[p + "qkv.weight"].float(), raw[p + "qkv.bias"].float(), cfg.rot_block_dim),
+            "proj": (raw[p + "proj.weight"].float(), raw[p + "proj.bias"].float(), cfg.rot_block_dim),
+            "fc1": (
+                interleave_gate_up(raw[p + "fc1.weight"].float(), H, Hp),
+                interleave_gate_up(raw[p + "fc1.bias"].float()[:, None], H, Hp)[:, 0],
+                cfg.rot_block_dim,
+            ),
+            "fc2": (
+                torch.nn.functional.pad(raw[p + "fc2.weight"].float(), (0, Hp - H)),
+                raw[p + "fc2.bias"].float(),
+                cfg.rot_block_hidden,
+            ),
+        }
+        for name, (w, b, block) in lin.items():
+            q, s = quantize_rows_int8(fwht_rows(w, block))
+            put(f"{p}{name}.qweight", q)
+            put(f"{p}{name}.wscale", s)
+            put(f"{p}{name}.bias", b.contiguous())
+    return out
+
+
+def synthetic(cfg: ModelConfig, seed: int = 0, device: str | torch.device = "cuda") -> dict[str, torch.Tensor]:
+    """Random-init model converted to the engine format, generated on `device`."""
+    return convert(random_raw(cfg, seed, device), cfg, device)

@@ -1,0 +1,199 @@
+/*
+ * foidfinder_b200 — C ABI of the sm_100a int8 tagger forward.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t passed as void*, returns an
+ * int status (FF_OK = 0) and never allocates caller-visible memory. On failure ff_last_error()
+ * returns a message for the calling thread. Kernels launch asynchronously on the given stream; a
+ * kernel whose bounded device-side wait ran out records a code in the per-device error word, which
+ * ff_device_error() returns after synchronising.
+ *
+ * Pointers named fp16 are IEEE binary16 arrays (uint16_t storage). All matrices are row-major and
+ * contiguous. Base pointers of TMA-fed operands (GEMM A and W) must be 16-byte aligned.
+ */
+#ifndef FOIDFINDER_B200_H
+#define FOIDFINDER_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* ---------------------------------------------------------------- status codes */
+#define FF_OK 0
+#define FF_ERR_INVALID_ARGUMENT 1   /* shape, alignment or pointer check failed on the host */
+#define FF_ERR_UNSUPPORTED_DEVICE 2 /* not an sm_100 device */
+#define FF_ERR_LAUNCH 3             /* a kernel launch or CUDA runtime call failed */
+#define FF_ERR_DEVICE_TIMEOUT 4     /* a bounded device wait ran out (see ff_device_error) */
+#define FF_ERR_OUT_OF_MEMORY 5
+
+/* Message describing the last failure on this thread ("" if none). */
+const char* ff_last_error(void);
+
+/* Library version, major * 10000 + minor * 100 + patch. */
+int ff_version(void);
+
+/* Reads (and, if clear != 0, resets) the error word of `device`; synchronises that device first.
+ * *code = 0 when no kernel reported a failure. */
+int ff_device_error(int device, int* code, int clear);
+
+/* ---------------------------------------------------------------- GEMM epilogues */
+#define FF_EPI_QKV_ROPE 0 /* fp16 out [M, N]; 2-D RoPE on columns [0, rope_cols) */
+#define FF_EPI_RESIDUAL 1 /* fp16 out [M, N] += y (the residual stream) */
+#define FF_EPI_SWIGLU 3   /* W rows interleaved [gate 64 | up 64]; fp16 out [M, N/2] = silu(gate) * up */
+#define FF_EPI_BIAS 4     /* fp16 out [M, N] = y */
+#define FF_EPI_S32 5      /* int32 out [M, N] = raw accumulators */
+
+/*
+ * W8A8 GEMM on tcgen05: y[m, n] = int32(sum_k A[m, k] * W[n, k]) * row_scale[m] * col_scale[n] + bias[n],
+ * then the epilogue `epi`.
+ *   A [M, K] int8 (per-token codes), W [N, K] int8 (per-channel codes), K % 128 == 0, N % 128 == 0.
+ *   rope_cos / rope_sin [tokens, 32] f32 are read only by FF_EPI_QKV_ROPE: row m uses position
+ *   m % tokens, and pair (2i, 2i+1) of every 64-wide head uses angle column (i % 32).
+ *   tile_n: 0 = automatic, else 128 or 256 output columns per CTA tile.
+ * Replaces torch.ops.foidfinder.gemm_s8 (foidfinder/backends/cuda/csrc/kernels.cu:187-217, schema
+ * kernels.cu:267-271); the reference's `stages` knob becomes `tile_n`, and its q_scale is folded into
+ * the q rows of W and bias at conversion time.
+ */
+int ff_gemm_s8(const int8_t* A, const int8_t* W, const float* row_scale, const float* col_scale, const float* bias,
+               void* out, int M, int N, int K, int epi, const float* rope_cos, const float* rope_sin, int rope_cols,
+               int tokens, int tile_n, void* stream);
+
+/*
+ * fp16 GEMM on tcgen05 with f32 accumulation, for the stem and the tag head.
+ *   FF_EPI_STEM:   A = patches [M = images * patches, K] fp16, W [N = dim, K] fp16;
+ *                  x[(m / patches) * tokens + 1 + m % patches, n] = fp16(acc + pos_bias[m % patches, n]).
+ *   FF_EPI_LOGITS: A [M, K] fp16, W [N, K] fp16; out[m, n] = acc + bias[n] (f32) for n < n_valid,
+ *                  out row stride ldo.
+ * Replaces the cuBLAS matmuls of engine.py:146 (patch embedding) and reference.py:140 (head linear).
+ */
+#define FF_EPI_STEM 6
+#define FF_EPI_LOGITS 7
+int ff_gemm_f16(const uint16_t* A, const uint16_t* W, const float* bias, void* out, int M, int N, int K, int epi,
+                int ldo, int n_valid, const float* pos_bias, int patches, int tokens, int tile_n, void* stream);
+
+/* ---------------------------------------------------------------- rotation + int8 quantisation */
+/*
+ * x [rows, cols] fp16 -> (LayerNorm over columns [0, valid_cols) with gamma/beta/eps when gamma != NULL;
+ * columns >= valid_cols become 0) -> block-diagonal normalised Sylvester Hadamard of size `block`
+ * -> per-row scale s = max(amax, 1e-12) / 127 -> codes clamp(rint(v / s), -127, 127).
+ * Supported (cols, block): cols % 256 == 0 and block in {128, 256, 512, 1024} dividing cols, cols <= 4096.
+ * Replaces rot_q8_1024 (kernels.cu:49-108, :220-235) and rot_q8_h128 (kernels.cu:112-160, :238-251).
+ */
+int ff_rot_q8(const uint16_t* x, const float* gamma, const float* beta, float eps, int rows, int cols,
+              int valid_cols, int block, int8_t* out, float* row_scale, void* stream);
+
+/* The reference's two entry points, same argument meaning (LayerNorm eps 1e-5 as in kernels.cu:91). */
+int ff_rot_q8_1024(const uint16_t* x, const float* gamma, const float* beta, int rows, int8_t* out, float* row_scale,
+                   void* stream);
+int ff_rot_q8_h128(const uint16_t* x, int rows, int cols, int8_t* out, float* row_scale, void* stream);
+
+/* ---------------------------------------------------------------- attention */
+/*
+ * Non-causal multi-head attention, head dim 64, fp16 in/out, f32 softmax and accumulation.
+ *   qkv [num_seqs * seq_len, 3 * heads * 64] fp16 (q | k | v column sections, head h at columns h*64),
+ *   out [num_seqs * seq_len, heads * 64] fp16. Any seq_len >= 1 (ragged tail tiles are masked).
+ *   rope_cos / rope_sin: NULL when q and k are already rotated (the QKV epilogue does it), else
+ *   [seq_len, 32] f32 tables applied to q and k on load. scale multiplies q·k (1 when folded into q).
+ * Replaces torch.ops.foidfinder.attention (foidfinder/backends/cuda/csrc/kernels.cu:255-265).
+ */
+int ff_attention(const uint16_t* qkv, uint16_t* out, int num_seqs, int seq_len, int heads, const float* rope_cos,
+                 const float* rope_sin, float scale, void* stream);
+
+/* ---------------------------------------------------------------- stem, norm, head */
+/*
+ * images [B, S, S, 3] uint8 -> patches [B * (S/p)^2, k_pad] fp16 with (kh, kw, c) column order
+ * (reference.py:103-107), each value (pixel / 255 - mean[c]) / std[c]; columns >= p*p*3 are 0.
+ */
+int ff_patchify(const uint8_t* images, int B, int image_size, int patch, const float* mean3, const float* std3,
+                uint16_t* patches, int k_pad, void* stream);
+
+/* Writes the class-token row cls_row [dim] fp16 into token 0 of each of B images of x [B * tokens, dim]. */
+int ff_fill_cls(const uint16_t* cls_row, uint16_t* x, int B, int tokens, int dim, void* stream);
+
+/* out[r] = LayerNorm(x[r * row_stride : + cols]) in fp16, r < rows, f32 statistics. */
+int ff_layernorm(const uint16_t* x, int64_t row_stride, const float* gamma, const float* beta, float eps, int rows,
+                 int cols, uint16_t* out, void* stream);
+
+/* Per row of logits [B, n]: the k (<= 64) largest values, descending, ties by lower index. */
+int ff_topk(const float* logits, int B, int n, int k, int32_t* idx_out, float* val_out, void* stream);
+
+/* ---------------------------------------------------------------- whole-model engine */
+typedef struct ff_model_config {
+  int image_size;       /* 448 */
+  int patch;            /* 14 */
+  int dim;              /* 1024 (EVA02-L) / 768 (EVA02-B) */
+  int depth;            /* 24 / 12 */
+  int heads;            /* dim / 64 */
+  int mlp_hidden;       /* 2730 / 2048 real SwiGLU width */
+  int mlp_hidden_pad;   /* 2816 / 2048: multiple of 128 */
+  int num_tags;         /* 30877 */
+  int num_tags_pad;     /* multiple of 256 */
+  int rot_block_dim;    /* Hadamard block for dim-wide activations: 1024 / 256 */
+  int rot_block_hidden; /* Hadamard block for hidden activations: 128 */
+  int topk;             /* <= 64 */
+  float ln_eps;         /* 1e-6 */
+  float mean[3];
+  float std[3];
+} ff_model_config;
+
+typedef struct ff_layer_weights {
+  const float *norm1_w, *norm1_b;
+  const int8_t* qkv_w; /* [3*dim, dim], q rows pre-scaled by 1/8 */
+  const float *qkv_s, *qkv_b;
+  const int8_t* proj_w; /* [dim, dim] */
+  const float *proj_s, *proj_b;
+  const float *norm2_w, *norm2_b;
+  const int8_t* fc1_w; /* [2*hidden_pad, dim], rows interleaved [gate 64 | up 64] */
+  const float *fc1_s, *fc1_b;
+  const float *mlp_norm_w, *mlp_norm_b; /* [hidden_pad] */
+  const int8_t* fc2_w; /* [dim, hidden_pad] */
+  const float *fc2_s, *fc2_b;
+} ff_layer_weights;
+
+typedef struct ff_model_weights {
+  const uint16_t* patch_w;  /* [dim, k_pad] fp16, k_pad = ceil(p*p*3 / 64) * 64 */
+  const float* pos_bias;    /* [patches, dim] f32 = patch bias + pos_embed[1:] */
+  const uint16_t* cls_row;  /* [dim] fp16 = cls_token + pos_embed[0] */
+  const float *rope_cos, *rope_sin; /* [tokens, 32] */
+  const ff_layer_weights* layers;   /* [depth] */
+  const float *norm_w, *norm_b;     /* final LayerNorm */
+  const uint16_t* head_w;           /* [num_tags_pad, dim] fp16 */
+  const float* head_b;              /* [num_tags_pad] */
+} ff_model_weights;
+
+typedef struct ff_engine ff_engine;
+
+/* Validates the config, keeps the weight pointers (the caller keeps them alive) and binds to `device`. */
+int ff_engine_create(const ff_model_config* cfg, const ff_model_weights* w, int device, ff_engine** out);
+
+/*
+ * images [B, S, S, 3] uint8 on the device -> logits [B, num_tags] f32 and, when topk_idx != NULL,
+ * the top cfg.topk tag indices [B, topk] int32 (and values when topk_val != NULL).
+ * The first call for a batch size allocates that size's activation buffers and captures the whole
+ * forward in a CUDA graph; later calls replay it. Replaces PixAICuda.__call__ (engine.py:163-184).
+ */
+int ff_engine_forward(ff_engine* e, const uint8_t* images, int B, float* logits, int32_t* topk_idx, float* topk_val,
+                      void* stream);
+
+/* Same forward without a graph (each kernel launched directly); used for debugging and tests. */
+int ff_engine_forward_eager(ff_engine* e, const uint8_t* images, int B, float* logits, int32_t* topk_idx,
+                            float* topk_val, void* stream);
+
+/* Bytes of device memory the engine holds for activations of batch size B. */
+int64_t ff_engine_workspace_bytes(const ff_model_config* cfg, int B);
+
+int ff_engine_destroy(ff_engine* e);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FOIDFINDER_B200_H */
