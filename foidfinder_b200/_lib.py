@@ -27,6 +27,9 @@ STATUS = {
 # (foidfinder/backends/cuda/csrc/gemm.cuh:8-12).
 EPI_QKV_ROPE, EPI_RESIDUAL, EPI_SWIGLU, EPI_BIAS, EPI_S32, EPI_STEM, EPI_LOGITS = 0, 1, 3, 4, 5, 6, 7
 
+# ff_engine_profile kernel classes (FF_PROF_*).
+PROF_CLASSES = ("stem_prep", "stem_gemm", "rotate", "gemm_qkv", "attention", "gemm_proj", "gemm_fc1", "gemm_fc2", "head")
+
 vp, i32, i64, f32 = C.c_void_p, C.c_int, C.c_int64, C.c_float
 
 
@@ -93,6 +96,8 @@ _SIGNATURES = {
     "ff_engine_forward": (i32, [vp, vp, i32, vp, vp, vp, vp]),
     "ff_engine_forward_eager": (i32, [vp, vp, i32, vp, vp, vp, vp]),
     "ff_engine_workspace_bytes": (i64, [C.POINTER(ModelConfig), i32]),
+    "ff_engine_profile": (i32, [vp, vp, i32, i32, C.POINTER(f32), C.POINTER(i32), vp]),
+    "ff_engine_launches_per_forward": (i32, [C.POINTER(ModelConfig)]),
     "ff_engine_destroy": (i32, [vp]),
 }
 

@@ -215,30 +215,57 @@ int build_batch(ff_engine* e, int B, ff_engine::Batch** out) {
     if (rc_ != FF_OK) return rc_; \
   } while (0)
 
+// Optional per-launch timing: events recorded around every launch, accumulated per kernel class.
+struct Profiler {
+  std::vector<cudaEvent_t> ev;
+  std::vector<int> cls;
+  size_t next = 0;
+  int begin(int klass, cudaStream_t s) {
+    if (next + 1 >= ev.size()) return FF_OK;  // out of events: stop recording
+    cls.push_back(klass);
+    return cudaEventRecord(ev[next++], s) == cudaSuccess ? FF_OK : check_launch("profiler: event record");
+  }
+  int end(cudaStream_t s) {
+    if (next >= ev.size() || cls.size() * 2 != next + 1) return FF_OK;
+    return cudaEventRecord(ev[next++], s) == cudaSuccess ? FF_OK : check_launch("profiler: event record");
+  }
+};
+
+#define FF_LAUNCH(klass, expr)                    \
+  do {                                            \
+    if (prof) FF_TRY(prof->begin((klass), s));    \
+    FF_TRY(expr);                                 \
+    if (prof) FF_TRY(prof->end(s));               \
+  } while (0)
+
 // Every launch of one forward of batch b on stream s.
-int run_forward(ff_engine* e, ff_engine::Batch* b, cudaStream_t s) {
+int run_forward(ff_engine* e, ff_engine::Batch* b, cudaStream_t s, Profiler* prof = nullptr) {
   const ff_model_config& c = e->cfg;
   const int B = b->B, M = B * e->tokens, D = c.dim, H = c.mlp_hidden_pad;
-  FF_TRY(patchify(b->images, B, c.image_size, c.patch, c.mean, c.std, b->patches, e->k_pad, s));
-  FF_TRY(gemm_launch(b->stem, s));
-  FF_TRY(fill_cls(e->w.cls_row, b->x, B, e->tokens, D, s));
+  FF_LAUNCH(FF_PROF_STEM_PREP, patchify(b->images, B, c.image_size, c.patch, c.mean, c.std, b->patches, e->k_pad, s));
+  FF_LAUNCH(FF_PROF_STEM_GEMM, gemm_launch(b->stem, s));
+  FF_LAUNCH(FF_PROF_STEM_PREP, fill_cls(e->w.cls_row, b->x, B, e->tokens, D, s));
   for (int i = 0; i < c.depth; ++i) {
     const ff_layer_weights& lw = e->layers[i];
-    FF_TRY(rot_q8(b->x, lw.norm1_w, lw.norm1_b, c.ln_eps, M, D, D, c.rot_block_dim, b->a8, b->rs, s));
-    FF_TRY(gemm_launch(b->qkv_p[i], s));
-    FF_TRY(attention(b->qkv, b->o, B, e->tokens, c.heads, nullptr, nullptr, 1.f, s));
-    FF_TRY(rot_q8(b->o, nullptr, nullptr, 0.f, M, D, D, c.rot_block_dim, b->a8, b->rs, s));
-    FF_TRY(gemm_launch(b->proj_p[i], s));
-    FF_TRY(rot_q8(b->x, lw.norm2_w, lw.norm2_b, c.ln_eps, M, D, D, c.rot_block_dim, b->a8, b->rs, s));
-    FF_TRY(gemm_launch(b->fc1_p[i], s));
-    FF_TRY(rot_q8(b->h, lw.mlp_norm_w, lw.mlp_norm_b, c.ln_eps, M, H, c.mlp_hidden, c.rot_block_hidden, b->a8, b->rs, s));
-    FF_TRY(gemm_launch(b->fc2_p[i], s));
+    FF_LAUNCH(FF_PROF_ROTATE, rot_q8(b->x, lw.norm1_w, lw.norm1_b, c.ln_eps, M, D, D, c.rot_block_dim, b->a8, b->rs, s));
+    FF_LAUNCH(FF_PROF_GEMM_QKV, gemm_launch(b->qkv_p[i], s));
+    FF_LAUNCH(FF_PROF_ATTENTION, attention(b->qkv, b->o, B, e->tokens, c.heads, nullptr, nullptr, 1.f, s));
+    FF_LAUNCH(FF_PROF_ROTATE, rot_q8(b->o, nullptr, nullptr, 0.f, M, D, D, c.rot_block_dim, b->a8, b->rs, s));
+    FF_LAUNCH(FF_PROF_GEMM_PROJ, gemm_launch(b->proj_p[i], s));
+    FF_LAUNCH(FF_PROF_ROTATE, rot_q8(b->x, lw.norm2_w, lw.norm2_b, c.ln_eps, M, D, D, c.rot_block_dim, b->a8, b->rs, s));
+    FF_LAUNCH(FF_PROF_GEMM_FC1, gemm_launch(b->fc1_p[i], s));
+    FF_LAUNCH(FF_PROF_ROTATE, rot_q8(b->h, lw.mlp_norm_w, lw.mlp_norm_b, c.ln_eps, M, H, c.mlp_hidden,
+                                     c.rot_block_hidden, b->a8, b->rs, s));
+    FF_LAUNCH(FF_PROF_GEMM_FC2, gemm_launch(b->fc2_p[i], s));
   }
-  FF_TRY(layernorm(b->x, static_cast<int64_t>(e->tokens) * D, e->w.norm_w, e->w.norm_b, c.ln_eps, B, D, b->cls, s));
-  FF_TRY(gemm_launch(b->head, s));
-  if (c.topk > 0) FF_TRY(topk(b->logits, B, c.num_tags, c.topk, b->top_idx, b->top_val, s));
+  FF_LAUNCH(FF_PROF_HEAD, layernorm(b->x, static_cast<int64_t>(e->tokens) * D, e->w.norm_w, e->w.norm_b, c.ln_eps, B, D,
+                                    b->cls, s));
+  FF_LAUNCH(FF_PROF_HEAD, gemm_launch(b->head, s));
+  if (c.topk > 0) FF_LAUNCH(FF_PROF_HEAD, topk(b->logits, B, c.num_tags, c.topk, b->top_idx, b->top_val, s));
   return FF_OK;
 }
+
+int launches_per_forward(const ff_model_config& c) { return 3 + 9 * c.depth + 2 + (c.topk > 0 ? 1 : 0); }
 
 int copy_out(ff_engine* e, ff_engine::Batch* b, float* logits, int32_t* top_idx, float* top_val, cudaStream_t s) {
   const ff_model_config& c = e->cfg;
@@ -371,6 +398,48 @@ extern "C" int ff_engine_forward(ff_engine* e, const uint8_t* images, int B, flo
     return check_launch("engine: image copy");
   if (cudaGraphLaunch(b->exec, s) != cudaSuccess) return check_launch("engine: graph launch");
   return copy_out(e, b, logits, top_idx, top_val, s);
+}
+
+extern "C" int ff_engine_profile(ff_engine* e, const uint8_t* images, int B, int iters, float* ms, int* launches,
+                                 void* stream) {
+  FF_REQUIRE(e && images && ms && B >= 1 && iters >= 1, "ff_engine_profile: bad arguments");
+  std::lock_guard<std::mutex> lock(e->mu);
+  DeviceScope scope(e->device);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ff_engine::Batch* b = nullptr;
+  FF_TRY(get_batch(e, B, &b));
+  const size_t in_bytes = static_cast<size_t>(B) * e->cfg.image_size * e->cfg.image_size * 3;
+  if (cudaMemcpyAsync(b->images, images, in_bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+    return check_launch("engine: image copy");
+  FF_TRY(run_forward(e, b, s));  // warm
+  const int n = launches_per_forward(e->cfg);
+  Profiler prof;
+  prof.ev.resize(static_cast<size_t>(2 * n * iters));
+  for (auto& ev : prof.ev)
+    if (cudaEventCreate(&ev) != cudaSuccess) return check_launch("ff_engine_profile: event create");
+  int rc = FF_OK;
+  for (int it = 0; it < iters && rc == FF_OK; ++it) rc = run_forward(e, b, s, &prof);
+  if (rc == FF_OK && cudaStreamSynchronize(s) != cudaSuccess) rc = check_launch("ff_engine_profile: sync");
+  for (int k = 0; k < FF_PROF_CLASSES; ++k) {
+    ms[k] = 0.f;
+    if (launches) launches[k] = 0;
+  }
+  if (rc == FF_OK) {
+    for (size_t i = 0; i < prof.cls.size() && 2 * i + 1 < prof.next; ++i) {
+      float t = 0.f;
+      cudaEventElapsedTime(&t, prof.ev[2 * i], prof.ev[2 * i + 1]);
+      ms[prof.cls[i]] += t / static_cast<float>(iters);
+      if (launches) launches[prof.cls[i]] += 1;
+    }
+    if (launches)
+      for (int k = 0; k < FF_PROF_CLASSES; ++k) launches[k] /= iters;
+  }
+  for (auto& ev : prof.ev) cudaEventDestroy(ev);
+  return rc;
+}
+
+extern "C" int ff_engine_launches_per_forward(const ff_model_config* cfg) {
+  return cfg == nullptr ? -1 : launches_per_forward(*cfg);
 }
 
 extern "C" int ff_engine_destroy(ff_engine* e) {

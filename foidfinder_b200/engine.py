@@ -114,6 +114,24 @@ class Engine:
         """images [B, S, S, 3] uint8 -> logits [B, num_tags] f32 (PixAICuda.__call__, engine.py:163-184)."""
         return self.forward(images, topk=False)[0]
 
+    @property
+    def launches_per_forward(self) -> int:
+        return int(_lib.lib().ff_engine_launches_per_forward(C.byref(self._c_cfg)))
+
+    @torch.no_grad()
+    def profile(self, images: torch.Tensor, iters: int = 3) -> dict[str, tuple[float, int]]:
+        """Mean ms per forward and launches per forward of each kernel class (eager launches, CUDA events)."""
+        images = images.to(self.device).contiguous()
+        ms = (C.c_float * len(_lib.PROF_CLASSES))()
+        n = (C.c_int * len(_lib.PROF_CLASSES))()
+        with torch.cuda.device(self.device):
+            stream = torch.cuda.current_stream(self.device).cuda_stream
+            _lib.check(
+                _lib.lib().ff_engine_profile(self._h, images.data_ptr(), images.shape[0], iters, ms, n, stream),
+                "ff_engine_profile",
+            )
+        return {k: (ms[i], n[i]) for i, k in enumerate(_lib.PROF_CLASSES)}
+
     def device_error(self) -> int:
         return _lib.device_error(self.device.index, clear=True)
 

@@ -184,6 +184,28 @@ int ff_engine_forward(ff_engine* e, const uint8_t* images, int B, float* logits,
 int ff_engine_forward_eager(ff_engine* e, const uint8_t* images, int B, float* logits, int32_t* topk_idx,
                             float* topk_val, void* stream);
 
+/* Kernel classes of ff_engine_profile. */
+#define FF_PROF_STEM_PREP 0 /* patchify + class-token rows */
+#define FF_PROF_STEM_GEMM 1
+#define FF_PROF_ROTATE 2    /* every LayerNorm/Hadamard/int8 quantisation launch */
+#define FF_PROF_GEMM_QKV 3
+#define FF_PROF_ATTENTION 4
+#define FF_PROF_GEMM_PROJ 5
+#define FF_PROF_GEMM_FC1 6  /* gate|up with the SwiGLU epilogue */
+#define FF_PROF_GEMM_FC2 7
+#define FF_PROF_HEAD 8      /* final LayerNorm, tag head GEMM, top-k */
+#define FF_PROF_CLASSES 9
+
+/*
+ * Runs the forward `iters` times without a graph, with CUDA events around every launch, and writes the
+ * mean milliseconds per forward spent in each kernel class to ms[FF_PROF_CLASSES] (and the number of
+ * launches per forward of each class to launches[FF_PROF_CLASSES] when not NULL). Synchronises stream.
+ */
+int ff_engine_profile(ff_engine* e, const uint8_t* images, int B, int iters, float* ms, int* launches, void* stream);
+
+/* Kernel launches in one forward of this configuration. */
+int ff_engine_launches_per_forward(const ff_model_config* cfg);
+
 /* Bytes of device memory the engine holds for activations of batch size B. */
 int64_t ff_engine_workspace_bytes(const ff_model_config* cfg, int B);
 

@@ -75,12 +75,27 @@ def rot_q8(
     if gamma is not None:
         v[:, :valid] = layer_norm(v[:, :valid], gamma[:valid], beta[:valid], eps)
     v[:, valid:] = 0.0
-    rot = blockdiag_hadamard(cols, block, torch.float64)
-    r = (v.double() @ rot).float()
+    r = (v.double().view(T, cols // block, block) @ hadamard(block, torch.float64)).view(T, cols).float()
     amax = r.abs().amax(1)
     scale = amax.clamp_min(1e-12) / 127.0
     inv = (1.0 / scale).float()
     q = torch.round(r * inv[:, None]).clamp(-127, 127).to(torch.int8)
+    return q, scale.float()
+
+
+def rot_q8_f32_fwht(x, gamma, beta, *, block, eps=1e-6, valid_cols=None):
+    """`rot_q8` with the Hadamard product rounded in f32 instead of f64. Not a reference algorithm: the
+    tests use it only to measure how far the int8 pipeline moves when nothing but rounding order
+    changes (the calibration of the free-running GPU-vs-oracle tolerance)."""
+    T, cols = x.shape
+    valid = valid_cols or cols
+    v = x.float().clone()
+    if gamma is not None:
+        v[:, :valid] = layer_norm(v[:, :valid], gamma[:valid], beta[:valid], eps)
+    v[:, valid:] = 0.0
+    r = (v.view(T, cols // block, block) @ hadamard(block, torch.float32)).view(T, cols)
+    scale = r.abs().amax(1).clamp_min(1e-12) / 127.0
+    q = torch.round(r * (1.0 / scale)[:, None]).clamp(-127, 127).to(torch.int8)
     return q, scale.float()
 
 
