@@ -9,6 +9,7 @@
 // applied to the Q and K tiles in shared memory right after they land, for callers whose q/k are not
 // rotated yet (the QKV GEMM epilogue already rotates them in the engine).
 #include "common.h"
+#include "kernels.h"
 #include "ptx.cuh"
 
 namespace ff {
@@ -213,6 +214,7 @@ int attention(const void* qkv, void* out, int num_seqs, int seq_len, int heads, 
   FF_REQUIRE((rc == nullptr) == (rsn == nullptr), "ff_attention: give both RoPE tables or neither");
   FF_REQUIRE(aligned16(qkv) && aligned16(out), "ff_attention: pointers must be 16-byte aligned");
   if (num_seqs == 0) return FF_OK;
+  if (rc == nullptr) return attention_tc(qkv, out, num_seqs, seq_len, heads, scale, s);
   const float scale_log2 = scale * 1.4426950408889634f;
   const dim3 grid((seq_len + BQ - 1) / BQ, heads, num_seqs);
   static bool configured[64] = {};

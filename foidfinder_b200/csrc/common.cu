@@ -61,8 +61,7 @@ int* device_error_word() {
   return g_err_word[dev];
 }
 
-int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elt_bytes, uint64_t inner,
-                 uint64_t outer, uint32_t box_inner, uint32_t box_outer) {
+static int load_encode() {
   if (g_encode == nullptr) {
     std::lock_guard<std::mutex> lock(g_mu);
     if (g_encode == nullptr) {
@@ -76,6 +75,13 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
       g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     }
   }
+  return FF_OK;
+}
+
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elt_bytes, uint64_t inner,
+                 uint64_t outer, uint32_t box_inner, uint32_t box_outer) {
+  const int lrc = load_encode();
+  if (lrc != FF_OK) return lrc;
   if (!aligned16(base) || (inner * elt_bytes) % 16 != 0) {
     set_error("TMA operand must be 16-byte aligned with a 16-byte multiple row pitch");
     return FF_ERR_INVALID_ARGUMENT;
@@ -90,6 +96,28 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed (%d) for [%llu, %llu] box [%u, %u]", static_cast<int>(r),
               static_cast<unsigned long long>(outer), static_cast<unsigned long long>(inner), box_outer, box_inner);
+    return FF_ERR_INVALID_ARGUMENT;
+  }
+  return FF_OK;
+}
+
+int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elt_bytes, uint64_t d0, uint64_t d1,
+                 uint64_t d2, uint32_t box0, uint32_t box1, uint32_t box2) {
+  const int lrc = load_encode();
+  if (lrc != FF_OK) return lrc;
+  if (!aligned16(base) || (d0 * elt_bytes) % 16 != 0) {
+    set_error("TMA operand must be 16-byte aligned with a 16-byte multiple row pitch");
+    return FF_ERR_INVALID_ARGUMENT;
+  }
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {d0 * static_cast<uint64_t>(elt_bytes), d0 * d1 * static_cast<uint64_t>(elt_bytes)};
+  cuuint32_t box[3] = {box0, box1, box2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = g_encode(map, dtype, 3, const_cast<void*>(base), dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled (3-D) failed (%d)", static_cast<int>(r));
     return FF_ERR_INVALID_ARGUMENT;
   }
   return FF_OK;

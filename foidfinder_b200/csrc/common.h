@@ -25,6 +25,10 @@ int* device_error_word();
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elt_bytes, uint64_t inner,
                  uint64_t outer, uint32_t box_inner, uint32_t box_outer);
 
+// 3-D tensor map over a row-major [d2, d1, d0] array (d0 innermost), 128-byte swizzle.
+int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elt_bytes, uint64_t d0, uint64_t d1,
+                 uint64_t d2, uint32_t box0, uint32_t box1, uint32_t box2);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace ff

@@ -21,7 +21,7 @@ int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, 
   }
   const int tiles = a.tiles_m * (a.N / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kernel<<<grid, 192, C::SMEM, stream>>>(ta, tb, a);
+  kernel<<<grid, C::THREADS, C::SMEM, stream>>>(ta, tb, a);
   return check_launch("gemm_tc_kernel");
 }
 

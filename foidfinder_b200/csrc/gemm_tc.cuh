@@ -4,11 +4,15 @@
 // cuBLAS fp16 matmuls of the stem and head (foidfinder/backends/cuda/engine.py:146,
 // foidfinder/backends/cuda/reference.py:133-140).
 //
-// Layout of one CTA (192 threads, one CTA per SM, grid = min(tiles, SMs)):
+// Layout of one CTA (320 threads, one CTA per SM, grid = min(tiles, SMs)):
 //   warp 0     TMA producer: A box 128 x 128 B and W box BN x 128 B per stage, 128-byte swizzle
 //   warp 1     TMEM allocator and MMA issuer: 4 tcgen05.mma (K = 32 bytes each) per stage
-//   warps 2-5  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes 32*(w%4)..+31, one
-//              output row per thread), fused dequantisation / bias / RoPE / SwiGLU / residual, store.
+//   warps 2-9  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes 32*(w%4)..+31, one
+//              output row per thread; two warps per lane quarter split the columns), fused
+//              dequantisation / bias / RoPE / SwiGLU / residual, then the warp's 32-row block goes out
+//              through a swizzled shared-memory stage as whole 128-byte lines.
+// The epilogue avoids the narrow XU pipe (int->float, division) so it hides under the next tile's
+// mainloop: see i2f_exact and silu_mul.
 // Accumulators are double-buffered in TMEM (2 x BN columns), so the epilogue of tile i overlaps the
 // mainloop of tile i+1. Stages are a ring of STAGES smem buffers guarded by full/empty mbarriers.
 #pragma once
@@ -25,23 +29,88 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * BKB;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;  // double-buffered accumulator
+  static constexpr int EPI_WARPS = 8;       // two per TMEM sub-partition, each owning half the tile's columns
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int STAGING = 4096;      // per epilogue warp: 32 rows x 128 B
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM = 1024 /*alignment slack*/ + STAGES * STAGE_BYTES + BAR_BYTES;
-  static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
-  static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM columns must be a power of two");
+  static constexpr int SMEM = 1024 /*alignment slack*/ + STAGES * STAGE_BYTES + EPI_WARPS * STAGING + BAR_BYTES;
+  static_assert(BN == 128 || BN == 256, "BN");
+  static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM columns must be a power of two");
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
-__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + __expf(-g)) * u; }
+// Exact round-to-nearest int32 -> f32 on the ALU/FMA pipes (the I2F conversion runs on the narrow XU
+// pipe): acc = hi * 4096 + lo, each half turned into a float by the magic-number method (an integer
+// placed in the mantissa of 1.5 * 2^23 resp. 2^23), recombined by one correctly rounded FMA.
+__device__ __forceinline__ float i2f_exact(uint32_t raw) {
+  const int acc = static_cast<int>(raw);
+  const float fhi = __int_as_float((acc >> 12) + 0x4B400000) - 12582912.f;
+  const float flo = __int_as_float((acc & 0xFFF) | 0x4B000000) - 8388608.f;
+  return fmaf(fhi, 4096.f, flo);
+}
+
+// 1 / d for d >= 1: the bit-level "magic constant" reciprocal estimate (a published method; relative
+// error below 1/8) refined by three Newton steps y <- y (2 - d y), all on the FMA pipe.
+__device__ __forceinline__ float rcp_newton(float d) {
+  float y = __int_as_float(0x7EF311C7 - __float_as_int(d));
+  y = y * fmaf(-d, y, 2.f);
+  y = y * fmaf(-d, y, 2.f);
+  y = y * fmaf(-d, y, 2.f);
+  return y;
+}
+
+// silu(g) * u with sigmoid(g) = 1 / (1 + 2^(-g log2 e)): one ex2 on the XU pipe, the rest on the FMA pipe.
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  const float e = ex2_approx(fminf(-g * 1.4426950408889634f, 64.f));
+  return g * rcp_newton(1.f + e) * u;
+}
+
+// Coalesced store of a warp's 32-row x 128-byte block: each lane wrote its own row into `stg` (16-byte
+// chunks XOR-swizzled by row % 8, so both phases are bank-conflict free); here every 8 lanes copy one
+// full row, 4 rows (4 whole cache lines) per warp instruction.
+__device__ __forceinline__ void stage_row128(uint8_t* stg, int lane, const uint32_t (&w)[32]) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    *reinterpret_cast<uint4*>(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+        make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+}
+__device__ __forceinline__ uint4 staged_chunk128(const uint8_t* stg, int r, int c) {
+  return *reinterpret_cast<const uint4*>(stg + r * 128 + ((c ^ (r & 7)) << 4));
+}
+// 64-byte rows (4 chunks, XOR-swizzled by (row / 2) % 4); 8 rows per warp instruction.
+__device__ __forceinline__ void stage_row64(uint8_t* stg, int lane, const uint32_t (&w)[16]) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    *reinterpret_cast<uint4*>(stg + lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4)) =
+        make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+}
+__device__ __forceinline__ uint4 staged_chunk64(const uint8_t* stg, int r, int c) {
+  return *reinterpret_cast<const uint4*>(stg + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+}
+
+// y[j] = acc[j] * rs * cs[n0 + j] + bias[n0 + j] for 32 consecutive columns.
+__device__ __forceinline__ void dequant32(const uint32_t (&r)[32], float rs, const float* cs, const float* bias,
+                                          float (&y)[32]) {
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {
+    const float4 c4 = *reinterpret_cast<const float4*>(cs + j);
+    const float4 b4 = *reinterpret_cast<const float4*>(bias + j);
+    y[j] = i2f_exact(r[j]) * rs * c4.x + b4.x;
+    y[j + 1] = i2f_exact(r[j + 1]) * rs * c4.y + b4.y;
+    y[j + 2] = i2f_exact(r[j + 2]) * rs * c4.z + b4.z;
+    y[j + 3] = i2f_exact(r[j + 3]) * rs * c4.w + b4.w;
+  }
+}
 
 template <int BN, int STAGES, bool F16IN, int EPI>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const GemmArgs args) {
   using C = GemmCfg<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint8_t* staging = smem + STAGES * C::STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::EPI_WARPS * C::STAGING);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -60,7 +129,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);  // one arrive per epilogue warp
+      mbar_init(&tempty[a], C::EPI_WARPS);  // one arrive per epilogue warp
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -176,115 +245,93 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ epilogue (warps 2..5)
-    const int q = warp & 3;  // TMEM sub-partition this warp can read
+    // ------------------------------------------------------------ epilogue (warps 2..9)
+    const int ew = warp - 2;
+    const int q = warp & 3;         // TMEM sub-partition (lanes 32q..32q+31) this warp can read
+    const int half = ew >> 2;       // which half of the tile's columns this warp owns
     const int row_in_tile = q * 32 + lane;
+    uint8_t* stg = staging + ew * C::STAGING;
+    constexpr int HALF = BN / 2;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, args.err, kDevTimeoutTmemFull)) break;
       tc_fence_after();
       const int tm = t / tiles_n, tn = t % tiles_n;
-      const int m = tm * C::BM + row_in_tile;
+      const int m_block = tm * C::BM + q * 32;  // first row of this warp's 32-row block
+      const int m = m_block + row_in_tile - q * 32;
       const bool row_ok = m < args.M;
       const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const int n_tile = tn * BN;
+      float rs = 1.f;
+      if constexpr (!F16IN) rs = row_ok ? args.row_scale[m] : 0.f;
+      __half* out16 = static_cast<__half*>(args.out);
 
       if constexpr (EPI == EPI_SWIGLU) {
-        // Tile columns hold [gate 64 | up 64] pairs; output h has N/2 columns.
-        const float rs = row_ok ? args.row_scale[m] : 0.f;
-        for (int g = 0; g < BN / 128; ++g)
-          for (int h = 0; h < 2; ++h) {
-            uint32_t rg[32], ru[32];
-            const int cg = g * 128 + h * 32, cu = cg + 64;
-            __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp must arrive converged
-            tmem_ld32(tbase + cg, rg);
-            tmem_ld32(tbase + cu, ru);
-            tmem_ld_wait();
-            if (row_ok) {
-              const int ng = n_tile + cg, nu = n_tile + cu;
-              uint32_t packed[16];
+        // Tile columns hold [gate 64 | up 64] groups; the output h has N/2 columns.
+        constexpr int OUTS = BN == 256 ? 64 : 32;  // output columns per warp
+        const int cg0 = BN == 256 ? half * 128 : half * 32;
+        uint32_t packed[OUTS / 2];
 #pragma unroll
-              for (int j = 0; j < 32; j += 2) {
-                const float2 csg = *reinterpret_cast<const float2*>(args.col_scale + ng + j);
-                const float2 csu = *reinterpret_cast<const float2*>(args.col_scale + nu + j);
-                const float2 bg = *reinterpret_cast<const float2*>(args.bias + ng + j);
-                const float2 bu = *reinterpret_cast<const float2*>(args.bias + nu + j);
-                const float g0 = static_cast<float>(static_cast<int>(rg[j])) * rs * csg.x + bg.x;
-                const float g1 = static_cast<float>(static_cast<int>(rg[j + 1])) * rs * csg.y + bg.y;
-                const float u0 = static_cast<float>(static_cast<int>(ru[j])) * rs * csu.x + bu.x;
-                const float u1 = static_cast<float>(static_cast<int>(ru[j + 1])) * rs * csu.y + bu.y;
-                packed[j / 2] = pack_half2(silu_mul(g0, u0), silu_mul(g1, u1));
-              }
-              const int no = (n_tile >> 1) + g * 64 + h * 32;
-              uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(args.out) + static_cast<size_t>(m) * args.ldo + no);
-#pragma unroll
-              for (int v = 0; v < 4; ++v)
-                dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
-            }
-          }
-      } else {
-        float rs = 1.f;
-        if constexpr (!F16IN) rs = row_ok ? args.row_scale[m] : 0.f;
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
+        for (int sub = 0; sub < OUTS / 32; ++sub) {
+          uint32_t rg[32], ru[32];
+          const int cg = cg0 + sub * 32, cu = cg + 64;
           __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp must arrive converged
-          tmem_ld32(tbase + c * 32, r);
+          tmem_ld32(tbase + cg, rg);
+          tmem_ld32(tbase + cu, ru);
           tmem_ld_wait();
-          const int n0 = n_tile + c * 32;
-          if (!row_ok) {
-            // rows past M: nothing to store
-          } else if constexpr (EPI == EPI_S32) {
-            int4* dst = reinterpret_cast<int4*>(static_cast<int*>(args.out) + static_cast<size_t>(m) * args.ldo + n0);
+          float g[32], u[32];
+          dequant32(rg, rs, args.col_scale + n_tile + cg, args.bias + n_tile + cg, g);
+          dequant32(ru, rs, args.col_scale + n_tile + cu, args.bias + n_tile + cu, u);
 #pragma unroll
-            for (int v = 0; v < 8; ++v)
-              dst[v] = make_int4(static_cast<int>(r[4 * v]), static_cast<int>(r[4 * v + 1]), static_cast<int>(r[4 * v + 2]),
-                                 static_cast<int>(r[4 * v + 3]));
-          } else if constexpr (EPI == EPI_LOGITS) {
-            // f32 logits, columns >= n_valid (padding of the tag count) are dropped.
-            float* dst = static_cast<float*>(args.out) + static_cast<size_t>(m) * args.ldo;
+          for (int j = 0; j < 32; j += 2)
+            packed[sub * 16 + j / 2] = pack_half2(silu_mul(g[j], u[j]), silu_mul(g[j + 1], u[j + 1]));
+        }
+        const int col0 = (n_tile >> 1) + (BN == 256 ? half * 64 : half * 32);
+        __syncwarp();
+        if constexpr (OUTS == 64) {
+          stage_row128(stg, lane, packed);
+          __syncwarp();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int n = n0 + j;
-              if (n < args.n_valid) dst[n] = __uint_as_float(r[j]) + args.bias[n];
-            }
-          } else if constexpr (EPI == EPI_STEM) {
-            // Patch row m of image b = m / patches goes to token b * tokens + 1 + (m % patches)
-            // (token 0 of each image is the class token). pos_bias = patch bias + position embedding.
-            const int b = m / args.patches, p = m - b * args.patches;
-            const float* pb = args.pos_bias + static_cast<size_t>(p) * args.N + n0;
-            __half* dst = static_cast<__half*>(args.out) + (static_cast<size_t>(b) * args.tokens + 1 + p) * args.ldo + n0;
-            uint32_t packed[16];
+          for (int it = 0; it < 8; ++it) {
+            const int r = it * 4 + (lane >> 3), c = lane & 7;
+            const uint4 v = staged_chunk128(stg, r, c);
+            if (m_block + r < args.M)
+              *reinterpret_cast<uint4*>(out16 + static_cast<size_t>(m_block + r) * args.ldo + col0 + c * 8) = v;
+          }
+        } else {
+          stage_row64(stg, lane, packed);
+          __syncwarp();
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              const float4 pv = *reinterpret_cast<const float4*>(pb + j);
-              packed[j / 2] = pack_half2(__uint_as_float(r[j]) + pv.x, __uint_as_float(r[j + 1]) + pv.y);
-              packed[j / 2 + 1] = pack_half2(__uint_as_float(r[j + 2]) + pv.z, __uint_as_float(r[j + 3]) + pv.w);
-            }
-            uint4* d4 = reinterpret_cast<uint4*>(dst);
+          for (int it = 0; it < 4; ++it) {
+            const int r = it * 8 + (lane >> 2), c = lane & 3;
+            const uint4 v = staged_chunk64(stg, r, c);
+            if (m_block + r < args.M)
+              *reinterpret_cast<uint4*>(out16 + static_cast<size_t>(m_block + r) * args.ldo + col0 + c * 8) = v;
+          }
+        }
+      } else if constexpr (EPI == EPI_BIAS || EPI == EPI_QKV_ROPE) {
+        // 64 fp16 output columns per chunk; the warp owns HALF columns.
+#pragma unroll 1
+        for (int ch = 0; ch < HALF / 64; ++ch) {
+          const int c0 = half * HALF + ch * 64;  // tile column of this chunk
+          const int n0 = n_tile + c0;
+          uint32_t packed[32];
 #pragma unroll
-            for (int v = 0; v < 4; ++v)
-              d4[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
-          } else {
-            // int32 -> f32 dequantisation: y = acc * row_scale[m] * col_scale[n] + bias[n]
+          for (int sub = 0; sub < 2; ++sub) {
+            uint32_t r[32];
+            __syncwarp();
+            tmem_ld32(tbase + c0 + sub * 32, r);
+            tmem_ld_wait();
             float y[32];
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              const float4 cs = *reinterpret_cast<const float4*>(args.col_scale + n0 + j);
-              const float4 bi = *reinterpret_cast<const float4*>(args.bias + n0 + j);
-              y[j] = static_cast<float>(static_cast<int>(r[j])) * rs * cs.x + bi.x;
-              y[j + 1] = static_cast<float>(static_cast<int>(r[j + 1])) * rs * cs.y + bi.y;
-              y[j + 2] = static_cast<float>(static_cast<int>(r[j + 2])) * rs * cs.z + bi.z;
-              y[j + 3] = static_cast<float>(static_cast<int>(r[j + 3])) * rs * cs.w + bi.w;
-            }
+            dequant32(r, rs, args.col_scale + n0 + sub * 32, args.bias + n0 + sub * 32, y);
             if constexpr (EPI == EPI_QKV_ROPE) {
               if (n0 < args.rope_cols) {
-                // Interleaved pairs (2i, 2i+1) of each 64-wide head rotate by the angle of pair
-                // (n % 64) / 2 at this token's position; the table row of position 0 (class token)
-                // is the identity.
-                const int pos = m % args.tokens;
-                const float* cr = args.rope_cos + static_cast<size_t>(pos) * 32 + ((n0 & 63) >> 1);
-                const float* sr = args.rope_sin + static_cast<size_t>(pos) * 32 + ((n0 & 63) >> 1);
+                // Interleaved pairs (2i, 2i+1) of each 64-wide head rotate by the angle of pair i at this
+                // token's position; the table row of position 0 (class token) is the identity.
+                const int pos = (row_ok ? m : 0) % args.tokens;
+                const float* cr = args.rope_cos + static_cast<size_t>(pos) * 32 + sub * 16;
+                const float* sr = args.rope_sin + static_cast<size_t>(pos) * 32 + sub * 16;
 #pragma unroll
                 for (int j = 0; j < 16; j += 4) {
                   const float4 c4 = *reinterpret_cast<const float4*>(cr + j);
@@ -299,28 +346,102 @@ __global__ void __launch_bounds__(192, 1)
                 }
               }
             }
-            __half* dst = static_cast<__half*>(args.out) + static_cast<size_t>(m) * args.ldo + n0;
-            uint4* d4 = reinterpret_cast<uint4*>(dst);
-            if constexpr (EPI == EPI_RESIDUAL) {
-              // fp16 residual stream: x = fp16(float(x) + y)
 #pragma unroll
-              for (int v = 0; v < 4; ++v) {
-                const uint4 old = d4[v];
-                const uint32_t ow[4] = {old.x, old.y, old.z, old.w};
-                uint32_t nw[4];
+            for (int j = 0; j < 32; j += 2) packed[sub * 16 + j / 2] = pack_half2(y[j], y[j + 1]);
+          }
+          __syncwarp();
+          stage_row128(stg, lane, packed);
+          __syncwarp();
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const float2 o2 = unpack_half2(ow[e]);
-                  nw[e] = pack_half2(o2.x + y[8 * v + 2 * e], o2.y + y[8 * v + 2 * e + 1]);
-                }
-                d4[v] = make_uint4(nw[0], nw[1], nw[2], nw[3]);
-              }
-            } else {
+          for (int it = 0; it < 8; ++it) {
+            const int r = it * 4 + (lane >> 3), c = lane & 7;
+            const uint4 v = staged_chunk128(stg, r, c);
+            if (m_block + r < args.M)
+              *reinterpret_cast<uint4*>(out16 + static_cast<size_t>(m_block + r) * args.ldo + n0 + c * 8) = v;
+          }
+        }
+      } else if constexpr (EPI == EPI_RESIDUAL) {
+        // fp16 residual stream: x = fp16(float(x) + y). y is staged in f32 (32 columns = 128 B per row)
+        // so the sum is rounded once; the old x is read in the coalesced phase.
+#pragma unroll 1
+        for (int ch = 0; ch < HALF / 32; ++ch) {
+          const int c0 = half * HALF + ch * 32;
+          const int n0 = n_tile + c0;
+          uint32_t r[32];
+          __syncwarp();
+          tmem_ld32(tbase + c0, r);
+          tmem_ld_wait();
+          float y[32];
+          dequant32(r, rs, args.col_scale + n0, args.bias + n0, y);
+          uint32_t yw[32];
 #pragma unroll
-              for (int v = 0; v < 4; ++v)
-                d4[v] = make_uint4(pack_half2(y[8 * v], y[8 * v + 1]), pack_half2(y[8 * v + 2], y[8 * v + 3]),
-                                   pack_half2(y[8 * v + 4], y[8 * v + 5]), pack_half2(y[8 * v + 6], y[8 * v + 7]));
+          for (int j = 0; j < 32; ++j) yw[j] = __float_as_uint(y[j]);
+          __syncwarp();
+          stage_row128(stg, lane, yw);
+          __syncwarp();
+          // All eight reads of the old stream first (independent, in flight together), then the stores.
+          const int c = lane & 7;
+          uint2 old[8];
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int rr = it * 4 + (lane >> 3);
+            old[it] = m_block + rr < args.M
+                          ? *reinterpret_cast<const uint2*>(out16 + static_cast<size_t>(m_block + rr) * args.ldo + n0 + c * 4)
+                          : make_uint2(0u, 0u);
+          }
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int rr = it * 4 + (lane >> 3);
+            const uint4 v = staged_chunk128(stg, rr, c);
+            if (m_block + rr < args.M) {
+              const float2 o0 = unpack_half2(old[it].x), o1 = unpack_half2(old[it].y);
+              *reinterpret_cast<uint2*>(out16 + static_cast<size_t>(m_block + rr) * args.ldo + n0 + c * 4) =
+                  make_uint2(pack_half2(o0.x + __uint_as_float(v.x), o0.y + __uint_as_float(v.y)),
+                             pack_half2(o1.x + __uint_as_float(v.z), o1.y + __uint_as_float(v.w)));
             }
+          }
+        }
+      } else {
+        // S32 (debug), LOGITS (ragged tag count) and STEM (row remap): one row per thread, direct stores.
+#pragma unroll 1
+        for (int ch = 0; ch < HALF / 32; ++ch) {
+          const int c0 = half * HALF + ch * 32;
+          const int n0 = n_tile + c0;
+          uint32_t r[32];
+          __syncwarp();
+          tmem_ld32(tbase + c0, r);
+          tmem_ld_wait();
+          if (!row_ok) {
+            // rows past M: nothing to store
+          } else if constexpr (EPI == EPI_S32) {
+            int4* dst = reinterpret_cast<int4*>(static_cast<int*>(args.out) + static_cast<size_t>(m) * args.ldo + n0);
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              dst[v] = make_int4(static_cast<int>(r[4 * v]), static_cast<int>(r[4 * v + 1]),
+                                 static_cast<int>(r[4 * v + 2]), static_cast<int>(r[4 * v + 3]));
+          } else if constexpr (EPI == EPI_LOGITS) {
+            float* dst = static_cast<float*>(args.out) + static_cast<size_t>(m) * args.ldo;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int n = n0 + j;
+              if (n < args.n_valid) dst[n] = __uint_as_float(r[j]) + args.bias[n];
+            }
+          } else if constexpr (EPI == EPI_STEM) {
+            // Patch row m of image b = m / patches goes to token b * tokens + 1 + (m % patches)
+            // (token 0 of each image is the class token). pos_bias = patch bias + position embedding.
+            const int b = m / args.patches, p = m - b * args.patches;
+            const float* pb = args.pos_bias + static_cast<size_t>(p) * args.N + n0;
+            uint32_t packed[16];
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              const float4 pv = *reinterpret_cast<const float4*>(pb + j);
+              packed[j / 2] = pack_half2(__uint_as_float(r[j]) + pv.x, __uint_as_float(r[j + 1]) + pv.y);
+              packed[j / 2 + 1] = pack_half2(__uint_as_float(r[j + 2]) + pv.z, __uint_as_float(r[j + 3]) + pv.w);
+            }
+            uint4* d4 = reinterpret_cast<uint4*>(out16 + (static_cast<size_t>(b) * args.tokens + 1 + p) * args.ldo + n0);
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              d4[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
           }
         }
       }

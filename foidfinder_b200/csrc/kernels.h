@@ -9,6 +9,7 @@ int rot_q8(const void* x, const float* g, const float* b, float eps, int rows, i
            int8_t* out, float* rs, cudaStream_t s);
 int attention(const void* qkv, void* out, int num_seqs, int seq_len, int heads, const float* rope_cos,
               const float* rope_sin, float scale, cudaStream_t s);
+int attention_tc(const void* qkv, void* out, int num_seqs, int seq_len, int heads, float scale, cudaStream_t s);
 int topk(const float* logits, int B, int n, int k, int32_t* idx, float* val, cudaStream_t s);
 int patchify(const uint8_t* img, int B, int S, int p, const float* mean, const float* stdv, void* out, int k_pad,
              cudaStream_t s);

@@ -68,9 +68,12 @@ __device__ __forceinline__ uint32_t order_key(float f) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// STAGED: the row's keys live in shared memory; otherwise (rows too long for it) every pass re-reads
+// the logits, which stay in L2.
+template <bool STAGED>
 __global__ void __launch_bounds__(kTopkThreads) topk_kernel(const float* __restrict__ logits, int n, int k,
                                                             int32_t* __restrict__ idx_out, float* __restrict__ val_out) {
-  extern __shared__ uint32_t keys[];  // [n]
+  extern __shared__ uint32_t keys_smem[];  // [n] when STAGED
   __shared__ uint32_t hist[256];
   __shared__ uint32_t s_prefix, s_remaining;
   __shared__ uint32_t s_sel_key[kTopkMax];
@@ -78,7 +81,9 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(const float* __restr
   __shared__ int s_count_gt, s_warp_ties[kTopkThreads / 32];
   const int row = blockIdx.x, tid = threadIdx.x;
   const float* lr = logits + static_cast<size_t>(row) * n;
-  for (int i = tid; i < n; i += kTopkThreads) keys[i] = order_key(lr[i]);
+  auto key_at = [&](int i) { return STAGED ? keys_smem[i] : order_key(lr[i]); };
+  if constexpr (STAGED)
+    for (int i = tid; i < n; i += kTopkThreads) keys_smem[i] = order_key(lr[i]);
   if (tid == 0) {
     s_prefix = 0;
     s_remaining = static_cast<uint32_t>(k);
@@ -91,7 +96,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(const float* __restr
     const uint32_t prefix = s_prefix;
     const uint32_t hmask = shift == 24 ? 0u : (0xffffffffu << (shift + 8));
     for (int i = tid; i < n; i += kTopkThreads) {
-      const uint32_t key = keys[i];
+      const uint32_t key = key_at(i);
       if ((key & hmask) == (prefix & hmask)) atomicAdd(&hist[(key >> shift) & 0xffu], 1u);
     }
     __syncthreads();
@@ -114,7 +119,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(const float* __restr
   const int per = (n + kTopkThreads - 1) / kTopkThreads;
   const int lo = tid * per, hi = min(n, lo + per);
   int my_ties = 0;
-  for (int i = lo; i < hi; ++i) my_ties += keys[i] == thr;
+  for (int i = lo; i < hi; ++i) my_ties += key_at(i) == thr;
   // exclusive scan of my_ties over the block
   const int lane = tid & 31, warp = tid >> 5;
   int incl = my_ties;
@@ -139,7 +144,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(const float* __restr
   int tie_rank = s_warp_ties[warp] + incl - my_ties;
   const int n_gt = k - static_cast<int>(ties_needed);
   for (int i = lo; i < hi; ++i) {
-    const uint32_t key = keys[i];
+    const uint32_t key = key_at(i);
     if (key > thr) {
       const int slot = atomicAdd(&s_count_gt, 1);
       s_sel_key[slot] = key;
@@ -171,17 +176,20 @@ int topk(const float* logits, int B, int n, int k, int32_t* idx, float* val, cud
   FF_REQUIRE(logits && idx, "ff_topk: NULL pointer");
   FF_REQUIRE(k >= 1 && k <= kTopkMax && n >= k, "ff_topk: need 1 <= k <= %d and k <= n (k=%d n=%d)", kTopkMax, k, n);
   const size_t smem = static_cast<size_t>(n) * sizeof(uint32_t);
-  FF_REQUIRE(smem <= 200 * 1024, "ff_topk: row of %d logits exceeds the shared-memory stage", n);
   if (B == 0) return FF_OK;
+  if (smem > 200 * 1024) {
+    topk_kernel<false><<<B, kTopkThreads, 0, s>>>(logits, n, k, idx, val);
+    return check_launch("topk_kernel");
+  }
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !configured[dev]) {
-    if (cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess)
+    if (cudaFuncSetAttribute(topk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess)
       return check_launch("ff_topk: cudaFuncSetAttribute");
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  topk_kernel<<<B, kTopkThreads, smem, s>>>(logits, n, k, idx, val);
+  topk_kernel<true><<<B, kTopkThreads, smem, s>>>(logits, n, k, idx, val);
   return check_launch("topk_kernel");
 }
 

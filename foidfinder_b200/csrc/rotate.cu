@@ -130,13 +130,15 @@ __global__ void __launch_bounds__(256) rot_q8_kernel(const __half* __restrict__ 
   int8_t* orow = out + static_cast<size_t>(row) * COLS;
 #pragma unroll
   for (int i = 0; i < NCH; ++i) {
-    uint32_t w[2] = {0u, 0u};
+    // rint(v * inv) (round half to even, as __float2int_rn) without the XU conversion: adding 1.5 * 2^23
+    // to the f32 product leaves the rounded integer in the low mantissa bits, whose low byte is the
+    // two's-complement int8 code. |v * inv| <= 127 by construction of the scale, so no clamp is needed.
+    uint32_t t[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int q = max(-127, min(127, __float2int_rn(v[i][e] * inv)));
-      w[e >> 2] |= (static_cast<uint32_t>(q) & 0xffu) << (8 * (e & 3));
-    }
-    *reinterpret_cast<uint2*>(orow + i * 256 + lane * 8) = make_uint2(w[0], w[1]);
+    for (int e = 0; e < 8; ++e) t[e] = __float_as_uint(__fadd_rn(__fmul_rn(v[i][e], inv), 12582912.f));
+    const uint32_t w0 = __byte_perm(__byte_perm(t[0], t[1], 0x0040), __byte_perm(t[2], t[3], 0x0040), 0x5410);
+    const uint32_t w1 = __byte_perm(__byte_perm(t[4], t[5], 0x0040), __byte_perm(t[6], t[7], 0x0040), 0x5410);
+    *reinterpret_cast<uint2*>(orow + i * 256 + lane * 8) = make_uint2(w0, w1);
   }
   if (lane == 0) row_scale[row] = scale;
 }
