@@ -4,41 +4,60 @@
 // softmax(q k^T) v per head on the packed QKV activations, scale folded into q), with f32 accumulation and
 // masked ragged tails (EVA02 at 448 px has 1025 tokens).
 //
-// One CTA = 128 queries of one (image, head); 192 threads, two CTAs per SM so one CTA's softmax overlaps
-// the other's tensor-core work:
-//   warp 0     TMA: Q once, then K/V tiles of 128 keys through a 2-stage ring (3-D tensor map
-//              [images, tokens, 3*dim], so rows past an image's last token arrive as zeros)
-//   warp 1     TMEM allocation (256 columns) and the MMA issuer:
-//                S = Q K^T          (SS, M128 N128 K64)         -> TMEM columns [0, 128)
-//                O += P V           (TS: P read from TMEM, V from smem as an MN-major operand) -> [128, 192)
-//                l += P 1           (TS, N16 against a constant tile of ones)                   -> [192, 208)
-//   warps 2-5  softmax, one query row per thread (TMEM lane = row, so no shuffles): mask, row max,
-//              lazy rescale of O and l in TMEM when the max grows by more than 2^8, P = 2^(s - m) as fp16
-//              pairs (ex2.approx.f16x2) written back over S; finally O / l -> fp16 -> global.
-// The row sum runs on the tensor core against the ones tile, so it is rescaled together with O.
+// One CTA = up to 256 queries (two 128-row tiles, Q0 and Q1) of one (image, head); 320 threads, one CTA
+// per SM (it owns all 512 TMEM columns):
+//   warp 0     TMA: Q0/Q1 once, then K/V tiles of 128 keys through a 3-stage ring. The tensor map is
+//              3-D [images, tokens, 3*dim], so rows past an image's last token arrive as zeros.
+//   warp 1     TMEM allocation and the MMA issuer, ping-ponging the two query tiles:
+//                S_i = Q_i K^T        (SS, M128 N128 K64)                           -> TMEM [128 i, +128)
+//                [O_i | l_i] += P_i [V | 1]  (TS: P_i read from TMEM; B = the V tile plus a constant
+//                                 64-wide atom of ones, MN-major, N = 80)     -> [256 + 80 i, +80)
+//              issue order per key tile j: PV_0(j), S_0(j+1), PV_1(j), S_1(j+1). An S MMA overwrites the
+//              columns its tile's P was read from; tcgen05.mma operations of one thread execute in issue
+//              order, so the preceding P V has consumed P by then.
+//   warps 2-5  softmax of Q0, warps 6-9 softmax of Q1: one query row per thread (TMEM lane = row),
+//              row max, lazy rescale of O and l in TMEM when the max grows by more than 2^8, then
+//              P = 2^(s log2e scale - m + 7) as fp16 pairs written back over S. The two warpgroups take
+//              turns at this exponential phase (order barriers), so each has the whole MUFU pipe while
+//              the other's P V and next S run on the tensor core. Exponentials go through MUFU ex2, or
+//              (build-time option) a degree-3 polynomial whose fp16 bits are assembled with integer ops.
+//              The 2^7 factor keeps every P in fp16 range (<= 2^15) while polynomial results below 2^-14
+//              (saturated there) are at most 2^-21 of the row maximum; it cancels in O / l.
+// The row sum l is column 64 of the widened P V product: it costs no extra MMA instruction (every
+// tcgen05.mma costs >= ~56 cycles whatever its N) and is rescaled together with O.
 #include "common.h"
 #include "ptx.cuh"
 
 namespace ff {
 namespace fa {
 
-constexpr int BQ = 128, BKV = 128, HD = 64, STAGES = 2;
+constexpr int BQ = 128, BKV = 128, HD = 64, STAGES = 3;
 constexpr int TILE = 128 * 128;  // 128 rows x 128 bytes (64 fp16)
-constexpr int OFF_Q = 0;
-constexpr int OFF_K = OFF_Q + TILE;
+constexpr int OFF_Q = 0;         // Q0, Q1
+constexpr int OFF_K = OFF_Q + 2 * TILE;
 constexpr int OFF_V = OFF_K + STAGES * TILE;
-constexpr int OFF_ONES = OFF_V + STAGES * TILE;  // 2 K-atoms x 16 rows x 128 B of fp16 1.0
-constexpr int OFF_BAR = OFF_ONES + 4096;
+constexpr int ONES_LBO = STAGES * TILE;          // V stage s + ONES_LBO: its atom of fp16 1.0
+constexpr int OFF_ONES = OFF_V + ONES_LBO;       // STAGES atoms of 128 rows x 128 B
+constexpr int OFF_BAR = OFF_ONES + STAGES * TILE;
 constexpr int SMEM = 1024 + OFF_BAR + 256;
-constexpr uint32_t T_S = 0, T_O = 128, T_L = 192, T_COLS = 256;
-constexpr float kRescaleThreshold = 8.f;  // log2 units: P may reach 2^8 before O and l are rescaled
+constexpr int THREADS = 320;
+constexpr uint32_t T_COLS = 512;
+__host__ __device__ constexpr uint32_t t_s(int i) { return 128u * i; }
+__host__ __device__ constexpr uint32_t t_o(int i) { return 256u + 80u * i; }  // O in [0, 64), l at 64
+__host__ __device__ constexpr uint32_t t_l(int i) { return t_o(i) + 64u; }
+constexpr float kRescaleThreshold = 8.f;  // log2 units: P may grow by 2^8 before O and l are rescaled
+constexpr float kPScaleLog2 = 7.f;        // P is computed as 2^(x + 7): max 2^15, inside fp16
 
-// MN-major operand with 128-byte swizzle: K rows of 128 B (64 fp16 along N), 8-row groups 1024 B apart.
+// Degree-3 fit of 2^f on [-0.5, 0.5] (relative error 7.5e-5, below half an fp16 ulp).
+constexpr float kP0 = 0.99992806f, kP1 = 0.69326103f, kP2 = 0.24261114f, kP3 = 0.055171605f;
+
+// MN-major operand with 128-byte swizzle: K rows of 128 B (64 fp16 along N), 8-row groups 1024 B apart,
+// the next 64-wide N atom (the ones) ONES_LBO bytes further.
 __device__ __forceinline__ uint64_t sdesc_mn_sw128(uint32_t saddr) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
-  d |= static_cast<uint64_t>(TILE >> 4) << 16;      // leading byte offset: next 64-wide N atom (unused at N = 64)
-  d |= static_cast<uint64_t>(1024u >> 4) << 32;     // stride byte offset: 8 K rows x 128 B
+  d |= static_cast<uint64_t>(ONES_LBO >> 4) << 16;  // leading byte offset: next 64-wide N atom
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;  // stride byte offset: 8 K rows x 128 B
   d |= static_cast<uint64_t>(1u) << 46;
   d |= static_cast<uint64_t>(2u) << 61;
   return d;
@@ -81,17 +100,75 @@ __device__ __forceinline__ void tmem_st1(uint32_t taddr, uint32_t r) {
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// (a - m, b - m) rounded to a half2, then 2^x on both halves in one MUFU operation.
-__device__ __forceinline__ uint32_t exp2_pair(float a, float b, float m) {
-  const uint32_t h = pack_half2(a - m, b - m);
-  uint32_t p;
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(p) : "r"(h));
-  return p;
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
+
+// Packed two-lane f32 arithmetic (one instruction for both lanes).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "sub.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// (2^x.x, 2^x.y) as fp16x2 through MUFU ex2 and the f32->f16x2 conversion (both on the XU pipe);
+// exact zeros for x = -inf.
+__device__ __forceinline__ uint32_t exp2_mufu(float2 x) { return pack_half2(ex2_approx(x.x), ex2_approx(x.y)); }
+
+// (2^x.x, 2^x.y) as fp16x2 for x <= 15 on the FMA/ALU pipes: x = n + f (n = rint(x), |f| <= 1/2), 2^f
+// by the polynomial, then the fp16 exponent n + 15 is added to the rounded 10-bit mantissa of 2^f.
+// x is clamped to >= -14 (results below 2^-14 saturate there).
+__device__ __forceinline__ uint32_t exp2_poly(float2 x) {
+  const float2 magic = make_float2(12582912.f, 12582912.f);  // 1.5 * 2^23: rint(x) lands in the low bits
+  x = make_float2(fmaxf(x.x, -14.f), fmaxf(x.y, -14.f));
+  const float2 t = add2(x, magic);
+  const float2 f = sub2(x, sub2(t, magic));
+  float2 q = fma2(make_float2(kP3, kP3), f, make_float2(kP2, kP2));
+  q = fma2(q, f, make_float2(kP1, kP1));
+  q = fma2(q, f, make_float2(kP0, kP0));
+  // (q rounded to 10 mantissa bits with its exponent rebased from f32 to fp16) + (n << 10);
+  // 0xC8001000 = 0x1000 - (112 << 23) (mod 2^32): rounding bias and exponent rebase in one add.
+  const uint32_t h0 = ((__float_as_uint(q.x) + 0xC8001000u) >> 13) + __float_as_uint(t.x) * 1024u;
+  const uint32_t h1 = ((__float_as_uint(q.y) + 0xC8001000u) >> 13) + __float_as_uint(t.y) * 1024u;
+  return __byte_perm(h0, h1, 0x5410);
+}
+
+// Which 32-key chunks of a tile take the polynomial path (bit c set: chunk c; the others use MUFU).
+// Tunable at build time. Measured on B200 (EVA02-L, 1025 tokens, batch 64): all-MUFU is fastest once
+// the two warpgroups alternate their exponential phases (371 TFLOP/s vs 348 with one polynomial chunk),
+// because the polynomial's ~15 instructions per pair cost more issue slots than the MUFU time they save.
+#ifndef FF_ATTN_POLY_CHUNKS
+#define FF_ATTN_POLY_CHUNKS 0x0u
+#endif
+constexpr unsigned kPolyChunks = FF_ATTN_POLY_CHUNKS;
 
 }  // namespace fa
 
-__global__ void __launch_bounds__(192, 2)
+__global__ void __launch_bounds__(fa::THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, __half* __restrict__ out, int T, int heads,
                         float scale_log2, int* err) {
   using namespace fa;
@@ -99,20 +176,21 @@ __global__ void __launch_bounds__(192, 2)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint64_t* q_full = bar + 0;
-  uint64_t* kv_full = bar + 1;   // [STAGES]
-  uint64_t* kv_empty = bar + 3;  // [STAGES]
-  uint64_t* s_full = bar + 5;
-  uint64_t* p_full = bar + 6;
-  uint64_t* pv_done = bar + 7;
-  uint64_t* o_full = bar + 8;
-  uint64_t* drain = bar + 9;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 10);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + 11);
+  uint64_t* kv_full = bar + 1;               // [STAGES]
+  uint64_t* kv_empty = bar + 1 + STAGES;     // [STAGES]
+  uint64_t* s_full = bar + 1 + 2 * STAGES;   // [2]
+  uint64_t* p_full = s_full + 2;             // [2]
+  uint64_t* o_full = p_full + 2;
+  uint64_t* order = o_full + 1;             // [2]: warpgroup g may run its exponentials
+  uint64_t* drain = order + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = blockIdx.x, h = blockIdx.y, img = blockIdx.z;
+  const int h = blockIdx.y, img = blockIdx.z;
   const int dim = heads * HD;
-  const int q0 = qt * BQ;
+  const int q0 = blockIdx.x * 2 * BQ;
+  const bool has1 = q0 + BQ < T;  // the second query tile holds at least one token
   const int nkv = (T + BKV - 1) / BKV;
 
   if (threadIdx.x == 0) {
@@ -121,9 +199,11 @@ __global__ void __launch_bounds__(192, 2)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(p_full, 4);
-    mbar_init(pv_done, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&order[i], 4);
+    }
     mbar_init(o_full, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -134,9 +214,10 @@ __global__ void __launch_bounds__(192, 2)
     tmem_alloc(tmem_slot, T_COLS);
     tmem_relinquish();
   }
-  if (warp >= 2) {  // the constant ones operand of the row-sum MMA (4 KB of fp16 1.0)
+  if (warp >= 2) {  // the constant ones atoms that widen V (fp16 1.0; the TMA never writes them)
     uint4* ones = reinterpret_cast<uint4*>(smem + OFF_ONES);
-    for (int i = threadIdx.x - 64; i < 4096 / 16; i += 128) ones[i] = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
+    for (int i = threadIdx.x - 64; i < STAGES * TILE / 16; i += THREADS - 64)
+      ones[i] = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
     fence_async_smem();
   }
   tc_fence_before();
@@ -147,9 +228,12 @@ __global__ void __launch_bounds__(192, 2)
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, TILE);
+      mbar_arrive_expect_tx(q_full, has1 ? 2 * TILE : TILE);
       tma_load_3d(smem + OFF_Q, &tm_qkv, q_full, h * HD, q0, img);
-      int last_phase[STAGES] = {-1, -1};
+      if (has1) tma_load_3d(smem + OFF_Q + TILE, &tm_qkv, q_full, h * HD, q0 + BQ, img);
+      int last_phase[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) last_phase[s] = -1;
       bool ok = true;
       for (int j = 0; j < nkv; ++j) {
         const int s = j % STAGES;
@@ -178,34 +262,50 @@ __global__ void __launch_bounds__(192, 2)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t id_s = idesc_f16(128, BKV);
-      constexpr uint32_t id_o = idesc_f16(128, HD) | (1u << 16);  // B (V) is MN-major
-      constexpr uint32_t id_l = idesc_f16(128, 16);
-      const uint32_t sq = smem_u32(smem + OFF_Q), sones = smem_u32(smem + OFF_ONES);
-      bool ok = mbar_wait(q_full, 0, abort_flag, err, kDevTimeoutAttn);
-      for (int j = 0; j < nkv && ok; ++j) {
-        const int s = j % STAGES;
-        const uint32_t ph = static_cast<uint32_t>(j / STAGES) & 1u;
-        if (!mbar_wait(&kv_full[s], ph, abort_flag, err, kDevTimeoutAttn)) break;
-        // S_j overwrites the TMEM columns P_{j-1} was read from: wait for the previous P V to finish.
-        if (j > 0 && !mbar_wait(pv_done, static_cast<uint32_t>(j - 1) & 1u, abort_flag, err, kDevTimeoutAttn)) break;
-        tc_fence_after();
-        const uint64_t qd = sdesc_k_sw128(sq);
-        const uint64_t kd = sdesc_k_sw128(smem_u32(smem + OFF_K + s * TILE));
+      constexpr uint32_t id_o = idesc_f16(128, HD + 16) | (1u << 16);  // B = [V | ones] is MN-major, N = 80
+      auto issue_s = [&](int i, int j) {
+        const uint64_t qd = sdesc_k_sw128(smem_u32(smem + OFF_Q + i * TILE));
+        const uint64_t kd = sdesc_k_sw128(smem_u32(smem + OFF_K + (j % STAGES) * TILE));
 #pragma unroll
-        for (int k = 0; k < 4; ++k) mma_f16(tmem + T_S, qd + 2 * k, kd + 2 * k, id_s, k > 0);
-        tc_commit(s_full);
-        if (!mbar_wait(p_full, static_cast<uint32_t>(j) & 1u, abort_flag, err, kDevTimeoutAttn)) break;
-        tc_fence_after();
-        const uint32_t sv = smem_u32(smem + OFF_V + s * TILE);
+        for (int k = 0; k < 4; ++k) mma_f16(tmem + t_s(i), qd + 2 * k, kd + 2 * k, id_s, k > 0);
+        tc_commit(&s_full[i]);
+      };
+      auto issue_pv = [&](int i, int j) {
+        const uint32_t sv = smem_u32(smem + OFF_V + (j % STAGES) * TILE);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {  // 16 keys per step: P columns 8k.., V rows 16k..
           const uint32_t acc = (j > 0 || k > 0) ? 1u : 0u;
-          mma_f16_ts(tmem + T_O, tmem + T_S + 8 * k, fa::sdesc_mn_sw128(sv + k * 2048), id_o, acc);
-          mma_f16_ts(tmem + T_L, tmem + T_S + 8 * k,
-                     sdesc_k_sw128(sones + (k >> 2) * 2048) + 2 * (k & 3), id_l, acc);
+          mma_f16_ts(tmem + t_o(i), tmem + t_s(i) + 8 * k, fa::sdesc_mn_sw128(sv + k * 2048), id_o, acc);
         }
-        tc_commit(&kv_empty[s]);
-        tc_commit(pv_done);
+      };
+      auto kv_wait = [&](int j) {
+        return mbar_wait(&kv_full[j % STAGES], static_cast<uint32_t>(j / STAGES) & 1u, abort_flag, err,
+                         kDevTimeoutAttn);
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag, err, kDevTimeoutAttn) && kv_wait(0);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        if (has1) issue_s(1, 0);
+      }
+      for (int j = 0; j < nkv && ok; ++j) {
+        const uint32_t par = static_cast<uint32_t>(j) & 1u;
+        if (!mbar_wait(&p_full[0], par, abort_flag, err, kDevTimeoutAttn)) break;
+        tc_fence_after();
+        issue_pv(0, j);
+        const bool next = j + 1 < nkv;
+        if (next) {
+          if (!kv_wait(j + 1)) break;
+          tc_fence_after();
+          issue_s(0, j + 1);
+        }
+        if (has1) {
+          if (!mbar_wait(&p_full[1], par, abort_flag, err, kDevTimeoutAttn)) break;
+          tc_fence_after();
+          issue_pv(1, j);
+        }
+        tc_commit(&kv_empty[j % STAGES]);
+        if (has1 && next) issue_s(1, j + 1);
       }
       tc_commit(o_full);
       tc_commit(drain);
@@ -218,94 +318,135 @@ __global__ void __launch_bounds__(192, 2)
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax + epilogue (warps 2..5)
+    // ------------------------------------------------------------ softmax + epilogue (warps 2..9)
+    const int g = (warp - 2) >> 2;  // query tile of this warpgroup
     const int q = warp & 3;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-    const int row = q0 + q * 32 + lane;
-    float m_ref = -INFINITY;
-    bool ok = true;
-    for (int j = 0; j < nkv && ok; ++j) {
-      if (!mbar_wait(s_full, static_cast<uint32_t>(j) & 1u, abort_flag, err, kDevTimeoutAttn)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      // Pass 1: row max of the valid keys (keys at columns >= valid belong to no token of this image).
-      const int valid = T - j * BKV;
-      float mx = -INFINITY;
+    const int row = q0 + g * BQ + q * 32 + lane;
+    if (g == 0 || has1) {
+      float m_ref = -INFINITY;
+      bool ok = true;
+      for (int j = 0; j < nkv && ok; ++j) {
+        if (!mbar_wait(&s_full[g], static_cast<uint32_t>(j) & 1u, abort_flag, err, kDevTimeoutAttn)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t ts = tmem + lane_base + t_s(g);
+        const int valid = T - j * BKV;  // keys at columns >= valid belong to no token of this image
+        const bool full_tile = valid >= BKV;
+        // Pass 1: row maximum; the whole 128-key row of S in registers, four loads, one wait.
+        float mx = -INFINITY;
+        {
+          uint32_t raw[4][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t raw[32];
-        tmem_ld32(tmem + lane_base + T_S + 32 * c, raw);
-        tmem_ld_wait();
+          for (int c = 0; c < 4; ++c) tmem_ld32(ts + 32 * c, raw[c]);
+          tmem_ld_wait();
+          if (full_tile) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e)
-          if (32 * c + e < valid) mx = fmaxf(mx, __uint_as_float(raw[e]));
-      }
-      const float m_new = fmaxf(m_ref, mx * scale_log2);
-      bool rescale = false;
-      float corr = 1.f;
-      if (j == 0) {
-        m_ref = m_new;
-      } else if (m_new > m_ref + kRescaleThreshold) {
-        corr = ex2_approx(m_ref - m_new);
-        m_ref = m_new;
-        rescale = true;
-      }
-      if (__any_sync(0xffffffffu, rescale)) {
-        uint32_t o[32];
+            for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          tmem_ld32(tmem + lane_base + T_O + 32 * c, o);
+              for (int e = 0; e < 32; e += 2) mx = max3(mx, __uint_as_float(raw[c][e]), __uint_as_float(raw[c][e + 1]));
+          } else {
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+#pragma unroll
+              for (int e = 0; e < 32; ++e)
+                if (32 * c + e < valid) mx = fmaxf(mx, __uint_as_float(raw[c][e]));
+          }
+        }
+        const float m_new = fmaxf(m_ref, mx * scale_log2);
+        bool rescale = false;
+        float corr = 1.f;
+        if (j == 0) {
+          m_ref = m_new;
+        } else if (m_new > m_ref + kRescaleThreshold) {
+          corr = ex2_approx(m_ref - m_new);
+          m_ref = m_new;
+          rescale = true;
+        }
+        if (__any_sync(0xffffffffu, rescale)) {
+          uint32_t o[32];
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            tmem_ld32(tmem + lane_base + t_o(g) + 32 * c, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
+            fa::tmem_st32(tmem + lane_base + t_o(g) + 32 * c, o);
+          }
+          uint32_t l;
+          fa::tmem_ld1(tmem + lane_base + t_l(g), l);
+          tmem_ld_wait();
+          fa::tmem_st1(tmem + lane_base + t_l(g), __float_as_uint(__uint_as_float(l) * corr));
+        }
+        // The two warpgroups take turns at the exponentials (WG0 of tile j, WG1 of tile j, WG0 of tile
+        // j+1, ...): each gets the whole MUFU pipe while the other's P V and next S run on the tensor core.
+        if (has1 && (g == 1 || j > 0) &&
+            !mbar_wait(&order[g], static_cast<uint32_t>(g == 0 ? j - 1 : j) & 1u, abort_flag, err, kDevTimeoutAttn)) {
+          ok = false;
+          break;
+        }
+        // Pass 2: P = 2^(s * scale_log2 - m_ref + 7) as fp16 pairs over S columns [0, 64), in two halves
+        // of 64 keys (two loads, one wait each). P of half hf (columns 32hf..32hf+31) only overlaps S
+        // columns already read (those of half 0).
+        const float2 sc2 = make_float2(scale_log2, scale_log2);
+        const float2 nm2 = make_float2(kPScaleLog2 - m_ref, kPScaleLog2 - m_ref);
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t raw[2][32];
+          tmem_ld32(ts + 64 * hf, raw[0]);
+          tmem_ld32(ts + 64 * hf + 32, raw[1]);
           tmem_ld_wait();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
-          fa::tmem_st32(tmem + lane_base + T_O + 32 * c, o);
+          for (int cc = 0; cc < 2; ++cc) {
+            const int c = 2 * hf + cc;
+            uint32_t pk[16];
+            if (full_tile) {
+#pragma unroll
+              for (int e = 0; e < 16; ++e) {
+                const float2 x =
+                    fma2(make_float2(__uint_as_float(raw[cc][2 * e]), __uint_as_float(raw[cc][2 * e + 1])), sc2, nm2);
+                pk[e] = ((kPolyChunks >> c) & 1u) ? fa::exp2_poly(x) : fa::exp2_mufu(x);
+              }
+            } else {
+#pragma unroll
+              for (int e = 0; e < 16; ++e) {
+                float2 x =
+                    fma2(make_float2(__uint_as_float(raw[cc][2 * e]), __uint_as_float(raw[cc][2 * e + 1])), sc2, nm2);
+                if (32 * c + 2 * e >= valid) x.x = -INFINITY;
+                if (32 * c + 2 * e + 1 >= valid) x.y = -INFINITY;
+                pk[e] = fa::exp2_mufu(x);  // exact zeros for masked keys
+              }
+            }
+            fa::tmem_st16(ts + 16 * c, pk);
+          }
         }
-        uint32_t l;
-        fa::tmem_ld1(tmem + lane_base + T_L, l);
-        tmem_ld_wait();
-        fa::tmem_st1(tmem + lane_base + T_L, __float_as_uint(__uint_as_float(l) * corr));
+        __syncwarp();
+        if (has1 && lane == 0) mbar_arrive(&order[g ^ 1]);
+        fa::tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[g]);
       }
-      // Pass 2: P = 2^(s * scale_log2 - m_ref) as fp16 pairs over TMEM columns [0, 64). Chunk c of S
-      // (columns 32c..32c+31) is read before P chunk c (columns 16c..16c+15) is written, and P chunk c
-      // only overlaps S columns of chunks <= c.
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t raw[32];
-        tmem_ld32(tmem + lane_base + T_S + 32 * c, raw);
+      if (ok && mbar_wait(o_full, 0, abort_flag, err, kDevTimeoutAttn)) {
+        tc_fence_after();
+        uint32_t o2[2][32], l;
+        tmem_ld32(tmem + lane_base + t_o(g), o2[0]);
+        tmem_ld32(tmem + lane_base + t_o(g) + 32, o2[1]);
+        fa::tmem_ld1(tmem + lane_base + t_l(g), l);
         tmem_ld_wait();
-        uint32_t pk[16];
+        const uint32_t* o = &o2[0][0];
+        if (row < T) {
+          const float inv = 1.f / __uint_as_float(l);
+          uint4* dst = reinterpret_cast<uint4*>(out + (static_cast<size_t>(img) * T + row) * dim + h * HD);
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float a = 32 * c + 2 * e < valid ? __uint_as_float(raw[2 * e]) * scale_log2 : -INFINITY;
-          const float b = 32 * c + 2 * e + 1 < valid ? __uint_as_float(raw[2 * e + 1]) * scale_log2 : -INFINITY;
-          pk[e] = fa::exp2_pair(a, b, m_ref);
+          for (int v4 = 0; v4 < 8; ++v4)
+            dst[v4] = make_uint4(pack_half2(__uint_as_float(o[8 * v4]) * inv, __uint_as_float(o[8 * v4 + 1]) * inv),
+                                 pack_half2(__uint_as_float(o[8 * v4 + 2]) * inv, __uint_as_float(o[8 * v4 + 3]) * inv),
+                                 pack_half2(__uint_as_float(o[8 * v4 + 4]) * inv, __uint_as_float(o[8 * v4 + 5]) * inv),
+                                 pack_half2(__uint_as_float(o[8 * v4 + 6]) * inv, __uint_as_float(o[8 * v4 + 7]) * inv));
         }
-        fa::tmem_st16(tmem + lane_base + T_S + 16 * c, pk);
-      }
-      fa::tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
-    }
-    if (ok && mbar_wait(o_full, 0, abort_flag, err, kDevTimeoutAttn)) {
-      tc_fence_after();
-      uint32_t o2[2][32], l;
-      tmem_ld32(tmem + lane_base + T_O, o2[0]);
-      tmem_ld32(tmem + lane_base + T_O + 32, o2[1]);
-      const uint32_t* o = &o2[0][0];
-      fa::tmem_ld1(tmem + lane_base + T_L, l);
-      tmem_ld_wait();
-      if (row < T) {
-        const float inv = 1.f / __uint_as_float(l);
-        uint4* dst = reinterpret_cast<uint4*>(out + (static_cast<size_t>(img) * T + row) * dim + h * HD);
-#pragma unroll
-        for (int v4 = 0; v4 < 8; ++v4)
-          dst[v4] = make_uint4(pack_half2(__uint_as_float(o[8 * v4]) * inv, __uint_as_float(o[8 * v4 + 1]) * inv),
-                               pack_half2(__uint_as_float(o[8 * v4 + 2]) * inv, __uint_as_float(o[8 * v4 + 3]) * inv),
-                               pack_half2(__uint_as_float(o[8 * v4 + 4]) * inv, __uint_as_float(o[8 * v4 + 5]) * inv),
-                               pack_half2(__uint_as_float(o[8 * v4 + 6]) * inv, __uint_as_float(o[8 * v4 + 7]) * inv));
       }
     }
   }
@@ -334,9 +475,9 @@ int attention_tc(const void* qkv, void* out, int num_seqs, int seq_len, int head
       return check_launch("attention_tc: cudaFuncSetAttribute");
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  const dim3 grid((seq_len + BQ - 1) / BQ, heads, num_seqs);
-  attention_tc_kernel<<<grid, 192, SMEM, s>>>(map, static_cast<__half*>(out), seq_len, heads,
-                                              scale * 1.4426950408889634f, err);
+  const dim3 grid((seq_len + 2 * BQ - 1) / (2 * BQ), heads, num_seqs);
+  attention_tc_kernel<<<grid, THREADS, SMEM, s>>>(map, static_cast<__half*>(out), seq_len, heads,
+                                                  scale * 1.4426950408889634f, err);
   return check_launch("attention_tc_kernel");
 }
 
