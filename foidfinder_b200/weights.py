@@ -179,3 +179,19 @@ def convert(raw: dict[str, torch.Tensor], cfg: ModelConfig, device: str | torch.
 def synthetic(cfg: ModelConfig, seed: int = 0, device: str | torch.device = "cuda") -> dict[str, torch.Tensor]:
     """Random-init model converted to the engine format, generated on `device`."""
     return convert(random_raw(cfg, seed, device), cfg, device)
+
+
+def from_folded(folded: dict, cfg: ModelConfig, device: str | torch.device = "cpu") -> dict[str, torch.Tensor]:
+    """The folded checkpoint foidfinder/haruka.py:fold writes (`patch_b` [patches, dim] with the position
+    embedding added, `cls` [1, dim] = class token + pos[0]; blocks in the same names as this module's raw
+    layout) -> the raw layout `convert` takes. Pool-head tensors (`pool.*`) are passed through."""
+    t = {k: torch.as_tensor(v).float().to(device) for k, v in folded.items()}
+    if "pos_embed" in t:
+        return t
+    D = cfg.dim
+    raw = dict(t)
+    raw["pos_embed"] = torch.cat([torch.zeros(1, D, device=device), t["patch_b"].reshape(cfg.patches, D)])
+    raw["patch_b"] = torch.zeros(D, device=device)
+    raw["cls_token"] = t["cls"].reshape(D)
+    del raw["cls"]
+    return raw

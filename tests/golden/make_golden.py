@@ -1,0 +1,149 @@
+"""Generates tests/golden/reference_vectors.npz by running the reference's own Python functions.
+
+Run where the reference project is importable (it is not needed at test time):
+
+    python tests/golden/make_golden.py /path/to/foidfinder-reference
+
+What it records (inputs are seeded; every function is the reference's, unmodified):
+- `foidfinder.backends.cuda.engine.hadamard(128)` and `(1024)` sign patterns (bit-packed) and scale;
+- `quantize_rows_int8` on a seeded matrix;
+- `convert_checkpoint` on a seeded one-block checkpoint (its block count, `DEPTH`, is set to 1 for the
+  call; the four block linears keep the reference's K and rotation sizes);
+- `apply_rope` of `foidfinder.backends.cuda.reference` on seeded x with `axial_rope(24, 1.0)` tables
+  (the interleaved-pair rotation convention);
+- `rope_tables(32, 16, 64)` of `foidfinder/backends/mlx/haruka.py` (the EVA02 RoPE), executed from the
+  function's source text because that module imports MLX at load time;
+- `foidfinder.haruka.fold` on a seeded tiny timm-style checkpoint (model dims shrunk through its
+  `MODEL` dict): the folded patch embedding (pixel normalisation inside the weights) and the fused
+  qkv with the q scale and zero k bias.
+"""
+
+from __future__ import annotations
+
+import ast
+import sys
+from pathlib import Path
+
+import numpy as np
+
+
+CONV_SHAPES = {"attn.qkv": (24, 1024), "attn.proj": (8, 1024), "mlp.fc1": (16, 1024), "mlp.fc2": (8, 256)}
+EVA_ROPE_ROWS = np.r_[0:40, 40:1025:37, 1024]
+
+
+def inputs() -> dict[str, np.ndarray]:
+    """Seeded inputs (numpy's PCG64 stream is stable across versions, so tests regenerate them)."""
+    rng = np.random.default_rng(1234)
+    inp = {"quant_in": (rng.standard_normal((64, 256)) * 0.02).astype(np.float32)}
+    for name, shape in CONV_SHAPES.items():
+        inp[f"conv_{name}_w"] = (rng.standard_normal(shape) * 0.02).astype(np.float32)
+    inp["rope_in"] = rng.standard_normal((1, 1, 576, 64)).astype(np.float32)
+    return inp
+
+
+def main(ref_root: str) -> None:
+    sys.path.insert(0, ref_root)
+    import torch
+
+    from foidfinder import haruka
+    from foidfinder.backends.cuda import engine, reference
+
+    out: dict[str, np.ndarray] = {}
+    inp = inputs()
+
+    for n in (128, 1024):
+        h = engine.hadamard(n, "cpu")
+        out[f"hadamard{n}_sign"] = np.packbits((h > 0).numpy())
+        out[f"hadamard{n}_abs"] = np.float32(h.abs().max().item())
+
+    q, s = engine.quantize_rows_int8(torch.from_numpy(inp["quant_in"]))
+    out["quant_q"], out["quant_scale"] = q.numpy(), s.numpy()
+
+    raw = {}
+    for name in CONV_SHAPES:
+        raw[f"blocks.0.{name}.weight"] = torch.from_numpy(inp[f"conv_{name}_w"])
+        raw[f"blocks.0.{name}.bias"] = torch.zeros(CONV_SHAPES[name][0])
+    saved_depth = engine.DEPTH
+    engine.DEPTH = 1
+    try:
+        conv = engine.convert_checkpoint(raw)
+    finally:
+        engine.DEPTH = saved_depth
+    for name in CONV_SHAPES:
+        key = f"blocks.0.{name}"
+        out[f"conv_{name}_qweight"] = conv[key + ".qweight"].numpy()
+        out[f"conv_{name}_wscale"] = conv[key + ".wscale"].numpy()
+
+    cos, sin = reference.axial_rope(24, 1.0)
+    out["rope_out"] = reference.apply_rope(torch.from_numpy(inp["rope_in"]), cos, sin).numpy()
+
+    src = (Path(ref_root) / "foidfinder/backends/mlx/haruka.py").read_text()
+    fn = next(node for node in ast.parse(src).body if isinstance(node, ast.FunctionDef) and node.name == "rope_tables")
+    ns: dict = {"np": np}
+    exec(compile(ast.Module(body=[fn], type_ignores=[]), "haruka_rope_tables", "exec"), ns)
+    ecos, esin = ns["rope_tables"](32, 16, 64)
+    rows = EVA_ROPE_ROWS
+    out["eva_rope_cos_even"] = ecos[rows, 0::2].astype(np.float32)
+    out["eva_rope_sin_even"] = esin[rows, 0::2].astype(np.float32)
+    out["eva_rope_pairs_equal"] = np.array(
+        bool(np.array_equal(ecos[:, 0::2], ecos[:, 1::2]) and np.array_equal(esin[:, 0::2], esin[:, 1::2]))
+    )
+    out["eva_rope_checksum"] = np.array([ecos.astype(np.float64).sum(), esin.astype(np.float64).sum(), ecos.shape[0]])
+
+    saved_model = dict(haruka.MODEL)
+    haruka.MODEL.update(dim=64, heads=2, depth=1)
+    try:
+        sd = fold_inputs()
+        folded = haruka.fold(sd)
+    finally:
+        haruka.MODEL.clear()
+        haruka.MODEL.update(saved_model)
+    for k in ("patch_w", "patch_b", "cls", "blocks.0.qkv.weight", "blocks.0.qkv.bias", "blocks.0.fc1.weight",
+              "blocks.0.fc1.bias"):
+        out["fold_out_" + k.replace(".", "_")] = folded[k]
+
+    dst = Path(__file__).resolve().parent / "reference_vectors.npz"
+    np.savez_compressed(dst, **out)
+    print(f"wrote {dst} ({dst.stat().st_size} bytes, {len(out)} arrays)")
+
+
+def fold_inputs() -> dict[str, np.ndarray]:
+    """A seeded tiny timm-style Haruka checkpoint: dim 64, 2 heads, 1 block, 4 patches."""
+    rng = np.random.default_rng(7)
+    D, p = 64, 14
+
+    def r(*shape):
+        return (rng.standard_normal(shape) * 0.02).astype(np.float32)
+
+    bb = "backbone."
+    sd = {
+        bb + "patch_embed.proj.weight": r(D, 3, p, p),
+        bb + "patch_embed.proj.bias": r(D),
+        bb + "pos_embed": r(1, 5, D),
+        bb + "cls_token": r(1, 1, D),
+        bb + "norm.weight": r(D),
+        bb + "norm.bias": r(D),
+        "head_pool.kv.weight": r(2 * D, D),
+        "head_pool.kv.bias": r(2 * D),
+        "head.weight": r(3, 4),
+        "head.bias": r(3),
+    }
+    for nm in ("norm", "trunk_norm", "child_q_norm", "leaf_norm"):
+        sd[f"head_pool.{nm}.weight"], sd[f"head_pool.{nm}.bias"] = r(D), r(D)
+    sd.update({"head_pool.q_coarse": r(1, 2, D), "head_pool.q_coarse_bias": r(1, 1, 2, 1),
+               "head_pool.q_child": r(1, 2, 1, D), "head_pool.q_child_bias": r(1, 1, 2, 1),
+               "head_pool.leaf_proj_weight": r(2, D, 4), "head_pool.leaf_proj_bias": r(2, 4)})
+    a, m = bb + "blocks.0.attn.", bb + "blocks.0.mlp."
+    for nm in ("q_proj", "k_proj", "v_proj", "proj"):
+        sd[a + nm + ".weight"], sd[a + nm + ".bias"] = r(D, D), r(D)
+    for nm in ("fc1_g", "fc1_x"):
+        sd[m + nm + ".weight"], sd[m + nm + ".bias"] = r(96, D), r(96)
+    sd[m + "fc2.weight"], sd[m + "fc2.bias"] = r(D, 96), r(D)
+    sd[m + "norm.weight"], sd[m + "norm.bias"] = r(96), r(96)
+    for nm in ("norm1", "norm2"):
+        sd[bb + f"blocks.0.{nm}.weight"], sd[bb + f"blocks.0.{nm}.bias"] = r(D), r(D)
+    return sd
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

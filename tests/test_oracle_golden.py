@@ -1,0 +1,112 @@
+"""Pins the oracle (and the host-side weight preparation) to vectors produced by the reference's own
+Python functions (tests/golden/make_golden.py). CPU only."""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT / "tests" / "golden"))
+
+import make_golden  # noqa: E402
+
+from foidfinder_b200 import weights as W  # noqa: E402
+from oracle import eva02 as E  # noqa: E402
+from oracle import fold as F  # noqa: E402
+from oracle import pixai as P  # noqa: E402
+from oracle import quant as Q  # noqa: E402
+
+ROT_BLOCK = {"attn.qkv": 1024, "attn.proj": 1024, "mlp.fc1": 1024, "mlp.fc2": 128}
+
+
+@pytest.fixture(scope="module")
+def gold():
+    with np.load(ROOT / "tests" / "golden" / "reference_vectors.npz") as z:
+        return {k: z[k] for k in z.files}
+
+
+@pytest.fixture(scope="module")
+def inp():
+    return make_golden.inputs()
+
+
+@pytest.mark.parametrize("n", [128, 1024])
+def test_hadamard(gold, n):
+    sign = np.unpackbits(gold[f"hadamard{n}_sign"])[: n * n].reshape(n, n).astype(bool)
+    h = Q.hadamard(n).numpy()
+    assert np.array_equal(h > 0, sign)
+    assert np.float32(np.abs(h).max()) == gold[f"hadamard{n}_abs"]
+    # The FWHT used for the weights is the same matrix.
+    assert np.allclose(W.fwht_rows(torch.eye(n), n).numpy(), h, atol=1e-7)
+
+
+@pytest.mark.parametrize("quant", [Q.quantize_rows_int8, W.quantize_rows_int8])
+def test_quantize_rows_int8(gold, inp, quant):
+    q, s = quant(torch.from_numpy(inp["quant_in"]))
+    assert np.array_equal(q.numpy(), gold["quant_q"])
+    assert np.array_equal(s.numpy(), gold["quant_scale"])
+
+
+@pytest.mark.parametrize("name", list(make_golden.CONV_SHAPES))
+def test_convert_checkpoint(gold, inp, name):
+    """Rotated per-channel int8 weights: the oracle's fp32 rotation and the weight converter's fp64 FWHT
+    each match the reference's codes except where a value lies within rounding of a half-step."""
+    w = torch.from_numpy(inp[f"conv_{name}_w"])
+    ref_q, ref_s = gold[f"conv_{name}_qweight"], gold[f"conv_{name}_wscale"]
+    for rotated in (Q.rotate_weight(w, ROT_BLOCK[name]), W.fwht_rows(w, ROT_BLOCK[name])):
+        q, s = W.quantize_rows_int8(rotated)
+        np.testing.assert_allclose(s.numpy(), ref_s, rtol=1e-6)
+        diff = np.abs(q.numpy().astype(np.int32) - ref_q.astype(np.int32))
+        assert diff.max() <= 1
+        assert (diff != 0).mean() < 1e-3
+
+
+def test_pixai_axial_rope(gold, inp):
+    cos, sin = P.axial_rope(24, 1.0)
+    out = P.apply_rope(torch.from_numpy(inp["rope_in"]), cos, sin).numpy()
+    np.testing.assert_allclose(out, gold["rope_out"], rtol=0, atol=1e-6)
+    # The engine's epilogue convention (pairs 2i, 2i+1 of each 64-wide head) gives the same rotation.
+    x = torch.from_numpy(inp["rope_in"]).reshape(-1, 64)
+    pairs = Q.apply_rope_pairs(x, cos, sin, torch.arange(x.shape[0]), 64)
+    np.testing.assert_allclose(pairs.numpy().reshape(out.shape), gold["rope_out"], rtol=0, atol=1e-6)
+
+
+@pytest.mark.parametrize("tables", [E.rope_tables, W.rope_tables])
+def test_eva02_rope_tables(gold, tables):
+    assert bool(gold["eva_rope_pairs_equal"])  # the reference's tables repeat each angle over a pair
+    cos, sin = tables(32, 16, 64)
+    rows = make_golden.EVA_ROPE_ROWS
+    np.testing.assert_allclose(cos.numpy()[rows], gold["eva_rope_cos_even"], rtol=0, atol=2e-6)
+    np.testing.assert_allclose(sin.numpy()[rows], gold["eva_rope_sin_even"], rtol=0, atol=2e-6)
+    csum, ssum, n = gold["eva_rope_checksum"]
+    assert cos.shape[0] == int(n)
+    # Full tables repeat each pair's value twice.
+    assert abs(2 * cos.double().sum().item() - csum) < 1e-2
+    assert abs(2 * sin.double().sum().item() - ssum) < 1e-2
+
+
+def test_haruka_fold(gold):
+    sd = make_golden.fold_inputs()
+    out = F.fold(sd, dim=64, heads=2, patch=14, depth=1)
+    for k in ("patch_w", "patch_b", "cls", "blocks.0.qkv.weight", "blocks.0.qkv.bias", "blocks.0.fc1.weight",
+              "blocks.0.fc1.bias"):
+        np.testing.assert_allclose(out[k], gold["fold_out_" + k.replace(".", "_")], rtol=1e-5, atol=1e-7, err_msg=k)
+
+
+def test_fold_matches_engine_patch_convention(gold):
+    """The folded patch embedding applied to raw pixels equals the unfolded one applied to normalised
+    pixels — the equivalence the engine's stem (mean/std applied on the fly) relies on."""
+    sd = make_golden.fold_inputs()
+    rng = np.random.default_rng(3)
+    px = rng.integers(0, 256, size=(4, 14, 14, 3)).astype(np.float32)
+    w = sd["backbone.patch_embed.proj.weight"].transpose(0, 2, 3, 1).reshape(64, -1)
+    b = sd["backbone.patch_embed.proj.bias"]
+    norm = ((px / 255.0 - F.IMAGENET_MEAN) / F.IMAGENET_STD).reshape(4, -1)
+    unfolded = norm @ w.T + b + sd["backbone.pos_embed"][0, 1:]
+    folded = px.reshape(4, -1) @ gold["fold_out_patch_w"].T + gold["fold_out_patch_b"]
+    np.testing.assert_allclose(folded, unfolded, rtol=1e-4, atol=1e-5)
