@@ -15,6 +15,7 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libfoidfinder_b200.so"
 
 FF_OK = 0
+FF_ERR_INVALID_ARGUMENT = 1
 STATUS = {
     1: "invalid argument",
     2: "unsupported device",
@@ -85,6 +86,7 @@ _SIGNATURES = {
     "ff_gemm_s8": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp, vp, i32, i32, i32, vp]),
     "ff_gemm_f16": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, i32, i32, i32, vp]),
     "ff_rot_q8": (i32, [vp, vp, vp, f32, i32, i32, i32, i32, vp, vp, vp]),
+    "ff_linear_w8a8_noalloc": (i32, [vp, vp, vp, f32, i32, i32, i32, i32, vp, vp, vp, vp, i32, i32, vp, vp]),
     "ff_rot_q8_1024": (i32, [vp, vp, vp, i32, vp, vp, vp]),
     "ff_rot_q8_h128": (i32, [vp, i32, i32, vp, vp, vp]),
     "ff_attention": (i32, [vp, vp, i32, i32, i32, vp, vp, f32, vp]),

@@ -79,7 +79,7 @@ int gemm_prepare(const GemmProblem& p, GemmPlan* plan) {
   plan->args.num_kb = static_cast<int>((static_cast<int64_t>(p.K) * elt) / 128);
   plan->args.tiles_m = (p.M + 127) / 128;
   plan->args.out = p.out;
-  plan->args.err = device_error_word();
+  plan->args.err = p.err_word != nullptr ? p.err_word : device_error_word();
   FF_REQUIRE(plan->args.err != nullptr, "gemm: no device error word");
   plan->bn = bn;
   plan->f16 = f16;

@@ -17,6 +17,7 @@ struct GemmProblem {
   int tile_n;  // 0 = automatic
   bool f16;
   GemmArgs args;  // epilogue fields; M/N/K/num_kb/tiles_m/out/err are filled in by gemm_prepare
+  int* err_word = nullptr;  // device error word to use instead of the library's allocated one
 };
 
 struct GemmPlan {

@@ -92,6 +92,25 @@ int ff_rot_q8_1024(const uint16_t* x, const float* gamma, const float* beta, int
                    void* stream);
 int ff_rot_q8_h128(const uint16_t* x, int rows, int cols, int8_t* out, float* row_scale, void* stream);
 
+/*
+ * Activation quantisation + W8A8 GEMM in one call that allocates no device memory, for callers that may
+ * not call cudaMalloc once running (a host that gives all GPU memory to its own pool at start-up, a
+ * serving loop where allocation and the synchronisation of cudaFree are not allowed, a plugin that only
+ * receives buffers). This entry point has no counterpart in the reference.
+ *   Computes what ff_rot_q8(x, gamma, beta, eps, rows, cols, valid_cols, block, codes, scales) followed by
+ *   ff_gemm_s8(codes, W, scales, col_scale, bias, out, rows, N, cols, epi, ...) computes, epi one of
+ *   FF_EPI_BIAS, FF_EPI_RESIDUAL, FF_EPI_SWIGLU, but the codes and row scales live in a static device
+ *   array built into the library (held by every GPU that loads it until the process exits).
+ *   Limits: rows <= 8192 and rows * cols <= 8 MiB; larger calls fail with FF_ERR_INVALID_ARGUMENT.
+ *   err: device int that records a bounded-wait timeout (NULL: a word inside the static array).
+ *   The first call on a device resolves the array's address and clears its error word (synchronising
+ *   that device); make that first call before any stream capture. All calls share the array: calls
+ *   that overlap on the GPU (e.g. on two streams) race.
+ */
+int ff_linear_w8a8_noalloc(const uint16_t* x, const float* gamma, const float* beta, float eps, int rows, int cols,
+                           int valid_cols, int block, const int8_t* W, const float* col_scale, const float* bias,
+                           void* out, int N, int epi, int* err, void* stream);
+
 /* ---------------------------------------------------------------- attention */
 /*
  * Non-causal multi-head attention, head dim 64, fp16 in/out, f32 softmax and accumulation.
