@@ -127,6 +127,17 @@ def measured_peaks() -> dict:
     return {"bf16": 1590.0, "bf16_sustained": 1400.0, "hbm": 6650.0, "source": "fallback"}
 
 
+def profiled_traffic(kernel: str) -> int | None:
+    """DRAM bytes per launch of `kernel` from the committed ncu launch-list summary (profiles/)."""
+    f = ROOT / "profiles" / "launches_eva02l_bs64.md"
+    if not f.is_file():
+        return None
+    for line in f.read_text().splitlines():
+        if line.startswith(f"traffic_bytes_per_launch[{kernel}]"):
+            return int(line.split("=")[1])
+    return None
+
+
 def cpu_forward_timing(cfg, n_images: int, warmup: int = 1) -> tuple[float, int, str]:
     """Seconds per image of the fp32 CPU forward (oracle restatement), all host threads."""
     from oracle.eva02 import forward_fp32
@@ -321,7 +332,10 @@ def run_ours(args) -> None:
             "peak": peak,
             "unit": "TFLOP/s",
             "frac": achieved / peak,
-            "traffic": None,
+            "traffic": profiled_traffic("gemm_tc_kernel int8"),
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, averaged over the 96 "
+            "int8 GEMM launches of one bs64 forward (profiles/launches_eva02l_bs64.md); algorithmic bytes per "
+            "launch average 427 MB",
             "peak_source": f"2 x bf16_tflops_sustained of MEASURED_PEAKS.json ({peaks['source']}): dense int8 runs "
             "at twice the dense bf16 rate on B200; int8 ops counted as 2 per multiply-add",
             "frac_of_nominal_4500": achieved / 4500.0,
