@@ -51,7 +51,19 @@ class ModelConfig(C.Structure):
         ("ln_eps", f32),
         ("mean", f32 * 3),
         ("std", f32 * 3),
+        ("head_kind", i32),
+        ("pool_heads", i32),
+        ("coarse_queries", i32),
+        ("leaf_queries", i32),
+        ("leaf_dim", i32),
     ]
+
+
+HEAD_CLS, HEAD_TREE = 0, 1
+POOL_FIELDS = (
+    "pool_norm_w", "pool_norm_b", "pool_kv_w", "pool_kv_b", "q_coarse", "q_coarse_bias", "q_child", "q_child_bias",
+    "trunk_norm_w", "trunk_norm_b", "child_q_norm_w", "child_q_norm_b", "leaf_norm_w", "leaf_norm_b", "leaf_w", "leaf_b",
+)
 
 
 class LayerWeights(C.Structure):
@@ -76,7 +88,7 @@ class ModelWeights(C.Structure):
         ("norm_b", vp),
         ("head_w", vp),
         ("head_b", vp),
-    ]
+    ] + [(name, vp) for name in POOL_FIELDS]
 
 
 _SIGNATURES = {
@@ -94,6 +106,8 @@ _SIGNATURES = {
     "ff_fill_cls": (i32, [vp, vp, i32, i32, i32, vp]),
     "ff_layernorm": (i32, [vp, i64, vp, vp, f32, i32, i32, vp, vp]),
     "ff_topk": (i32, [vp, i32, i32, i32, vp, vp, vp]),
+    "ff_tree_pool": (i32, [C.POINTER(ModelConfig), C.POINTER(ModelWeights), vp, i32, vp, i64, vp, vp]),
+    "ff_tree_pool_workspace_bytes": (i64, [C.POINTER(ModelConfig), i32]),
     "ff_engine_create": (i32, [C.POINTER(ModelConfig), C.POINTER(ModelWeights), i32, C.POINTER(vp)]),
     "ff_engine_forward": (i32, [vp, vp, i32, vp, vp, vp, vp]),
     "ff_engine_forward_eager": (i32, [vp, vp, i32, vp, vp, vp, vp]),

@@ -4,8 +4,10 @@ foidfinder/backends/cuda/reference.py:12-17).
 - EVA02_L: BASELINE config 0/3, "PixAI-shaped EVA02-L/14": 448 px, patch 14, 1024 patches + class token,
   24 blocks, dim 1024, 16 heads of 64, SwiGLU hidden 2730 with the EVA02 hidden LayerNorm, 2-D RoPE,
   final LayerNorm, class-token linear head to 30,877 tags, pixel mean/std 0.5.
-- EVA02_B: the Haruka backbone shape (foidfinder/haruka.py:13-27): dim 768, 12 blocks, 12 heads,
-  hidden 2048, ImageNet mean/std, 98,782 tags.
+- EVA02_B: the Haruka Tagger shape (foidfinder/haruka.py:13-27): dim 768, 12 blocks, 12 heads,
+  hidden 2048, ImageNet mean/std, the tree attention pool head (16 pool heads, 6 coarse and 18 leaf
+  queries, leaf dim 64; foidfinder/backends/mlx/haruka.py:104-136) and a linear head from the 1152 leaf
+  features to 98,782 tags.
 """
 
 from __future__ import annotations
@@ -37,6 +39,16 @@ class ModelConfig:
     rot_block_dim: int = 1024  # Hadamard block of the dim-wide GEMM inputs (qkv, proj, fc1)
     rot_block_hidden: int = 128  # Hadamard block of the hidden-wide GEMM input (fc2)
     topk: int = 50
+    head: str = "cls"  # "cls": class-token linear head; "tree": the Haruka tree attention pool
+    pool_heads: int = 16
+    coarse_queries: int = 6
+    leaf_queries: int = 18
+    leaf_dim: int = 64
+
+    @property
+    def head_in(self) -> int:
+        """K of the tag head: dim (class token) or leaf_queries * leaf_dim (tree pool)."""
+        return self.dim if self.head == "cls" else self.leaf_queries * self.leaf_dim
 
     @property
     def grid(self) -> int:
@@ -94,6 +106,7 @@ EVA02_B = ModelConfig(
     mean=IMAGENET_MEAN,
     std=IMAGENET_STD,
     rot_block_dim=256,
+    head="tree",
 )
 
 CONFIGS = {c.name: c for c in (EVA02_L, EVA02_B)}

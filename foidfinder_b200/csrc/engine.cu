@@ -6,7 +6,8 @@
 //   per block: LN1+H(dim)+q8 -> QKV GEMM (+bias, 2-D RoPE) -> attention -> H(dim)+q8 -> proj GEMM
 //              (+bias, residual) -> LN2+H(dim)+q8 -> gate|up GEMM (+bias, SwiGLU) -> mlp LN+H128+q8 ->
 //              down GEMM (+bias, residual)
-// followed by the final LayerNorm of the class tokens, the fp16 tag head and a device top-k.
+// followed by the head — the final LayerNorm of the class tokens (FF_HEAD_CLS) or the Haruka tree
+// attention pool over all tokens (FF_HEAD_TREE, pool.cu) — the fp16 tag head and a device top-k.
 // Graph capture per batch size replaces the torch.cuda.graph capture of engine.py:163-184.
 #include <cuda_fp16.h>
 
@@ -18,6 +19,7 @@
 #include "common.h"
 #include "gemm.h"
 #include "kernels.h"
+#include "pool.h"
 
 struct ff_engine {
   struct Batch {
@@ -31,11 +33,12 @@ struct ff_engine {
     __half* qkv = nullptr;
     __half* o = nullptr;
     __half* h = nullptr;
-    __half* cls = nullptr;
+    __half* cls = nullptr;  // head input: [B, dim] class rows or [B, leaves * leaf_dim] leaf features
     float* logits = nullptr;
     int32_t* top_idx = nullptr;
     float* top_val = nullptr;
-    ff::GemmPlan stem, head;
+    ff::GemmPlan stem, head, pool_kv;
+    ff::PoolBuffers pool;
     std::vector<ff::GemmPlan> qkv_p, proj_p, fc1_p, fc2_p;
     cudaGraphExec_t exec = nullptr;
     cudaStream_t capture_stream = nullptr;
@@ -64,8 +67,10 @@ struct DeviceScope {
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 struct Layout {
-  size_t images, patches, x, a8, rs, qkv, o, h, cls, logits, top_idx, top_val, total;
+  size_t images, patches, x, a8, rs, qkv, o, h, cls, logits, top_idx, top_val, pool, total;
 };
+
+int head_in(const ff_model_config& c) { return c.head_kind == FF_HEAD_TREE ? c.leaf_queries * c.leaf_dim : c.dim; }
 
 Layout layout_for(const ff_model_config& c, int B) {
   const size_t G = c.image_size / c.patch, P = G * G, T = P + 1, M = static_cast<size_t>(B) * T;
@@ -86,10 +91,11 @@ Layout layout_for(const ff_model_config& c, int B) {
   l.qkv = take(M * 3 * c.dim * 2);
   l.o = take(M * c.dim * 2);
   l.h = take(M * c.mlp_hidden_pad * 2);
-  l.cls = take(static_cast<size_t>(B) * c.dim * 2);
+  l.cls = take(static_cast<size_t>(B) * head_in(c) * 2);
   l.logits = take(static_cast<size_t>(B) * c.num_tags * 4);
   l.top_idx = take(static_cast<size_t>(B) * (c.topk > 0 ? c.topk : 1) * 4);
   l.top_val = take(static_cast<size_t>(B) * (c.topk > 0 ? c.topk : 1) * 4);
+  l.pool = take(c.head_kind == FF_HEAD_TREE ? pool_small_bytes(c, B) : 0);
   l.total = off;
   return l;
 }
@@ -107,6 +113,7 @@ int validate(const ff_model_config& c) {
              "engine: num_tags %d / pad %d", c.num_tags, c.num_tags_pad);
   FF_REQUIRE(c.dim % c.rot_block_dim == 0 && c.mlp_hidden_pad % c.rot_block_hidden == 0, "engine: rotation blocks");
   FF_REQUIRE(c.topk >= 0 && c.topk <= 64 && c.topk <= c.num_tags, "engine: topk %d", c.topk);
+  FF_REQUIRE(c.head_kind == FF_HEAD_CLS || c.head_kind == FF_HEAD_TREE, "engine: head_kind %d", c.head_kind);
   return FF_OK;
 }
 
@@ -134,6 +141,14 @@ int build_batch(ff_engine* e, int B, ff_engine::Batch** out) {
   b->logits = reinterpret_cast<float*>(base + l.logits);
   b->top_idx = reinterpret_cast<int32_t*>(base + l.top_idx);
   b->top_val = reinterpret_cast<float*>(base + l.top_val);
+  if (c.head_kind == FF_HEAD_TREE) {
+    // The pool reuses activation buffers that are free once the last block has run: the attention
+    // output for the final-normed tokens, the residual stream for the pool-normed ones, qkv for keys/values.
+    b->pool.xf = b->o;
+    b->pool.xn = b->x;
+    b->pool.kv = b->qkv;
+    pool_carve_small(c, B, base + l.pool, &b->pool);
+  }
   cudaMemset(b->block, 0, l.total);
 
   const int M = B * e->tokens, D = c.dim, H = c.mlp_hidden_pad;
@@ -161,7 +176,7 @@ int build_batch(ff_engine* e, int B, ff_engine::Batch** out) {
     p.out = b->logits;
     p.M = B;
     p.N = c.num_tags_pad;
-    p.K = D;
+    p.K = head_in(c);
     p.epi = EPI_LOGITS;
     p.f16 = true;
     p.args.bias = e->w.head_b;
@@ -169,6 +184,7 @@ int build_batch(ff_engine* e, int B, ff_engine::Batch** out) {
     p.args.n_valid = c.num_tags;
     rc = gemm_prepare(p, &b->head);
   }
+  if (rc == FF_OK && c.head_kind == FF_HEAD_TREE) rc = pool_prepare(c, e->w, B, e->tokens, b->pool, &b->pool_kv);
   b->qkv_p.resize(c.depth);
   b->proj_p.resize(c.depth);
   b->fc1_p.resize(c.depth);
@@ -258,14 +274,19 @@ int run_forward(ff_engine* e, ff_engine::Batch* b, cudaStream_t s, Profiler* pro
                                      c.rot_block_hidden, b->a8, b->rs, s));
     FF_LAUNCH(FF_PROF_GEMM_FC2, gemm_launch(b->fc2_p[i], s));
   }
-  FF_LAUNCH(FF_PROF_HEAD, layernorm(b->x, static_cast<int64_t>(e->tokens) * D, e->w.norm_w, e->w.norm_b, c.ln_eps, B, D,
-                                    b->cls, s));
+  if (c.head_kind == FF_HEAD_TREE)
+    FF_LAUNCH(FF_PROF_HEAD, pool_run(c, e->w, b->x, B, e->tokens, b->pool, b->pool_kv, b->cls, s));
+  else
+    FF_LAUNCH(FF_PROF_HEAD, layernorm(b->x, static_cast<int64_t>(e->tokens) * D, e->w.norm_w, e->w.norm_b, c.ln_eps, B,
+                                      D, b->cls, s));
   FF_LAUNCH(FF_PROF_HEAD, gemm_launch(b->head, s));
   if (c.topk > 0) FF_LAUNCH(FF_PROF_HEAD, topk(b->logits, B, c.num_tags, c.topk, b->top_idx, b->top_val, s));
   return FF_OK;
 }
 
-int launches_per_forward(const ff_model_config& c) { return 3 + 9 * c.depth + 2 + (c.topk > 0 ? 1 : 0); }
+int launches_per_forward(const ff_model_config& c) {
+  return 3 + 9 * c.depth + (c.head_kind == FF_HEAD_TREE ? kPoolLaunches : 1) + 1 + (c.topk > 0 ? 1 : 0);
+}
 
 int copy_out(ff_engine* e, ff_engine::Batch* b, float* logits, int32_t* top_idx, float* top_val, cudaStream_t s) {
   const ff_model_config& c = e->cfg;
@@ -318,6 +339,7 @@ extern "C" int ff_engine_create(const ff_model_config* cfg, const ff_model_weigh
   FF_REQUIRE(w->patch_w && w->pos_bias && w->cls_row && w->rope_cos && w->rope_sin && w->layers && w->norm_w &&
                  w->norm_b && w->head_w && w->head_b,
              "ff_engine_create: a model weight pointer is NULL");
+  if (cfg->head_kind == FF_HEAD_TREE) FF_TRY(pool_validate(*cfg, *w));
   for (int i = 0; i < cfg->depth; ++i) {
     const ff_layer_weights& l = w->layers[i];
     FF_REQUIRE(l.norm1_w && l.norm1_b && l.qkv_w && l.qkv_s && l.qkv_b && l.proj_w && l.proj_s && l.proj_b &&

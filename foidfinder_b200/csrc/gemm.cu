@@ -32,6 +32,7 @@ int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const Ge
     switch (epi) {
       case EPI_STEM: return launch_one<BN, STAGES, true, EPI_STEM>(ta, tb, a, s);
       case EPI_LOGITS: return launch_one<BN, STAGES, true, EPI_LOGITS>(ta, tb, a, s);
+      case EPI_BIAS: return launch_one<BN, STAGES, true, EPI_BIAS>(ta, tb, a, s);
     }
   } else {
     switch (epi) {
@@ -137,8 +138,10 @@ extern "C" int ff_gemm_s8(const int8_t* A, const int8_t* W, const float* row_sca
 extern "C" int ff_gemm_f16(const uint16_t* A, const uint16_t* W, const float* bias, void* out, int M, int N, int K,
                            int epi, int ldo, int n_valid, const float* pos_bias, int patches, int tokens, int tile_n,
                            void* stream) {
-  FF_REQUIRE(epi == EPI_STEM || epi == EPI_LOGITS, "ff_gemm_f16: unknown epilogue %d", epi);
-  if (epi == EPI_STEM) {
+  FF_REQUIRE(epi == EPI_STEM || epi == EPI_LOGITS || epi == EPI_BIAS, "ff_gemm_f16: unknown epilogue %d", epi);
+  if (epi == EPI_BIAS) {
+    FF_REQUIRE(bias != nullptr && ldo >= N && ldo % 8 == 0, "ff_gemm_f16: bias epilogue needs bias and ldo >= N, ldo %% 8 == 0");
+  } else if (epi == EPI_STEM) {
     FF_REQUIRE(pos_bias != nullptr && patches >= 1 && tokens >= patches + 1, "ff_gemm_f16: stem needs pos_bias, patches, tokens");
     FF_REQUIRE(ldo >= N && ldo % 8 == 0, "ff_gemm_f16: stem ldo %d", ldo);
   } else {

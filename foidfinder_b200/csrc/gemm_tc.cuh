@@ -324,7 +324,20 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
             tmem_ld32(tbase + c0 + sub * 32, r);
             tmem_ld_wait();
             float y[32];
-            dequant32(r, rs, args.col_scale + n0 + sub * 32, args.bias + n0 + sub * 32, y);
+            if constexpr (F16IN) {
+              // fp16 operands: the accumulator is already f32; y = acc + bias.
+              const float* bp = args.bias + n0 + sub * 32;
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                const float4 b4 = *reinterpret_cast<const float4*>(bp + j);
+                y[j] = __uint_as_float(r[j]) + b4.x;
+                y[j + 1] = __uint_as_float(r[j + 1]) + b4.y;
+                y[j + 2] = __uint_as_float(r[j + 2]) + b4.z;
+                y[j + 3] = __uint_as_float(r[j + 3]) + b4.w;
+              }
+            } else {
+              dequant32(r, rs, args.col_scale + n0 + sub * 32, args.bias + n0 + sub * 32, y);
+            }
             if constexpr (EPI == EPI_QKV_ROPE) {
               if (n0 < args.rope_cols) {
                 // Interleaved pairs (2i, 2i+1) of each 64-wide head rotate by the angle of pair i at this

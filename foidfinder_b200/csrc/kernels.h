@@ -16,5 +16,13 @@ int patchify(const uint8_t* img, int B, int S, int p, const float* mean, const f
 int fill_cls(const void* cls, void* x, int B, int tokens, int dim, cudaStream_t s);
 int layernorm(const void* x, int64_t stride, const float* g, const float* b, float eps, int rows, int cols, void* out,
               cudaStream_t s);
+int slot_attend(const float* q, int64_t q_img_stride, const float* bias, int M, const void* kv, int B, int tokens,
+                int dim, int heads, float* z, float* mass_part, cudaStream_t s);
+int pool_trunk(const float* z, int B, int coarse, int leaves, int dim, const float* trunk_w, const float* trunk_b,
+               const float* q_child, const float* child_w, const float* child_b, float eps, float* z_coarse,
+               float* q_leaf, cudaStream_t s);
+int pool_leaf(const float* z_coarse, const float* z_child, const float* mass_part, int B, int coarse, int leaves,
+              int heads, int dim, int leaf_dim, const float* leaf_nw, const float* leaf_nb, float eps,
+              const float* leaf_w, const float* leaf_b, void* out, int ld_out, cudaStream_t s);
 
 }  // namespace ff

@@ -46,7 +46,47 @@ def c_config(cfg: ModelConfig) -> _lib.ModelConfig:
     c.rot_block_dim, c.rot_block_hidden, c.topk, c.ln_eps = cfg.rot_block_dim, cfg.rot_block_hidden, cfg.topk, cfg.ln_eps
     c.mean = (C.c_float * 3)(*cfg.mean)
     c.std = (C.c_float * 3)(*cfg.std)
+    c.head_kind = _lib.HEAD_TREE if cfg.head == "tree" else _lib.HEAD_CLS
+    c.pool_heads, c.coarse_queries, c.leaf_queries, c.leaf_dim = (
+        cfg.pool_heads, cfg.coarse_queries, cfg.leaf_queries, cfg.leaf_dim)
     return c
+
+
+_POOL_KEYS = {
+    "pool_norm_w": "pool.norm.weight",
+    "pool_norm_b": "pool.norm.bias",
+    "pool_kv_w": "pool.kv.weight",
+    "pool_kv_b": "pool.kv.bias",
+    "q_coarse": "pool.q_coarse",
+    "q_coarse_bias": "pool.q_coarse_bias",
+    "q_child": "pool.q_child",
+    "q_child_bias": "pool.q_child_bias",
+    "trunk_norm_w": "pool.trunk_norm.weight",
+    "trunk_norm_b": "pool.trunk_norm.bias",
+    "child_q_norm_w": "pool.child_q_norm.weight",
+    "child_q_norm_b": "pool.child_q_norm.bias",
+    "leaf_norm_w": "pool.leaf_norm.weight",
+    "leaf_norm_b": "pool.leaf_norm.bias",
+    "leaf_w": "pool.leaf.weight",
+    "leaf_b": "pool.leaf.bias",
+}
+
+
+def c_weights(cfg: ModelConfig, L: dict[str, torch.Tensor], layers) -> _lib.ModelWeights:
+    """Device tensors in the engine format -> the C weight struct (pointers only; `L` must stay alive)."""
+    for i in range(cfg.depth):
+        for field, key in _LAYER_KEYS.items():
+            setattr(layers[i], field, L[f"blocks.{i}.{key}"].data_ptr())
+    mw = _lib.ModelWeights()
+    mw.patch_w, mw.pos_bias, mw.cls_row = L["patch_w"].data_ptr(), L["pos_bias"].data_ptr(), L["cls_row"].data_ptr()
+    mw.rope_cos, mw.rope_sin = L["rope_cos"].data_ptr(), L["rope_sin"].data_ptr()
+    mw.layers = C.cast(layers, C.POINTER(_lib.LayerWeights))
+    mw.norm_w, mw.norm_b = L["norm.weight"].data_ptr(), L["norm.bias"].data_ptr()
+    mw.head_w, mw.head_b = L["head.weight"].data_ptr(), L["head.bias"].data_ptr()
+    if cfg.head == "tree":
+        for field, key in _POOL_KEYS.items():
+            setattr(mw, field, L[key].data_ptr())
+    return mw
 
 
 class Engine:
@@ -58,18 +98,9 @@ class Engine:
         if weights is None:
             weights = synthetic(cfg, seed, self.device)
         self.w = {k: v.to(self.device).contiguous() for k, v in weights.items()}
-        L = self.w
         self._c_cfg = c_config(cfg)
         self._layers = (_lib.LayerWeights * cfg.depth)()
-        for i in range(cfg.depth):
-            for field, key in _LAYER_KEYS.items():
-                setattr(self._layers[i], field, L[f"blocks.{i}.{key}"].data_ptr())
-        mw = _lib.ModelWeights()
-        mw.patch_w, mw.pos_bias, mw.cls_row = L["patch_w"].data_ptr(), L["pos_bias"].data_ptr(), L["cls_row"].data_ptr()
-        mw.rope_cos, mw.rope_sin = L["rope_cos"].data_ptr(), L["rope_sin"].data_ptr()
-        mw.layers = C.cast(self._layers, C.POINTER(_lib.LayerWeights))
-        mw.norm_w, mw.norm_b = L["norm.weight"].data_ptr(), L["norm.bias"].data_ptr()
-        mw.head_w, mw.head_b = L["head.weight"].data_ptr(), L["head.bias"].data_ptr()
+        mw = c_weights(cfg, self.w, self._layers)
         self._c_w = mw
         handle = C.c_void_p()
         _lib.check(

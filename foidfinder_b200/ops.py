@@ -16,7 +16,7 @@ from ._lib import EPI_BIAS, EPI_LOGITS, EPI_QKV_ROPE, EPI_RESIDUAL, EPI_S32, EPI
 __all__ = [
     "EPI_QKV_ROPE", "EPI_RESIDUAL", "EPI_SWIGLU", "EPI_BIAS", "EPI_S32", "EPI_STEM", "EPI_LOGITS",
     "gemm_s8", "gemm_f16", "rot_q8", "rot_q8_1024", "rot_q8_h128", "attention", "patchify", "fill_cls",
-    "layernorm", "topk",
+    "layernorm", "topk", "tree_pool",
 ]
 
 
@@ -200,3 +200,28 @@ def topk(logits: torch.Tensor, k: int, idx: torch.Tensor, val: torch.Tensor | No
 def device_error(device: int = 0, clear: bool = True) -> int:
     """Error code left by a kernel whose bounded wait ran out (0 = none); synchronises the device."""
     return _lib.device_error(device, clear)
+
+
+def tree_pool(cfg, weights: dict[str, torch.Tensor], x: torch.Tensor, leaf_out: torch.Tensor) -> None:
+    """Haruka tree attention pool head: x [B * tokens, dim] fp16 (backbone output before its final
+    LayerNorm) -> leaf_out [B, leaf_queries * leaf_dim] fp16. `weights` in the engine format
+    (`weights.convert`), on x's device."""
+    from .engine import _POOL_KEYS, c_config
+
+    _cuda(x, leaf_out)
+    _need(cfg.head == "tree", "tree_pool: config has no tree head")
+    _need(x.dtype == torch.float16 and leaf_out.dtype == torch.float16, "tree_pool: fp16 tensors expected")
+    B = x.shape[0] // cfg.tokens
+    _need(x.shape == (B * cfg.tokens, cfg.dim) and leaf_out.shape == (B, cfg.head_in), "tree_pool: bad shapes")
+    c = c_config(cfg)
+    mw = _lib.ModelWeights()
+    for field, key in {"norm_w": "norm.weight", "norm_b": "norm.bias"}.items():
+        setattr(mw, field, weights[key].data_ptr())
+    for field, key in _POOL_KEYS.items():
+        setattr(mw, field, weights[key].data_ptr())
+    nbytes = int(lib().ff_tree_pool_workspace_bytes(C.byref(c), B))
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+    with torch.cuda.device(x.device):
+        check(lib().ff_tree_pool(C.byref(c), C.byref(mw), _ptr(x), B, _ptr(ws), nbytes, _ptr(leaf_out), _stream(x)),
+              "tree_pool")
+        torch.cuda.current_stream(x.device).synchronize()  # keeps the workspace alive until the pool has run

@@ -55,9 +55,11 @@ def random_raw(cfg: ModelConfig, seed: int = 0, device: str | torch.device = "cp
         "cls_token": n(D),
         "norm.weight": 1.0 + n(D),
         "norm.bias": n(D),
-        "head.weight": n(cfg.num_tags, D),
+        "head.weight": n(cfg.num_tags, cfg.head_in),
         "head.bias": n(cfg.num_tags),
     }
+    if cfg.head == "tree":
+        raw.update(random_pool(cfg, n))
     q_scale = cfg.head_dim**-0.5
     for i in range(cfg.depth):
         p = f"blocks.{i}."
@@ -84,6 +86,25 @@ def random_raw(cfg: ModelConfig, seed: int = 0, device: str | torch.device = "cp
             }
         )
     return raw
+
+
+def random_pool(cfg: ModelConfig, n) -> dict[str, torch.Tensor]:
+    """Tree-pool weights in the folded layout (foidfinder/haruka.py:fold:66-80). Linear weights and biases
+    ~ N(0, 0.02) (key rows then scaled by pool_head_dim^-0.5 as the folding does); LayerNorm weights
+    1 + N(0, 0.02); the learned queries ~ N(0, 1) (the scale of trained query embeddings, so the slot
+    softmax is not uniform); query biases -2 + N(0, 0.02) (the model card's initial value)."""
+    D, C, Qn, L = cfg.dim, cfg.coarse_queries, cfg.leaf_queries, cfg.leaf_dim
+    kv_w, kv_b = n(2 * D, D), n(2 * D)
+    scale = (D // cfg.pool_heads) ** -0.5
+    kv_w[:D] *= scale
+    kv_b[:D] *= scale
+    out = {"pool.kv.weight": kv_w, "pool.kv.bias": kv_b}
+    for nm in ("norm", "trunk_norm", "child_q_norm", "leaf_norm"):
+        out[f"pool.{nm}.weight"], out[f"pool.{nm}.bias"] = 1.0 + n(D), n(D)
+    out["pool.q_coarse"], out["pool.q_coarse_bias"] = n(C, D, std=1.0), -2.0 + n(C)
+    out["pool.q_child"], out["pool.q_child_bias"] = n(Qn, D, std=1.0), -2.0 + n(Qn)
+    out["pool.leaf.weight"], out["pool.leaf.bias"] = n(Qn, D, L), n(Qn, L)
+    return out
 
 
 def fwht_rows(w: torch.Tensor, block: int) -> torch.Tensor:
@@ -138,12 +159,16 @@ def convert(raw: dict[str, torch.Tensor], cfg: ModelConfig, device: str | torch.
     put("rope_sin", sin)
     put("norm.weight", raw["norm.weight"].float())
     put("norm.bias", raw["norm.bias"].float())
-    hw = torch.zeros(cfg.num_tags_pad, D, device=raw["head.weight"].device)
+    hw = torch.zeros(cfg.num_tags_pad, cfg.head_in, device=raw["head.weight"].device)
     hw[: cfg.num_tags] = raw["head.weight"].float()
     hb = torch.zeros(cfg.num_tags_pad, device=hw.device)
     hb[: cfg.num_tags] = raw["head.bias"].float()
     put("head.weight", hw.half())
     put("head.bias", hb)
+    if cfg.head == "tree":
+        for k, v in raw.items():
+            if k.startswith("pool."):
+                put(k, v.half() if k == "pool.kv.weight" else v.float())
     for i in range(cfg.depth):
         p = f"blocks.{i}."
         for n in ("norm1", "norm2"):

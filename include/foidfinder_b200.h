@@ -69,6 +69,8 @@ int ff_gemm_s8(const int8_t* A, const int8_t* W, const float* row_scale, const f
  *                  x[(m / patches) * tokens + 1 + m % patches, n] = fp16(acc + pos_bias[m % patches, n]).
  *   FF_EPI_LOGITS: A [M, K] fp16, W [N, K] fp16; out[m, n] = acc + bias[n] (f32) for n < n_valid,
  *                  out row stride ldo.
+ *   FF_EPI_BIAS:   A [M, K] fp16, W [N, K] fp16; out[m, n] = fp16(acc + bias[n]), out row stride ldo
+ *                  (the Haruka pool's key/value projection, foidfinder/backends/mlx/haruka.py:124).
  * Replaces the cuBLAS matmuls of engine.py:146 (patch embedding) and reference.py:140 (head linear).
  */
 #define FF_EPI_STEM 6
@@ -158,7 +160,18 @@ typedef struct ff_model_config {
   float ln_eps;         /* 1e-6 */
   float mean[3];
   float std[3];
+  /* Head. FF_HEAD_CLS: final LayerNorm of the class token -> linear [num_tags, dim]. FF_HEAD_TREE: the
+   * Haruka tree attention pool (foidfinder/backends/mlx/haruka.py:104-136) over all tokens ->
+   * linear [num_tags, leaf_queries * leaf_dim]. */
+  int head_kind;
+  int pool_heads;     /* 16; dim / pool_heads in {48, 64} */
+  int coarse_queries; /* 6 */
+  int leaf_queries;   /* 18, a multiple of coarse_queries */
+  int leaf_dim;       /* 64 */
 } ff_model_config;
+
+#define FF_HEAD_CLS 0
+#define FF_HEAD_TREE 1
 
 typedef struct ff_layer_weights {
   const float *norm1_w, *norm1_b;
@@ -181,9 +194,32 @@ typedef struct ff_model_weights {
   const float *rope_cos, *rope_sin; /* [tokens, 32] */
   const ff_layer_weights* layers;   /* [depth] */
   const float *norm_w, *norm_b;     /* final LayerNorm */
-  const uint16_t* head_w;           /* [num_tags_pad, dim] fp16 */
+  const uint16_t* head_w;           /* [num_tags_pad, dim] (CLS) or [num_tags_pad, leaf_queries * leaf_dim] fp16 */
   const float* head_b;              /* [num_tags_pad] */
+  /* FF_HEAD_TREE only (NULL otherwise); layout of foidfinder/haruka.py:fold, f32 unless noted. */
+  const float *pool_norm_w, *pool_norm_b;     /* [dim] */
+  const uint16_t* pool_kv_w;                  /* [2*dim, dim] fp16, key rows pre-scaled by head_dim^-0.5 */
+  const float* pool_kv_b;                     /* [2*dim] */
+  const float *q_coarse, *q_coarse_bias;      /* [coarse, dim], [coarse] */
+  const float *q_child, *q_child_bias;        /* [leaves, dim], [leaves] */
+  const float *trunk_norm_w, *trunk_norm_b;   /* [dim] */
+  const float *child_q_norm_w, *child_q_norm_b;
+  const float *leaf_norm_w, *leaf_norm_b;
+  const float *leaf_w, *leaf_b;               /* [leaves, dim, leaf_dim], [leaves, leaf_dim] */
 } ff_model_weights;
+
+/*
+ * The Haruka tree attention pool head on its own: x [B * tokens, dim] fp16 (the backbone's output before its
+ * final LayerNorm; tokens = (image_size / patch)^2 + 1) -> leaf features leaf_out [B, leaf_queries * leaf_dim]
+ * fp16, the input of the tag head. Runs: final LayerNorm (w->norm_*), pool LayerNorm, key/value GEMM
+ * (tcgen05 fp16), coarse slot attention, trunk/child LayerNorms, leaf slot attention, leaf LayerNorm x
+ * mass gate x per-leaf projection (foidfinder/backends/mlx/haruka.py:104-136). cfg->head_kind must be
+ * FF_HEAD_TREE. workspace: caller-allocated device memory, 256-byte aligned, at least
+ * ff_tree_pool_workspace_bytes(cfg, B) bytes.
+ */
+int ff_tree_pool(const ff_model_config* cfg, const struct ff_model_weights* w, const uint16_t* x, int B,
+                 void* workspace, int64_t workspace_bytes, uint16_t* leaf_out, void* stream);
+int64_t ff_tree_pool_workspace_bytes(const ff_model_config* cfg, int B);
 
 typedef struct ff_engine ff_engine;
 

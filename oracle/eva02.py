@@ -78,8 +78,48 @@ def forward_fp32(raw: dict[str, torch.Tensor], cfg, images: torch.Tensor) -> tor
         hid = Q.silu_mul(gu[:, : cfg.mlp_hidden], gu[:, cfg.mlp_hidden :])
         hid = Q.layer_norm(hid, raw[p + "mlp_norm.weight"], raw[p + "mlp_norm.bias"], eps)
         x = x + hid @ raw[p + "fc2.weight"].float().t() + raw[p + "fc2.bias"].float()
-    xc = Q.layer_norm(x.view(B, T, D)[:, 0], raw["norm.weight"], raw["norm.bias"], eps)
-    return xc @ raw["head.weight"].float().t() + raw["head.bias"].float()
+    if cfg.head == "tree":
+        xf = Q.layer_norm(x, raw["norm.weight"], raw["norm.bias"], eps).view(B, T, D)
+        feat = tree_pool(xf, raw, cfg, half=False)
+    else:
+        feat = Q.layer_norm(x.view(B, T, D)[:, 0], raw["norm.weight"], raw["norm.bias"], eps)
+    return feat @ raw["head.weight"].float().t() + raw["head.bias"].float()
+
+
+def tree_pool(x: torch.Tensor, w: dict, cfg, half: bool, eps: float | None = None) -> torch.Tensor:
+    """Haruka tree attention pool (foidfinder/backends/mlx/haruka.py:104-136; the model card's MHAttnPool,
+    tests/test_haruka.py:73-122) on final-normed tokens x [B, T, D] -> leaf features [B, leaves * leaf_dim].
+
+    w holds the folded pool weights (`pool.*`, haruka.py:fold:66-80: key rows of `pool.kv` carry the
+    1/sqrt(pool head dim) scale). With half=True the fp16 storage points of the GPU engine are applied
+    (pool-normed tokens, key/value, leaf features); everything else is f32. The LayerNorm eps is the
+    backbone's (1e-6, as mlx/haruka.py:19 uses for every norm) unless given: the model card's pool
+    LayerNorms use torch's default 1e-5."""
+    B, T, D = x.shape
+    Hp, C, Qn, L = cfg.pool_heads, cfg.coarse_queries, cfg.leaf_queries, cfg.leaf_dim
+    hd, eps = D // Hp, cfg.ln_eps if eps is None else eps
+    f = (lambda t: t.half().float()) if half else (lambda t: t)
+    g = lambda k: w[k].float()  # noqa: E731
+    xn = f(Q.layer_norm(x.reshape(B * T, D).float(), g("pool.norm.weight"), g("pool.norm.bias"), eps))
+    kv = f(xn @ g("pool.kv.weight").t() + g("pool.kv.bias")).view(B, T, 2, Hp, hd)
+    k, v = kv[:, :, 0].transpose(1, 2), kv[:, :, 1].transpose(1, 2)  # [B, Hp, T, hd]
+
+    def slot_attend(q: torch.Tensor, bias: torch.Tensor):  # q [B, M, D] -> attn [B, Hp, M, T], z [B, M, D]
+        qh = q.view(B, -1, Hp, hd).transpose(1, 2)
+        logits = qh @ k.transpose(-1, -2)
+        attn = torch.softmax(logits, dim=2) * torch.sigmoid(logits + bias.view(1, 1, -1, 1))
+        return attn, (attn @ v).transpose(1, 2).reshape(B, -1, D)
+
+    _, z = slot_attend(g("pool.q_coarse").expand(B, C, D), g("pool.q_coarse_bias"))
+    z_coarse = Q.layer_norm(z, g("pool.trunk_norm.weight"), g("pool.trunk_norm.bias"), eps)
+    z_parent = z_coarse.repeat_interleave(Qn // C, dim=1)
+    q_leaf = Q.layer_norm(z_parent + g("pool.q_child"), g("pool.child_q_norm.weight"), g("pool.child_q_norm.bias"), eps)
+    attn, z_child = slot_attend(q_leaf, g("pool.q_child_bias"))
+    z_tree = Q.layer_norm(z_parent + z_child, g("pool.leaf_norm.weight"), g("pool.leaf_norm.bias"), eps)
+    mass = attn.sum(-1).mean(1)[..., None]  # [B, leaves, 1]
+    z_tree = z_tree * (mass / (mass + 4.0))
+    leaf = torch.einsum("bqd,qdf->bqf", z_tree, g("pool.leaf.weight")) + g("pool.leaf.bias")
+    return f(leaf.reshape(B, Qn * L))
 
 
 def _lin(a8: torch.Tensor, rs: torch.Tensor, conv: dict, name: str) -> torch.Tensor:
@@ -132,7 +172,11 @@ def forward_int8(
                 dict(x_in=x_in, a8=a8, rs=rs, qkv=qkv, o=o, a8o=a8o, rso=rso, x_attn=x_mid, a8m=a8m, rsm=rsm, h=h,
                      a8h=a8h, rsh=rsh, x_out=x)
             )
-    xc = Q.layer_norm(x.view(B, T, D)[:, 0], conv["norm.weight"], conv["norm.bias"], eps).half()
+    if cfg.head == "tree":
+        xf = Q.layer_norm(x.float(), conv["norm.weight"], conv["norm.bias"], eps).half().float().view(B, T, D)
+        xc = tree_pool(xf, conv, cfg, half=True).half()
+    else:
+        xc = Q.layer_norm(x.view(B, T, D)[:, 0], conv["norm.weight"], conv["norm.bias"], eps).half()
     logits = xc.float() @ conv["head.weight"].float()[: cfg.num_tags].t() + conv["head.bias"][: cfg.num_tags]
     if trace is not None:
         trace.append(dict(x_stem=x_stem, patches=patches.half(), x_final=x, cls=xc, logits=logits))

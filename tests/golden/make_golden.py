@@ -14,8 +14,10 @@ What it records (inputs are seeded; every function is the reference's, unmodifie
 - `rope_tables(32, 16, 64)` of `foidfinder/backends/mlx/haruka.py` (the EVA02 RoPE), executed from the
   function's source text because that module imports MLX at load time;
 - `foidfinder.haruka.fold` on a seeded tiny timm-style checkpoint (model dims shrunk through its
-  `MODEL` dict): the folded patch embedding (pixel normalisation inside the weights) and the fused
-  qkv with the q scale and zero k bias.
+  `MODEL` dict): the folded patch embedding (pixel normalisation inside the weights), the fused qkv with
+  the q scale and zero k bias, and the tree-pool tensors (key rows scaled);
+- the model card's tree attention pool `MHAttnPool` (defined inside the `haruka` fixture of
+  `tests/test_haruka.py`, executed from its source text) on seeded tokens with the same checkpoint.
 """
 
 from __future__ import annotations
@@ -27,6 +29,7 @@ from pathlib import Path
 import numpy as np
 
 
+TREE = {"dim": 64, "pool_heads": 4, "coarse": 6, "leaves": 18, "leaf_dim": 8, "tokens": 9, "images": 2}
 CONV_SHAPES = {"attn.qkv": (24, 1024), "attn.proj": (8, 1024), "mlp.fc1": (16, 1024), "mlp.fc2": (8, 256)}
 EVA_ROPE_ROWS = np.r_[0:40, 40:1025:37, 1024]
 
@@ -91,20 +94,43 @@ def main(ref_root: str) -> None:
     out["eva_rope_checksum"] = np.array([ecos.astype(np.float64).sum(), esin.astype(np.float64).sum(), ecos.shape[0]])
 
     saved_model = dict(haruka.MODEL)
-    haruka.MODEL.update(dim=64, heads=2, depth=1)
+    haruka.MODEL.update(dim=64, heads=2, depth=1, pool_heads=TREE["pool_heads"])
     try:
         sd = fold_inputs()
         folded = haruka.fold(sd)
     finally:
         haruka.MODEL.clear()
         haruka.MODEL.update(saved_model)
-    for k in ("patch_w", "patch_b", "cls", "blocks.0.qkv.weight", "blocks.0.qkv.bias", "blocks.0.fc1.weight",
-              "blocks.0.fc1.bias"):
+    for k in FOLD_KEYS:
         out["fold_out_" + k.replace(".", "_")] = folded[k]
+
+    # The model card's tree pool (MHAttnPool, defined inside the `haruka` fixture of tests/test_haruka.py),
+    # executed from its source text with the same seeded weights.
+    src = (Path(ref_root) / "tests/test_haruka.py").read_text()
+    fixture = next(n for n in ast.parse(src).body if isinstance(n, ast.FunctionDef) and n.name == "haruka")
+    cls_def = next(n for n in ast.walk(fixture) if isinstance(n, ast.ClassDef) and n.name == "MHAttnPool")
+    ns = {"torch": torch, "nn": torch.nn}
+    exec(compile(ast.Module(body=[cls_def], type_ignores=[]), "model_card_MHAttnPool", "exec"), ns)
+    pool = ns["MHAttnPool"](dim=TREE["dim"], num_heads=TREE["pool_heads"], num_queries=TREE["leaves"],
+                            leaf_dim=TREE["leaf_dim"])
+    pool.load_state_dict({k[len("head_pool."):]: torch.from_numpy(v) for k, v in sd.items() if k.startswith("head_pool.")})
+    with torch.no_grad():
+        out["tree_leaf"] = pool(torch.from_numpy(tree_input())).numpy()
 
     dst = Path(__file__).resolve().parent / "reference_vectors.npz"
     np.savez_compressed(dst, **out)
     print(f"wrote {dst} ({dst.stat().st_size} bytes, {len(out)} arrays)")
+
+
+FOLD_KEYS = ("patch_w", "patch_b", "cls", "blocks.0.qkv.weight", "blocks.0.qkv.bias", "blocks.0.fc1.weight",
+             "blocks.0.fc1.bias", "pool.kv.weight", "pool.kv.bias", "pool.q_coarse", "pool.q_coarse_bias",
+             "pool.q_child", "pool.q_child_bias", "pool.leaf.weight", "pool.leaf.bias", "pool.trunk_norm.weight")
+
+
+def tree_input() -> np.ndarray:
+    """Seeded final-normed tokens [images, tokens, dim] for the tree pool."""
+    rng = np.random.default_rng(11)
+    return rng.standard_normal((TREE["images"], TREE["tokens"], TREE["dim"])).astype(np.float32)
 
 
 def fold_inputs() -> dict[str, np.ndarray]:
@@ -112,8 +138,8 @@ def fold_inputs() -> dict[str, np.ndarray]:
     rng = np.random.default_rng(7)
     D, p = 64, 14
 
-    def r(*shape):
-        return (rng.standard_normal(shape) * 0.02).astype(np.float32)
+    def r(*shape, std=0.02):
+        return (rng.standard_normal(shape) * std).astype(np.float32)
 
     bb = "backbone."
     sd = {
@@ -123,16 +149,16 @@ def fold_inputs() -> dict[str, np.ndarray]:
         bb + "cls_token": r(1, 1, D),
         bb + "norm.weight": r(D),
         bb + "norm.bias": r(D),
-        "head_pool.kv.weight": r(2 * D, D),
-        "head_pool.kv.bias": r(2 * D),
-        "head.weight": r(3, 4),
+        "head.weight": r(3, TREE["leaves"] * TREE["leaf_dim"]),
         "head.bias": r(3),
     }
     for nm in ("norm", "trunk_norm", "child_q_norm", "leaf_norm"):
-        sd[f"head_pool.{nm}.weight"], sd[f"head_pool.{nm}.bias"] = r(D), r(D)
-    sd.update({"head_pool.q_coarse": r(1, 2, D), "head_pool.q_coarse_bias": r(1, 1, 2, 1),
-               "head_pool.q_child": r(1, 2, 1, D), "head_pool.q_child_bias": r(1, 1, 2, 1),
-               "head_pool.leaf_proj_weight": r(2, D, 4), "head_pool.leaf_proj_bias": r(2, 4)})
+        sd[f"head_pool.{nm}.weight"], sd[f"head_pool.{nm}.bias"] = 1.0 + r(D), r(D)
+    C, Qn, L = TREE["coarse"], TREE["leaves"], TREE["leaf_dim"]
+    sd.update({"head_pool.q_coarse": r(1, C, D, std=1.0), "head_pool.q_coarse_bias": -2.0 + r(1, 1, C, 1),
+               "head_pool.q_child": r(1, C, Qn // C, D, std=1.0), "head_pool.q_child_bias": -2.0 + r(1, 1, Qn, 1),
+               "head_pool.leaf_proj_weight": r(Qn, D, L, std=0.1), "head_pool.leaf_proj_bias": r(Qn, L),
+               "head_pool.kv.weight": r(2 * D, D, std=0.2), "head_pool.kv.bias": r(2 * D)})
     a, m = bb + "blocks.0.attn.", bb + "blocks.0.mlp."
     for nm in ("q_proj", "k_proj", "v_proj", "proj"):
         sd[a + nm + ".weight"], sd[a + nm + ".bias"] = r(D, D), r(D)

@@ -109,3 +109,30 @@ def test_attention_zero_sequences_is_a_no_op():
 def test_kernel_error_maps_status():
     with pytest.raises(_lib.KernelError, match="invalid argument"):
         _lib.check(1, "probe")
+
+
+def test_struct_layouts_match_ctypes(tmp_path):
+    """The ctypes mirrors of the header's structs have the C compiler's sizes and field offsets."""
+    import shutil
+
+    gcc = shutil.which("gcc") or shutil.which("cc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    structs = {"ff_model_config": _lib.ModelConfig, "ff_layer_weights": _lib.LayerWeights,
+               "ff_model_weights": _lib.ModelWeights}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "foidfinder_b200.h"', "int main(void) {"]
+    for cname, py in structs.items():
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for field, _ in py._fields_:
+            lines.append(f'  printf("{cname}.{field} %zu\\n", offsetof({cname}, {field}));')
+    lines.append("  return 0;\n}")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run([gcc, "-I", str(ROOT / "include"), str(src), "-o", str(exe)], check=True)
+    got = dict(line.rsplit(" ", 1) for line in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                              check=True).stdout.splitlines())
+    for cname, py in structs.items():
+        assert int(got[f"{cname} size"]) == C.sizeof(py), cname
+        for field, _ in py._fields_:
+            assert int(got[f"{cname}.{field}"]) == getattr(py, field).offset, f"{cname}.{field}"

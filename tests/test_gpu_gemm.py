@@ -133,6 +133,25 @@ def test_gemm_f16_logits_epilogue(cuda_device, no_device_error):
     torch.testing.assert_close(out.cpu(), ref[:, :n_tags], atol=1e-4, rtol=1e-4)
 
 
+@pytest.mark.parametrize("M", [1025 * 3, 77])
+def test_gemm_f16_bias_epilogue(cuda_device, no_device_error, M):
+    """fp16 x fp16 -> f32 accumulation + bias -> fp16 (the tree pool's key/value projection shape)."""
+    from foidfinder_b200 import ops
+
+    g = torch.Generator().manual_seed(9)
+    K, N = 768, 1536
+    A = torch.randn(M, K, generator=g).half()
+    W = (torch.randn(N, K, generator=g) * 0.05).half()
+    bias = torch.randn(N, generator=g) * 0.1
+    ref = (A.float() @ W.float().t() + bias).half()
+    d = cuda_device
+    out = torch.full((M, N), float("nan"), dtype=torch.float16, device=d)
+    ops.gemm_f16(A.to(d), W.to(d), out, ops.EPI_BIAS, bias=bias.to(d))
+    torch.cuda.synchronize()
+    # f32 accumulation in a different order, then one fp16 rounding: at most one fp16 ulp apart.
+    torch.testing.assert_close(out.cpu().float(), ref.float(), atol=2e-3, rtol=1e-3)
+
+
 def test_gemm_f16_stem_epilogue(cuda_device, no_device_error):
     from foidfinder_b200 import ops
 

@@ -94,14 +94,21 @@ def _teacher_forced(cfg, conv, imgs, d):
         torch.cuda.synchronize()
         _fp16_close(xr, st["x_out"], tag + " down GEMM + residual")
 
-    cls = torch.empty(B, D, dtype=torch.float16, device=d)
-    ops.layernorm(fin["x_final"].to(d), T * D, B, D, W["norm.weight"], W["norm.bias"], eps, cls)
+    cls = torch.empty(B, cfg.head_in, dtype=torch.float16, device=d)
+    if cfg.head == "tree":
+        ops.tree_pool(cfg, W, fin["x_final"].to(d), cls)
+        torch.cuda.synchronize()
+        err = (cls.cpu().float() - fin["cls"].float()).abs().max().item()
+        assert err <= 4e-3 * fin["cls"].float().abs().max().item(), f"tree pool: max err {err:.3e}"
+    else:
+        ops.layernorm(fin["x_final"].to(d), T * D, B, D, W["norm.weight"], W["norm.bias"], eps, cls)
+        torch.cuda.synchronize()
+        _fp16_close(cls, fin["cls"], "final LayerNorm")
     logits = torch.empty(B, cfg.num_tags, device=d)
     ops.gemm_f16(fin["cls"].to(d), W["head.weight"], logits, ops.EPI_LOGITS, bias=W["head.bias"], n_valid=cfg.num_tags)
     idx = torch.empty(B, cfg.topk, dtype=torch.int32, device=d)
     ops.topk(fin["logits"].to(d), cfg.topk, idx)
     torch.cuda.synchronize()
-    _fp16_close(cls, fin["cls"], "final LayerNorm")
     torch.testing.assert_close(logits.cpu(), fin["logits"], atol=1e-4, rtol=1e-4)
     ref_idx = torch.sort(fin["logits"], dim=1, descending=True, stable=True).indices[:, : cfg.topk]
     assert torch.equal(idx.cpu().long(), ref_idx)
@@ -127,8 +134,8 @@ def test_teacher_forced_full_eva02_l(cuda_device, no_device_error):
     _teacher_forced(EVA02_L, conv, imgs, cuda_device)
 
 
-def test_teacher_forced_eva02_b_backbone(cuda_device, no_device_error):
-    """The Haruka backbone shape (dim 768, H256 rotation, hidden 2048, ImageNet normalisation)."""
+def test_teacher_forced_eva02_b(cuda_device, no_device_error):
+    """The Haruka shape (dim 768, H256 rotation, hidden 2048, ImageNet normalisation, tree pool head)."""
     from foidfinder_b200.config import EVA02_B
     from foidfinder_b200.weights import convert, random_raw
 

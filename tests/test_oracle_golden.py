@@ -92,10 +92,29 @@ def test_eva02_rope_tables(gold, tables):
 
 def test_haruka_fold(gold):
     sd = make_golden.fold_inputs()
-    out = F.fold(sd, dim=64, heads=2, patch=14, depth=1)
-    for k in ("patch_w", "patch_b", "cls", "blocks.0.qkv.weight", "blocks.0.qkv.bias", "blocks.0.fc1.weight",
-              "blocks.0.fc1.bias"):
+    out = F.fold(sd, dim=64, heads=2, patch=14, depth=1, pool_heads=make_golden.TREE["pool_heads"])
+    for k in make_golden.FOLD_KEYS:
         np.testing.assert_allclose(out[k], gold["fold_out_" + k.replace(".", "_")], rtol=1e-5, atol=1e-7, err_msg=k)
+
+
+def test_tree_pool_matches_model_card(gold):
+    """The oracle's tree pool on the folded weights reproduces the model card's MHAttnPool (unfolded
+    weights, f32, its LayerNorms at torch's default eps 1e-5)."""
+    from foidfinder_b200.config import EVA02_B
+
+    T = make_golden.TREE
+    cfg = EVA02_B.with_(dim=T["dim"], pool_heads=T["pool_heads"], coarse_queries=T["coarse"],
+                        leaf_queries=T["leaves"], leaf_dim=T["leaf_dim"])
+    w = {k: torch.from_numpy(np.asarray(v)) for k, v in
+         F.fold(make_golden.fold_inputs(), dim=T["dim"], heads=2, patch=14, depth=1, pool_heads=T["pool_heads"]).items()}
+    x = torch.from_numpy(make_golden.tree_input())
+    got = E.tree_pool(x, w, cfg, half=False, eps=1e-5).numpy()
+    assert np.abs(gold["tree_leaf"]).max() > 0.05  # the pool is not degenerate at these scales
+    np.testing.assert_allclose(got, gold["tree_leaf"], rtol=1e-4, atol=1e-5)
+    # At the backbone's eps (what the MLX port and the engine use) the features move by far less than
+    # the int8 noise.
+    got6 = E.tree_pool(x, w, cfg, half=False).numpy()
+    assert np.abs(got6 - gold["tree_leaf"]).max() < 1e-3
 
 
 def test_fold_matches_engine_patch_convention(gold):
