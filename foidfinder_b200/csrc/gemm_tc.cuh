@@ -11,8 +11,9 @@
 //              output row per thread; two warps per lane quarter split the columns), fused
 //              dequantisation / bias / RoPE / SwiGLU / residual, then the warp's 32-row block goes out
 //              through a swizzled shared-memory stage as whole 128-byte lines.
-// The epilogue avoids the narrow XU pipe (int->float, division) so it hides under the next tile's
-// mainloop: see i2f_exact and silu_mul.
+// The epilogue balances the issue slots against the narrow XU pipe: int->float uses the hardware
+// conversion (acc_to_float), the SwiGLU sigmoid one ex2 plus a Newton reciprocal (silu_mul), so the
+// epilogue of one tile hides under the next tile's mainloop as far as possible.
 // Accumulators are double-buffered in TMEM (2 x BN columns), so the epilogue of tile i overlaps the
 // mainloop of tile i+1. Stages are a ring of STAGES smem buffers guarded by full/empty mbarriers.
 #pragma once
@@ -38,16 +39,6 @@ struct GemmCfg {
   static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM columns must be a power of two");
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
-
-// Exact round-to-nearest int32 -> f32 on the ALU/FMA pipes (the I2F conversion runs on the narrow XU
-// pipe): acc = hi * 4096 + lo, each half turned into a float by the magic-number method (an integer
-// placed in the mantissa of 1.5 * 2^23 resp. 2^23), recombined by one correctly rounded FMA.
-__device__ __forceinline__ float i2f_exact(uint32_t raw) {
-  const int acc = static_cast<int>(raw);
-  const float fhi = __int_as_float((acc >> 12) + 0x4B400000) - 12582912.f;
-  const float flo = __int_as_float((acc & 0xFFF) | 0x4B000000) - 8388608.f;
-  return fmaf(fhi, 4096.f, flo);
-}
 
 // 1 / d for d >= 1: the bit-level "magic constant" reciprocal estimate (a published method; relative
 // error below 1/8) refined by three Newton steps y <- y (2 - d y), all on the FMA pipe.
@@ -89,16 +80,22 @@ __device__ __forceinline__ uint4 staged_chunk64(const uint8_t* stg, int r, int c
 }
 
 // y[j] = acc[j] * rs * cs[n0 + j] + bias[n0 + j] for 32 consecutive columns.
+// int32 accumulator -> f32, correctly rounded. The hardware conversion (I2F, on the XU pipe) costs one
+// issue slot per 32 values; an exact integer/FMA-pipe form (two magic-number halves recombined by an FMA)
+// costs six. With the current epilogues the XU pipe has room, and I2F measured faster on every GEMM
+// shape (SwiGLU epilogue +12%).
+__device__ __forceinline__ float acc_to_float(uint32_t raw) { return __int2float_rn(static_cast<int>(raw)); }
+
 __device__ __forceinline__ void dequant32(const uint32_t (&r)[32], float rs, const float* cs, const float* bias,
                                           float (&y)[32]) {
 #pragma unroll
   for (int j = 0; j < 32; j += 4) {
     const float4 c4 = *reinterpret_cast<const float4*>(cs + j);
     const float4 b4 = *reinterpret_cast<const float4*>(bias + j);
-    y[j] = i2f_exact(r[j]) * rs * c4.x + b4.x;
-    y[j + 1] = i2f_exact(r[j + 1]) * rs * c4.y + b4.y;
-    y[j + 2] = i2f_exact(r[j + 2]) * rs * c4.z + b4.z;
-    y[j + 3] = i2f_exact(r[j + 3]) * rs * c4.w + b4.w;
+    y[j] = acc_to_float(r[j]) * rs * c4.x + b4.x;
+    y[j + 1] = acc_to_float(r[j + 1]) * rs * c4.y + b4.y;
+    y[j + 2] = acc_to_float(r[j + 2]) * rs * c4.z + b4.z;
+    y[j + 3] = acc_to_float(r[j + 3]) * rs * c4.w + b4.w;
   }
 }
 
@@ -341,21 +338,19 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
             if constexpr (EPI == EPI_QKV_ROPE) {
               if (n0 < args.rope_cols) {
                 // Interleaved pairs (2i, 2i+1) of each 64-wide head rotate by the angle of pair i at this
-                // token's position; the table row of position 0 (class token) is the identity.
+                // token's position; the table column of position 0 (class token) is the identity. The
+                // tables are angle-major [32, tokens], so the warp's 32 consecutive rows read 128
+                // contiguous bytes per angle (one wavefront) instead of 32 scattered 16-byte pieces.
                 const int pos = (row_ok ? m : 0) % args.tokens;
-                const float* cr = args.rope_cos + static_cast<size_t>(pos) * 32 + sub * 16;
-                const float* sr = args.rope_sin + static_cast<size_t>(pos) * 32 + sub * 16;
+                const float* cr = args.rope_cos + static_cast<size_t>(sub * 16) * args.tokens + pos;
+                const float* sr = args.rope_sin + static_cast<size_t>(sub * 16) * args.tokens + pos;
 #pragma unroll
-                for (int j = 0; j < 16; j += 4) {
-                  const float4 c4 = *reinterpret_cast<const float4*>(cr + j);
-                  const float4 s4 = *reinterpret_cast<const float4*>(sr + j);
-                  const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-                  for (int e = 0; e < 4; ++e) {
-                    const float x0 = y[2 * (j + e)], x1 = y[2 * (j + e) + 1];
-                    y[2 * (j + e)] = x0 * cc[e] - x1 * ss[e];
-                    y[2 * (j + e) + 1] = x0 * ss[e] + x1 * cc[e];
-                  }
+                for (int j = 0; j < 16; ++j) {
+                  const float cc = __ldg(cr + static_cast<size_t>(j) * args.tokens);
+                  const float ss = __ldg(sr + static_cast<size_t>(j) * args.tokens);
+                  const float x0 = y[2 * j], x1 = y[2 * j + 1];
+                  y[2 * j] = x0 * cc - x1 * ss;
+                  y[2 * j + 1] = x0 * ss + x1 * cc;
                 }
               }
             }

@@ -5,128 +5,208 @@
 // (kernels.cu:112-160); quantiser semantics from common.cuh:45-48; the EVA02 LayerNorm eps and the
 // SwiGLU hidden norm from foidfinder/backends/mlx/haruka.py:19,97-98.
 //
-// One warp per row, 8 rows per 256-thread CTA. Lane l owns 8 consecutive columns of every 256-column
-// chunk i (columns i*256 + l*8 + e), loaded as 16-byte vectors, so a row costs one coalesced read of
-// 2 B/column and one write of 1 B/column plus the 4-byte scale: the kernel is HBM-bound. The
-// Hadamard butterflies over column bits 0-2 run in registers, bits 3-7 across lanes (shuffles), bits 8+
-// across the lane's chunks (registers).
+// One warp per row, kRotWarps rows per CTA; the whole row stays in registers. Lane l holds 8
+// consecutive columns of every 256-column chunk i (columns i*256 + l*8 + e), loaded as 16-byte vectors,
+// so a row costs one coalesced read of 2 B/column and one write of 1 B/column plus the 4-byte scale.
+//
+// The Hadamard butterflies over column bits 0-2 (e) and 8+ (chunk) run in registers in that layout. The
+// butterflies over bits 3..7 (the lane index) do not use shuffles: a group of UNIT chunks is written to a
+// per-warp shared-memory buffer and read back transposed — lane (e, q) then holds the G = 2^TB values
+// whose columns differ only in bits 3..3+TB-1 — the butterflies run in registers, and the values go back
+// through the same buffer into the load layout. Two shared-memory round trips per element replace one
+// shuffle + select + add per element per lane-bit stage. The buffer is padded by 8 floats every 8*G
+// columns so the transposed accesses hit 32 distinct banks. Arithmetic is packed f32x2 wherever both
+// halves of a register pair take the same operation (exactly rounded per lane, like scalar FADD/FFMA).
+//
+// The LayerNorm runs over the first valid_cols columns: columns past it are zeroed at load, their
+// (0 - mean)^2 terms are taken back out of the variance, and they are zeroed again after the affine step.
 #include "common.h"
 #include "ptx.cuh"
 
 namespace ff {
 
+constexpr int kRotWarps = 4;  // small CTAs: the 2816-column rows need ~134 registers per thread
+
 template <int NCH, int BLOCK, bool NORM>
-__global__ void __launch_bounds__(256) rot_q8_kernel(const __half* __restrict__ x, const float* __restrict__ gamma,
-                                                     const float* __restrict__ beta, float eps, int rows,
-                                                     int valid_cols, int8_t* __restrict__ out,
-                                                     float* __restrict__ row_scale) {
+__global__ void __launch_bounds__(kRotWarps * 32)
+    rot_q8_kernel(const __half* __restrict__ x, const float* __restrict__ gamma, const float* __restrict__ beta,
+                  float eps, int rows, int valid_cols, int8_t* __restrict__ out, float* __restrict__ row_scale) {
+  constexpr int LB = BLOCK == 128 ? 7 : BLOCK == 256 ? 8 : BLOCK == 512 ? 9 : 10;
+  constexpr int TB = LB - 3 < 5 ? LB - 3 : 5;  // column bits 3..3+TB-1 run in the transposed layout
+  constexpr int G = 1 << TB;                   // values per lane in the transposed layout
+  constexpr int UNIT = G / 8;                  // 256-column chunks per transpose
+  constexpr int NCHP = (NCH + UNIT - 1) / UNIT * UNIT;
   constexpr int COLS = NCH * 256;
-  const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  constexpr int QB = 8 * G;  // columns per transposed lane group (padding period)
+  constexpr int SW = UNIT * 256 + 8 * (UNIT * 256 / QB);
+  static_assert((1 << LB) == BLOCK && BLOCK / 256 <= UNIT, "unsupported Hadamard block");
+  __shared__ __align__(16) float smem[kRotWarps][SW];
+
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int row = blockIdx.x * kRotWarps + wid;
   if (row >= rows) return;
+  float* sw = smem[wid];
   const __half* xr = x + static_cast<size_t>(row) * COLS;
-  float v[NCH][8];
+
+  float2 v[NCHP][4];
 #pragma unroll
-  for (int i = 0; i < NCH; ++i) {
-    const uint4 u = __ldg(reinterpret_cast<const uint4*>(xr + i * 256 + lane * 8));
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  for (int i = 0; i < NCHP; ++i) {
+    if (i < NCH) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(xr + i * 256 + lane * 8));
+      v[i][0] = unpack_half2(u.x);
+      v[i][1] = unpack_half2(u.y);
+      v[i][2] = unpack_half2(u.z);
+      v[i][3] = unpack_half2(u.w);
+    } else {
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = unpack_half2(w[e]);
-      v[i][2 * e] = f.x;
-      v[i][2 * e + 1] = f.y;
+      for (int k = 0; k < 4; ++k) v[i][k] = make_float2(0.f, 0.f);
     }
   }
-  if constexpr (NORM) {
-    float s = 0.f;
+  // Columns >= valid_cols: only chunks that reach past the boundary take this (warp-uniform) branch.
+  auto zero_ragged = [&](int i) {
+    if (i < NCH && (i + 1) * 256 > valid_cols) {
 #pragma unroll
-    for (int i = 0; i < NCH; ++i)
-#pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (i * 256 + lane * 8 + e < valid_cols) s += v[i][e];
-    const float inv_n = 1.f / static_cast<float>(valid_cols);
-    const float mean = warp_sum(s) * inv_n;
-    float q = 0.f;
-#pragma unroll
-    for (int i = 0; i < NCH; ++i)
-#pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (i * 256 + lane * 8 + e < valid_cols) {
-          const float d = v[i][e] - mean;
-          q += d * d;
-        }
-    const float rstd = rsqrtf(warp_sum(q) * inv_n + eps);
-#pragma unroll
-    for (int i = 0; i < NCH; ++i) {
-      const int c = i * 256 + lane * 8;
-      const float4 g0 = __ldg(reinterpret_cast<const float4*>(gamma + c));
-      const float4 g1 = __ldg(reinterpret_cast<const float4*>(gamma + c + 4));
-      const float4 b0 = __ldg(reinterpret_cast<const float4*>(beta + c));
-      const float4 b1 = __ldg(reinterpret_cast<const float4*>(beta + c + 4));
-      const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-      const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[i][e] = c + e < valid_cols ? (v[i][e] - mean) * rstd * g[e] + b[e] : 0.f;
+      for (int k = 0; k < 4; ++k) {
+        const int c = i * 256 + lane * 8 + 2 * k;
+        if (c >= valid_cols) v[i][k].x = 0.f;
+        if (c + 1 >= valid_cols) v[i][k].y = 0.f;
+      }
     }
-  } else {
+  };
+#pragma unroll
+  for (int i = 0; i < NCH; ++i) zero_ragged(i);
+
+  float rstd = 0.f;
+  if constexpr (NORM) {
+    float2 s2 = make_float2(0.f, 0.f);
 #pragma unroll
     for (int i = 0; i < NCH; ++i)
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (i * 256 + lane * 8 + e >= valid_cols) v[i][e] = 0.f;
+      for (int k = 0; k < 4; ++k) s2 = add2(s2, v[i][k]);
+    const float inv_n = 1.f / static_cast<float>(valid_cols);
+    const float mean = warp_sum(s2.x + s2.y) * inv_n;
+    const float2 m2 = make_float2(mean, mean);
+    float2 q2 = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < NCH; ++i)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        v[i][k] = sub2(v[i][k], m2);
+        q2 = fma2(v[i][k], v[i][k], q2);
+      }
+    const float q = warp_sum(q2.x + q2.y) - static_cast<float>(COLS - valid_cols) * mean * mean;
+    rstd = rsqrtf(fmaxf(q, 0.f) * inv_n + eps);
   }
 
-  // Column bits 0-2: inside the lane's 8-element group.
 #pragma unroll
-  for (int h = 1; h < 8; h <<= 1)
+  for (int c0 = 0; c0 < NCHP; c0 += UNIT) {
+    if constexpr (NORM) {
+      const float2 r2 = make_float2(rstd, rstd);
 #pragma unroll
-    for (int i = 0; i < NCH; ++i)
-#pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (!(e & h)) {
-          const float a = v[i][e], b = v[i][e + h];
-          v[i][e] = a + b;
-          v[i][e + h] = a - b;
+      for (int i = c0; i < c0 + UNIT; ++i) {
+        if (i < NCH) {
+          const int c = i * 256 + lane * 8;
+          const float4 g0 = __ldg(reinterpret_cast<const float4*>(gamma + c));
+          const float4 g1 = __ldg(reinterpret_cast<const float4*>(gamma + c + 4));
+          const float4 b0 = __ldg(reinterpret_cast<const float4*>(beta + c));
+          const float4 b1 = __ldg(reinterpret_cast<const float4*>(beta + c + 4));
+          v[i][0] = fma2(v[i][0], mul2(r2, make_float2(g0.x, g0.y)), make_float2(b0.x, b0.y));
+          v[i][1] = fma2(v[i][1], mul2(r2, make_float2(g0.z, g0.w)), make_float2(b0.z, b0.w));
+          v[i][2] = fma2(v[i][2], mul2(r2, make_float2(g1.x, g1.y)), make_float2(b1.x, b1.y));
+          v[i][3] = fma2(v[i][3], mul2(r2, make_float2(g1.z, g1.w)), make_float2(b1.z, b1.w));
+          zero_ragged(i);
         }
-  // Column bits 3..min(7, log2(BLOCK)-1): across lanes.
-#pragma unroll
-  for (int m = 1; m < 32 && m * 8 < BLOCK; m <<= 1) {
-    const bool upper = lane & m;
-#pragma unroll
-    for (int i = 0; i < NCH; ++i)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float o = __shfl_xor_sync(0xffffffffu, v[i][e], m);
-        v[i][e] = upper ? o - v[i][e] : v[i][e] + o;
       }
-  }
-  // Column bits 8..log2(BLOCK)-1: across the lane's chunks.
+    }
+    // Column bit 0 (inside a register pair), bits 1-2 (across pairs), then chunk bits 8.. (across chunks).
 #pragma unroll
-  for (int h = 1; h * 256 < BLOCK; h <<= 1)
+    for (int i = c0; i < c0 + UNIT; ++i) {
 #pragma unroll
-    for (int i = 0; i < NCH; ++i)
-      if (!(i & h))
+      for (int k = 0; k < 4; ++k) v[i][k] = make_float2(v[i][k].x + v[i][k].y, v[i][k].x - v[i][k].y);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float a = v[i][e], b = v[i + h][e];
-          v[i][e] = a + b;
-          v[i + h][e] = a - b;
+      for (int h = 1; h < 4; h <<= 1)
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (!(k & h)) {
+            const float2 a = v[i][k], b = v[i][k + h];
+            v[i][k] = add2(a, b);
+            v[i][k + h] = sub2(a, b);
+          }
+    }
+#pragma unroll
+    for (int h = 1; h * 256 < BLOCK; h <<= 1)
+#pragma unroll
+      for (int i = c0; i < c0 + UNIT; ++i)
+        if (!((i - c0) & h))
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 a = v[i][k], b = v[i + h][k];
+            v[i][k] = add2(a, b);
+            v[i + h][k] = sub2(a, b);
+          }
+
+    // Transpose through shared memory: column c of the group sits at c + 8 * (c / QB).
+#pragma unroll
+    for (int i = c0; i < c0 + UNIT; ++i) {
+      const int c = (i - c0) * 256 + lane * 8;
+      float* d = sw + c + 8 * (c / QB);
+      *reinterpret_cast<float4*>(d) = make_float4(v[i][0].x, v[i][0].y, v[i][1].x, v[i][1].y);
+      *reinterpret_cast<float4*>(d + 4) = make_float4(v[i][2].x, v[i][2].y, v[i][3].x, v[i][3].y);
+    }
+    __syncwarp();
+    const int e = lane & 7, q = lane >> 3;
+    float* tp = sw + e + q * (QB + 8);  // transposed element t at tp[8 t]
+    float2 tv[G / 2];
+#pragma unroll
+    for (int j = 0; j < G / 2; ++j) tv[j] = make_float2(tp[16 * j], tp[16 * j + 8]);
+#pragma unroll
+    for (int j = 0; j < G / 2; ++j) tv[j] = make_float2(tv[j].x + tv[j].y, tv[j].x - tv[j].y);
+#pragma unroll
+    for (int h = 1; h < G / 2; h <<= 1)
+#pragma unroll
+      for (int j = 0; j < G / 2; ++j)
+        if (!(j & h)) {
+          const float2 a = tv[j], b = tv[j + h];
+          tv[j] = add2(a, b);
+          tv[j + h] = sub2(a, b);
         }
+#pragma unroll
+    for (int j = 0; j < G / 2; ++j) {
+      tp[16 * j] = tv[j].x;
+      tp[16 * j + 8] = tv[j].y;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = c0; i < c0 + UNIT; ++i) {
+      const int c = (i - c0) * 256 + lane * 8;
+      const float* d = sw + c + 8 * (c / QB);
+      const float4 a = *reinterpret_cast<const float4*>(d);
+      const float4 b = *reinterpret_cast<const float4*>(d + 4);
+      v[i][0] = make_float2(a.x, a.y);
+      v[i][1] = make_float2(a.z, a.w);
+      v[i][2] = make_float2(b.x, b.y);
+      v[i][3] = make_float2(b.z, b.w);
+    }
+    __syncwarp();
+  }
+
   constexpr float kNorm = BLOCK == 128   ? 0.08838834764831845f
                           : BLOCK == 256 ? 0.0625f
                           : BLOCK == 512 ? 0.04419417382415922f
                                          : 0.03125f;  // 1 / sqrt(BLOCK)
+  const float2 n2 = make_float2(kNorm, kNorm);
   float amax = 0.f;
 #pragma unroll
   for (int i = 0; i < NCH; ++i)
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      v[i][e] *= kNorm;
-      amax = fmaxf(amax, fabsf(v[i][e]));
+    for (int k = 0; k < 4; ++k) {
+      v[i][k] = mul2(v[i][k], n2);
+      amax = max3(amax, fabsf(v[i][k].x), fabsf(v[i][k].y));
     }
   amax = warp_max(amax);
   const float scale = fmaxf(amax, 1e-12f) / 127.f;
   const float inv = 1.f / scale;
+  const float2 inv2 = make_float2(inv, inv), magic2 = make_float2(12582912.f, 12582912.f);
   int8_t* orow = out + static_cast<size_t>(row) * COLS;
 #pragma unroll
   for (int i = 0; i < NCH; ++i) {
@@ -135,7 +215,11 @@ __global__ void __launch_bounds__(256) rot_q8_kernel(const __half* __restrict__ 
     // two's-complement int8 code. |v * inv| <= 127 by construction of the scale, so no clamp is needed.
     uint32_t t[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) t[e] = __float_as_uint(__fadd_rn(__fmul_rn(v[i][e], inv), 12582912.f));
+    for (int k = 0; k < 4; ++k) {
+      const float2 r = add2(mul2(v[i][k], inv2), magic2);
+      t[2 * k] = __float_as_uint(r.x);
+      t[2 * k + 1] = __float_as_uint(r.y);
+    }
     const uint32_t w0 = __byte_perm(__byte_perm(t[0], t[1], 0x0040), __byte_perm(t[2], t[3], 0x0040), 0x5410);
     const uint32_t w1 = __byte_perm(__byte_perm(t[4], t[5], 0x0040), __byte_perm(t[6], t[7], 0x0040), 0x5410);
     *reinterpret_cast<uint2*>(orow + i * 256 + lane * 8) = make_uint2(w0, w1);
@@ -148,11 +232,11 @@ namespace {
 template <int NCH, int BLOCK>
 int launch_rot(const __half* x, const float* g, const float* b, float eps, int rows, int valid, int8_t* out,
                float* rs, cudaStream_t s) {
-  const dim3 grid((rows + 7) / 8);
+  const dim3 grid((rows + kRotWarps - 1) / kRotWarps);
   if (g != nullptr)
-    rot_q8_kernel<NCH, BLOCK, true><<<grid, 256, 0, s>>>(x, g, b, eps, rows, valid, out, rs);
+    rot_q8_kernel<NCH, BLOCK, true><<<grid, kRotWarps * 32, 0, s>>>(x, g, b, eps, rows, valid, out, rs);
   else
-    rot_q8_kernel<NCH, BLOCK, false><<<grid, 256, 0, s>>>(x, g, b, eps, rows, valid, out, rs);
+    rot_q8_kernel<NCH, BLOCK, false><<<grid, kRotWarps * 32, 0, s>>>(x, g, b, eps, rows, valid, out, rs);
   return check_launch("rot_q8_kernel");
 }
 

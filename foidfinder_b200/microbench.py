@@ -2,6 +2,7 @@
 stream after warm-up. Also the entry point for ncu captures of single kernels.
 
     python -m foidfinder_b200.microbench gemm [--batch 64] [--shape 1024x3072] [--iters 20]
+                                              [--epilogue bias|swiglu|residual|qkv_rope]
     python -m foidfinder_b200.microbench attention [--batch 64] [--rope] [--iters 20]
     python -m foidfinder_b200.microbench rotate [--batch 64] [--iters 20]
 
@@ -51,9 +52,16 @@ def bench_gemm(batch: int, shapes: list[str], iters: int, epi: str) -> None:
         rs = torch.rand(M, generator=g, device=d) * 1e-2
         cs = torch.rand(N, generator=g, device=d) * 1e-3
         b = torch.randn(N, generator=g, device=d) * 0.02
-        e = {"bias": ops.EPI_BIAS, "swiglu": ops.EPI_SWIGLU, "residual": ops.EPI_RESIDUAL}[epi]
+        e = {"bias": ops.EPI_BIAS, "swiglu": ops.EPI_SWIGLU, "residual": ops.EPI_RESIDUAL,
+             "qkv_rope": ops.EPI_QKV_ROPE}[epi]
         out = torch.zeros(M, N // 2 if e == ops.EPI_SWIGLU else N, device=d, dtype=torch.float16)
-        ms = _time(lambda: ops.gemm_s8(A, W, rs, cs, b, out, e), iters)
+        rope = {}
+        if e == ops.EPI_QKV_ROPE:
+            from .weights import rope_tables
+
+            cos, sin = (t.t().contiguous().to(d) for t in rope_tables(32, 16))  # angle-major
+            rope = dict(rope_cos=cos, rope_sin=sin, rope_cols=2 * N // 3, tokens=TOKENS)
+        ms = _time(lambda: ops.gemm_s8(A, W, rs, cs, b, out, e, **rope), iters)
         n_alg = {"1024x5632": 5460, "2816x1024": 1024}.get(name, N)
         k_alg = 2730 if name == "2816x1024" else K
         ops_alg = 2 * M * n_alg * k_alg
@@ -98,7 +106,7 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--shape", action="append", choices=sorted(GEMM_SHAPES))
-    ap.add_argument("--epilogue", default="bias", choices=("bias", "swiglu", "residual"))
+    ap.add_argument("--epilogue", default="bias", choices=("bias", "swiglu", "residual", "qkv_rope"))
     ap.add_argument("--rope", action="store_true")
     a = ap.parse_args()
     if a.kernel == "gemm":

@@ -53,7 +53,8 @@ def gemm_s8(
     rope_cols: int = 0,
     tokens: int = 1,
 ) -> None:
-    """A [M, K] int8 x W [N, K] int8 -> epilogue into out (see include/foidfinder_b200.h)."""
+    """A [M, K] int8 x W [N, K] int8 -> epilogue into out (see include/foidfinder_b200.h). RoPE tables
+    for EPI_QKV_ROPE are angle-major [32, tokens]."""
     _cuda(A, W, row_scale, col_scale, bias, out, rope_cos, rope_sin)
     _need(A.dtype == torch.int8 and W.dtype == torch.int8, "gemm_s8: A and W must be int8")
     M, K = A.shape

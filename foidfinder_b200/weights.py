@@ -155,8 +155,8 @@ def convert(raw: dict[str, torch.Tensor], cfg: ModelConfig, device: str | torch.
     put("pos_bias", raw["patch_b"].float()[None, :] + pos[1:])
     put("cls_row", (raw["cls_token"].float() + pos[0]).half())
     cos, sin = rope_tables(cfg.grid, cfg.rope_ref_grid, cfg.head_dim)
-    put("rope_cos", cos)
-    put("rope_sin", sin)
+    put("rope_cos", cos.t())  # angle-major [32, tokens], the QKV epilogue's layout
+    put("rope_sin", sin.t())
     put("norm.weight", raw["norm.weight"].float())
     put("norm.bias", raw["norm.bias"].float())
     hw = torch.zeros(cfg.num_tags_pad, cfg.head_in, device=raw["head.weight"].device)

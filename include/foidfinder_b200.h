@@ -52,8 +52,8 @@ int ff_device_error(int device, int* code, int clear);
  * W8A8 GEMM on tcgen05: y[m, n] = int32(sum_k A[m, k] * W[n, k]) * row_scale[m] * col_scale[n] + bias[n],
  * then the epilogue `epi`.
  *   A [M, K] int8 (per-token codes), W [N, K] int8 (per-channel codes), K % 128 == 0, N % 128 == 0.
- *   rope_cos / rope_sin [tokens, 32] f32 are read only by FF_EPI_QKV_ROPE: row m uses position
- *   m % tokens, and pair (2i, 2i+1) of every 64-wide head uses angle column (i % 32).
+ *   rope_cos / rope_sin [32, tokens] f32 (angle-major) are read only by FF_EPI_QKV_ROPE: row m uses
+ *   position m % tokens, and pair (2i, 2i+1) of every 64-wide head uses angle row (i % 32).
  *   tile_n: 0 = automatic, else 128 or 256 output columns per CTA tile.
  * Replaces torch.ops.foidfinder.gemm_s8 (foidfinder/backends/cuda/csrc/kernels.cu:187-217, schema
  * kernels.cu:267-271); the reference's `stages` knob becomes `tile_n`, and its q_scale is folded into
@@ -191,7 +191,7 @@ typedef struct ff_model_weights {
   const uint16_t* patch_w;  /* [dim, k_pad] fp16, k_pad = ceil(p*p*3 / 64) * 64 */
   const float* pos_bias;    /* [patches, dim] f32 = patch bias + pos_embed[1:] */
   const uint16_t* cls_row;  /* [dim] fp16 = cls_token + pos_embed[0] */
-  const float *rope_cos, *rope_sin; /* [tokens, 32] */
+  const float *rope_cos, *rope_sin; /* [32, tokens], angle-major */
   const ff_layer_weights* layers;   /* [depth] */
   const float *norm_w, *norm_b;     /* final LayerNorm */
   const uint16_t* head_w;           /* [num_tags_pad, dim] (CLS) or [num_tags_pad, leaf_queries * leaf_dim] fp16 */

@@ -148,7 +148,7 @@ def forward_int8(
     x[:, 1:] = stem.half()
     x[:, 0] = conv["cls_row"]
     x = x.reshape(B * T, D)
-    cos, sin = conv["rope_cos"].float(), conv["rope_sin"].float()
+    cos, sin = conv["rope_cos"].float().t(), conv["rope_sin"].float().t()  # stored angle-major [32, tokens]
     x_stem = x
     for i in range(cfg.depth):
         p = f"blocks.{i}."

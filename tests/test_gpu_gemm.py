@@ -110,7 +110,7 @@ def test_gemm_s8_qkv_rope_epilogue(cuda_device, no_device_error):
     out = torch.full((M, N), float("nan"), dtype=torch.float16, device=d)
     ops.gemm_s8(
         A.to(d), W.to(d), rs.to(d), cs.to(d), b.to(d), out, ops.EPI_QKV_ROPE,
-        rope_cos=cos.to(d), rope_sin=sin.to(d), rope_cols=2 * dim, tokens=tokens,
+        rope_cos=cos.t().contiguous().to(d), rope_sin=sin.t().contiguous().to(d), rope_cols=2 * dim, tokens=tokens,
     )
     torch.cuda.synchronize()
     torch.testing.assert_close(out.float().cpu(), ref.half().float(), atol=2e-3, rtol=3e-3)
