@@ -133,10 +133,112 @@ constexpr unsigned kPolyChunks = FF_ATTN_POLY_CHUNKS;
 
 }  // namespace fa
 
+// Query rows past the last full 128-row tile, when there are at most kTailRows of them (EVA02: 1025 =
+// 8 x 128 + 1), go to one extra CTA per (image, head) that computes them on the CUDA cores in f32: a
+// tensor-core CTA for them would run a whole query tile (and all key tiles) for one row. Each
+// quarter-warp (8 lanes x 8 dims = one 128-byte key/value row, coalesced) walks its share of the keys
+// with its own online softmax (running max m, sum l, o over its 8 dims per lane), four keys in flight;
+// the 40 partial results are then merged through shared memory. Called by every thread of the CTA.
+namespace fa {
+constexpr int kTailRows = 4;
+
+__device__ __noinline__ void attention_tail_rows(const __half* __restrict__ qkv, __half* __restrict__ out, int T,
+                                                 int T_main, int heads, float scale_log2, int img, int h) {
+  constexpr int NQ = THREADS / 8;  // quarter-warps
+  constexpr int UNR = 4;           // keys in flight per quarter-warp
+  __shared__ float part_m[NQ], part_l[NQ];
+  __shared__ float part_o[NQ][HD];
+  const int dim = heads * HD, t = threadIdx.x, qw = t >> 3, ql = t & 7;
+  const size_t img_row0 = static_cast<size_t>(img) * T;
+  const unsigned qmask = 0xFFu << (t & 24);  // this quarter-warp's lanes
+  for (int r = T_main; r < T; ++r) {
+    // q: this lane's 8 dims, in log2 units.
+    float q[8];
+    {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(qkv + (img_row0 + r) * 3 * dim + h * HD) + ql);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = unpack_half2(w[e]);
+        q[2 * e] = f.x * scale_log2;
+        q[2 * e + 1] = f.y * scale_log2;
+      }
+    }
+    float m = -INFINITY, l = 0.f, o[8];
+#pragma unroll
+    for (int d = 0; d < 8; ++d) o[d] = 0.f;
+    for (int k0 = qw; k0 < T; k0 += NQ * UNR) {
+      uint4 kr[UNR], vr[UNR];
+#pragma unroll
+      for (int i = 0; i < UNR; ++i) {
+        const int key = k0 + i * NQ;
+        if (key < T) {
+          const __half* base = qkv + (img_row0 + key) * 3 * dim + h * HD;
+          kr[i] = __ldg(reinterpret_cast<const uint4*>(base + dim) + ql);
+          vr[i] = __ldg(reinterpret_cast<const uint4*>(base + 2 * dim) + ql);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < UNR; ++i) {
+        const int key = k0 + i * NQ;
+        if (key >= T) break;  // uniform within the quarter-warp
+        const uint32_t kw[4] = {kr[i].x, kr[i].y, kr[i].z, kr[i].w};
+        float sc = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = unpack_half2(kw[e]);
+          sc = fmaf(q[2 * e], f.x, fmaf(q[2 * e + 1], f.y, sc));
+        }
+        sc += __shfl_xor_sync(qmask, sc, 1, 8);
+        sc += __shfl_xor_sync(qmask, sc, 2, 8);
+        sc += __shfl_xor_sync(qmask, sc, 4, 8);
+        const float m_new = fmaxf(m, sc);
+        const float corr = ex2_approx(m - m_new);  // 0 while m is still -inf
+        const float p = ex2_approx(sc - m_new);
+        m = m_new;
+        l = l * corr + p;
+        const uint32_t vw[4] = {vr[i].x, vr[i].y, vr[i].z, vr[i].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = unpack_half2(vw[e]);
+          o[2 * e] = fmaf(p, f.x, o[2 * e] * corr);
+          o[2 * e + 1] = fmaf(p, f.y, o[2 * e + 1] * corr);
+        }
+      }
+    }
+    __syncthreads();  // the previous row's merge has read the partials
+    if (ql == 0) {
+      part_m[qw] = m;
+      part_l[qw] = l;
+    }
+#pragma unroll
+    for (int d = 0; d < 8; ++d) part_o[qw][8 * ql + d] = o[d];
+    __syncthreads();
+    if (t < HD) {
+      float mm = -INFINITY;
+#pragma unroll 8
+      for (int i = 0; i < NQ; ++i) mm = fmaxf(mm, part_m[i]);
+      float ll = 0.f, acc = 0.f;
+#pragma unroll 8
+      for (int i = 0; i < NQ; ++i) {
+        const float w = part_m[i] == -INFINITY ? 0.f : ex2_approx(part_m[i] - mm);
+        ll = fmaf(part_l[i], w, ll);
+        acc = fmaf(part_o[i][t], w, acc);
+      }
+      out[(img_row0 + r) * dim + h * HD + t] = __float2half_rn(acc / ll);
+    }
+  }
+}
+}  // namespace fa
+
 __global__ void __launch_bounds__(fa::THREADS, 1)
-    attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, __half* __restrict__ out, int T, int heads,
-                        float scale_log2, int* err) {
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __half* __restrict__ qkv,
+                        __half* __restrict__ out, int T, int T_main, int heads, float scale_log2, int* err) {
   using namespace fa;
+  if (T_main < T && blockIdx.x == gridDim.x - 1) {
+    attention_tail_rows(qkv, out, T, T_main, heads, scale_log2, blockIdx.z, blockIdx.y);
+    return;
+  }
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
@@ -155,8 +257,12 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
   const int h = blockIdx.y, img = blockIdx.z;
   const int dim = heads * HD;
   const int q0 = blockIdx.x * 2 * BQ;
-  const bool has1 = q0 + BQ < T;  // the second query tile holds at least one token
+  const bool has1 = q0 + BQ < T_main;  // the second query tile holds at least one token
   const int nkv = (T + BKV - 1) / BKV;
+  // The last key tile may be ragged: its S and P V products only cover the first kv_tail_n keys
+  // (a multiple of 16; keys past T inside them are masked in the softmax).
+  const int kv_tail = T - (nkv - 1) * BKV;
+  const int kv_tail_n = (kv_tail + 15) & ~15;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -227,20 +333,25 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t id_s = idesc_f16(128, BKV);
+      const uint32_t id_s_tail = idesc_f16(128, kv_tail_n);
       constexpr uint32_t id_o = idesc_f16(128, HD + 16) | (1u << 16);  // B = [V | ones] is MN-major, N = 80
       auto issue_s = [&](int i, int j) {
         const uint64_t qd = sdesc_k_sw128(smem_u32(smem + OFF_Q + i * TILE));
         const uint64_t kd = sdesc_k_sw128(smem_u32(smem + OFF_K + (j % STAGES) * TILE));
+        const uint32_t id = j == nkv - 1 ? id_s_tail : id_s;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) mma_f16(tmem + t_s(i), qd + 2 * k, kd + 2 * k, id_s, k > 0);
+        for (int k = 0; k < 4; ++k) mma_f16(tmem + t_s(i), qd + 2 * k, kd + 2 * k, id, k > 0);
         tc_commit(&s_full[i]);
       };
       auto issue_pv = [&](int i, int j) {
         const uint32_t sv = smem_u32(smem + OFF_V + (j % STAGES) * TILE);
+        const int steps = j == nkv - 1 ? kv_tail_n / 16 : 8;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {  // 16 keys per step: P columns 8k.., V rows 16k..
-          const uint32_t acc = (j > 0 || k > 0) ? 1u : 0u;
-          mma_f16_ts(tmem + t_o(i), tmem + t_s(i) + 8 * k, fa::sdesc_mn_sw128(sv + k * 2048), id_o, acc);
+          if (k < steps) {
+            const uint32_t acc = (j > 0 || k > 0) ? 1u : 0u;
+            mma_f16_ts(tmem + t_o(i), tmem + t_s(i) + 8 * k, fa::sdesc_mn_sw128(sv + k * 2048), id_o, acc);
+          }
         }
       };
       auto kv_wait = [&](int j) {
@@ -359,6 +470,7 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
         const float2 nm2 = make_float2(kPScaleLog2 - m_ref, kPScaleLog2 - m_ref);
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
+          if (!full_tile && 64 * hf >= valid) break;  // P past the ragged tile's keys is never read
           uint32_t raw[2][32];
           tmem_ld32(ts + 64 * hf, raw[0]);
           tmem_ld32(ts + 64 * hf + 32, raw[1]);
@@ -366,6 +478,7 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
 #pragma unroll
           for (int cc = 0; cc < 2; ++cc) {
             const int c = 2 * hf + cc;
+            if (!full_tile && 32 * c >= valid) break;
             uint32_t pk[16];
             if (full_tile) {
 #pragma unroll
@@ -402,7 +515,7 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
         fa::tmem_ld1(tmem + lane_base + t_l(g), l);
         tmem_ld_wait();
         const uint32_t* o = &o2[0][0];
-        if (row < T) {
+        if (row < T_main) {
           const float inv = 1.f / __uint_as_float(l);
           uint4* dst = reinterpret_cast<uint4*>(out + (static_cast<size_t>(img) * T + row) * dim + h * HD);
 #pragma unroll
@@ -440,9 +553,13 @@ int attention_tc(const void* qkv, void* out, int num_seqs, int seq_len, int head
       return check_launch("attention_tc: cudaFuncSetAttribute");
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  const dim3 grid((seq_len + 2 * BQ - 1) / (2 * BQ), heads, num_seqs);
-  attention_tc_kernel<<<grid, THREADS, SMEM, s>>>(map, static_cast<__half*>(out), seq_len, heads,
-                                                  scale * 1.4426950408889634f, err);
+  // Rows past the last full query tile go to one CUDA-core CTA per (image, head) when they are few.
+  const int rem = seq_len % BQ;
+  const int t_main = rem != 0 && rem <= kTailRows && seq_len > BQ ? seq_len - rem : seq_len;
+  const int tail_ctas = t_main < seq_len ? 1 : 0;
+  const dim3 grid((t_main + 2 * BQ - 1) / (2 * BQ) + tail_ctas, heads, num_seqs);
+  attention_tc_kernel<<<grid, THREADS, SMEM, s>>>(map, static_cast<const __half*>(qkv), static_cast<__half*>(out),
+                                                  seq_len, t_main, heads, scale * 1.4426950408889634f, err);
   return check_launch("attention_tc_kernel");
 }
 

@@ -145,13 +145,18 @@ __global__ void __launch_bounds__(kRotWarps * 32)
             v[i + h][k] = sub2(a, b);
           }
 
-    // Transpose through shared memory: column c of the group sits at c + 8 * (c / QB).
+    // Transpose through shared memory: column c of the group sits at c + 8 * (c / QB). Lanes with bit 2
+    // set move their two 16-byte halves in the opposite order, so each quarter-warp phase of a 16-byte
+    // access covers all 32 banks once.
+    const bool swap_halves = lane & 4;
 #pragma unroll
     for (int i = c0; i < c0 + UNIT; ++i) {
       const int c = (i - c0) * 256 + lane * 8;
       float* d = sw + c + 8 * (c / QB);
-      *reinterpret_cast<float4*>(d) = make_float4(v[i][0].x, v[i][0].y, v[i][1].x, v[i][1].y);
-      *reinterpret_cast<float4*>(d + 4) = make_float4(v[i][2].x, v[i][2].y, v[i][3].x, v[i][3].y);
+      const float4 lo = make_float4(v[i][0].x, v[i][0].y, v[i][1].x, v[i][1].y);
+      const float4 hi = make_float4(v[i][2].x, v[i][2].y, v[i][3].x, v[i][3].y);
+      *reinterpret_cast<float4*>(d + (swap_halves ? 4 : 0)) = swap_halves ? hi : lo;
+      *reinterpret_cast<float4*>(d + (swap_halves ? 0 : 4)) = swap_halves ? lo : hi;
     }
     __syncwarp();
     const int e = lane & 7, q = lane >> 3;
@@ -180,8 +185,10 @@ __global__ void __launch_bounds__(kRotWarps * 32)
     for (int i = c0; i < c0 + UNIT; ++i) {
       const int c = (i - c0) * 256 + lane * 8;
       const float* d = sw + c + 8 * (c / QB);
-      const float4 a = *reinterpret_cast<const float4*>(d);
-      const float4 b = *reinterpret_cast<const float4*>(d + 4);
+      const float4 first = *reinterpret_cast<const float4*>(d + (swap_halves ? 4 : 0));
+      const float4 second = *reinterpret_cast<const float4*>(d + (swap_halves ? 0 : 4));
+      const float4 a = swap_halves ? second : first;
+      const float4 b = swap_halves ? first : second;
       v[i][0] = make_float2(a.x, a.y);
       v[i][1] = make_float2(a.z, a.w);
       v[i][2] = make_float2(b.x, b.y);

@@ -100,7 +100,11 @@ def _ref_attention(qkv, seqs, T, heads, scale, rope=None):
 
 
 @pytest.mark.parametrize(("seqs", "T", "heads", "rope"), [(1, 1025, 16, False), (2, 1025, 16, True), (3, 65, 12, False),
-                                                          (1, 1, 16, False), (2, 577, 16, True), (1, 128, 4, False)])
+                                                          (1, 1, 16, False), (2, 577, 16, True), (1, 128, 4, False),
+                                                          # tensor-core path: masked ragged query tile (577),
+                                                          # CUDA-core tail rows (259: 3 rows; 1540: 4 rows and
+                                                          # more keys than one pass of the tail CTA)
+                                                          (2, 577, 16, False), (2, 259, 8, False), (1, 1540, 4, False)])
 def test_attention_matches_oracle(cuda_device, no_device_error, seqs, T, heads, rope):
     from foidfinder_b200 import ops
 
