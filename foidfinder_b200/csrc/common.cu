@@ -80,19 +80,26 @@ static int load_encode() {
 
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elt_bytes, uint64_t inner,
                  uint64_t outer, uint32_t box_inner, uint32_t box_outer) {
+  return make_tmap_2d_pitched(map, base, dtype, elt_bytes, inner, outer, inner * static_cast<uint64_t>(elt_bytes),
+                              box_inner, box_outer, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int make_tmap_2d_pitched(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elt_bytes, uint64_t inner,
+                         uint64_t outer, uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer,
+                         CUtensorMapSwizzle swizzle) {
   const int lrc = load_encode();
   if (lrc != FF_OK) return lrc;
-  if (!aligned16(base) || (inner * elt_bytes) % 16 != 0) {
+  if (!aligned16(base) || pitch_bytes % 16 != 0 || pitch_bytes < inner * elt_bytes) {
     set_error("TMA operand must be 16-byte aligned with a 16-byte multiple row pitch");
     return FF_ERR_INVALID_ARGUMENT;
   }
   cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {inner * static_cast<uint64_t>(elt_bytes)};
+  cuuint64_t strides[1] = {pitch_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   const CUresult r = g_encode(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
-                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed (%d) for [%llu, %llu] box [%u, %u]", static_cast<int>(r),
               static_cast<unsigned long long>(outer), static_cast<unsigned long long>(inner), box_outer, box_inner);

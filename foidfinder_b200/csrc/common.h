@@ -24,6 +24,10 @@ int* device_error_word();
 // 2-D tensor map over a row-major [outer, inner] matrix, 128-byte swizzle, box {box_inner, box_outer}.
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elt_bytes, uint64_t inner,
                  uint64_t outer, uint32_t box_inner, uint32_t box_outer);
+// Same with an explicit row pitch (bytes) and swizzle mode.
+int make_tmap_2d_pitched(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elt_bytes, uint64_t inner,
+                         uint64_t outer, uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer,
+                         CUtensorMapSwizzle swizzle);
 
 // 3-D tensor map over a row-major [d2, d1, d0] array (d0 innermost), 128-byte swizzle.
 int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elt_bytes, uint64_t d0, uint64_t d1,

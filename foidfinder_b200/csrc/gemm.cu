@@ -8,7 +8,8 @@ namespace ff {
 namespace {
 
 template <int BN, int STAGES, bool F16IN, int EPI>
-int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, cudaStream_t stream) {
+int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& a,
+               cudaStream_t stream) {
   using C = GemmCfg<BN, STAGES>;
   auto kernel = gemm_tc_kernel<BN, STAGES, F16IN, EPI>;
   static bool configured[64] = {};  // per instantiation and device
@@ -21,26 +22,27 @@ int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, 
   }
   const int tiles = a.tiles_m * (a.N / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kernel<<<grid, C::THREADS, C::SMEM, stream>>>(ta, tb, a);
+  kernel<<<grid, C::THREADS, C::SMEM, stream>>>(ta, tb, tc, a);
   return check_launch("gemm_tc_kernel");
 }
 
 template <int BN, bool F16IN>
-int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, cudaStream_t s) {
+int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& a,
+                 cudaStream_t s) {
   constexpr int STAGES = BN == 256 ? 4 : 6;
   if constexpr (F16IN) {
     switch (epi) {
-      case EPI_STEM: return launch_one<BN, STAGES, true, EPI_STEM>(ta, tb, a, s);
-      case EPI_LOGITS: return launch_one<BN, STAGES, true, EPI_LOGITS>(ta, tb, a, s);
-      case EPI_BIAS: return launch_one<BN, STAGES, true, EPI_BIAS>(ta, tb, a, s);
+      case EPI_STEM: return launch_one<BN, STAGES, true, EPI_STEM>(ta, tb, tc, a, s);
+      case EPI_LOGITS: return launch_one<BN, STAGES, true, EPI_LOGITS>(ta, tb, tc, a, s);
+      case EPI_BIAS: return launch_one<BN, STAGES, true, EPI_BIAS>(ta, tb, tc, a, s);
     }
   } else {
     switch (epi) {
-      case EPI_QKV_ROPE: return launch_one<BN, STAGES, false, EPI_QKV_ROPE>(ta, tb, a, s);
-      case EPI_RESIDUAL: return launch_one<BN, STAGES, false, EPI_RESIDUAL>(ta, tb, a, s);
-      case EPI_SWIGLU: return launch_one<BN, STAGES, false, EPI_SWIGLU>(ta, tb, a, s);
-      case EPI_BIAS: return launch_one<BN, STAGES, false, EPI_BIAS>(ta, tb, a, s);
-      case EPI_S32: return launch_one<BN, STAGES, false, EPI_S32>(ta, tb, a, s);
+      case EPI_QKV_ROPE: return launch_one<BN, STAGES, false, EPI_QKV_ROPE>(ta, tb, tc, a, s);
+      case EPI_RESIDUAL: return launch_one<BN, STAGES, false, EPI_RESIDUAL>(ta, tb, tc, a, s);
+      case EPI_SWIGLU: return launch_one<BN, STAGES, false, EPI_SWIGLU>(ta, tb, tc, a, s);
+      case EPI_BIAS: return launch_one<BN, STAGES, false, EPI_BIAS>(ta, tb, tc, a, s);
+      case EPI_S32: return launch_one<BN, STAGES, false, EPI_S32>(ta, tb, tc, a, s);
     }
   }
   set_error("gemm: epilogue %d is not available for %s inputs", epi, F16IN ? "fp16" : "int8");
@@ -73,6 +75,21 @@ int gemm_prepare(const GemmProblem& p, GemmPlan* plan) {
   rc = make_tmap_2d(&plan->tb, p.W, dt, elt, static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.N), box_k,
                     static_cast<uint32_t>(bn));
   if (rc != FF_OK) return rc;
+  // Output map for the TMA-store epilogues: fp16 [M, out_cols] with row pitch ldo, boxes of 32 rows x
+  // 64 columns (128-byte swizzle) or, for the 128-wide SwiGLU tile, 32 columns (64-byte swizzle) — the
+  // layouts the epilogue's staging buffer is written in.
+  plan->tc = plan->ta;
+  if (p.epi == EPI_BIAS || p.epi == EPI_QKV_ROPE || p.epi == EPI_SWIGLU) {
+    const int out_cols = p.epi == EPI_SWIGLU ? p.N / 2 : p.N;
+    const int ldo = p.args.ldo;
+    FF_REQUIRE(ldo >= out_cols && ldo % 8 == 0, "gemm: output row stride %d for %d columns", ldo, out_cols);
+    FF_REQUIRE(aligned16(p.out), "gemm: out must be 16-byte aligned");
+    const bool narrow = p.epi == EPI_SWIGLU && bn == 128;
+    rc = make_tmap_2d_pitched(&plan->tc, p.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, static_cast<uint64_t>(out_cols),
+                              static_cast<uint64_t>(p.M), static_cast<uint64_t>(ldo) * 2, narrow ? 32 : 64, 32,
+                              narrow ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != FF_OK) return rc;
+  }
   plan->args = p.args;
   plan->args.M = p.M;
   plan->args.N = p.N;
@@ -90,10 +107,10 @@ int gemm_prepare(const GemmProblem& p, GemmPlan* plan) {
 
 int gemm_launch(const GemmPlan& plan, cudaStream_t stream) {
   if (plan.f16)
-    return plan.bn == 256 ? dispatch_epi<256, true>(plan.epi, plan.ta, plan.tb, plan.args, stream)
-                          : dispatch_epi<128, true>(plan.epi, plan.ta, plan.tb, plan.args, stream);
-  return plan.bn == 256 ? dispatch_epi<256, false>(plan.epi, plan.ta, plan.tb, plan.args, stream)
-                        : dispatch_epi<128, false>(plan.epi, plan.ta, plan.tb, plan.args, stream);
+    return plan.bn == 256 ? dispatch_epi<256, true>(plan.epi, plan.ta, plan.tb, plan.tc, plan.args, stream)
+                          : dispatch_epi<128, true>(plan.epi, plan.ta, plan.tb, plan.tc, plan.args, stream);
+  return plan.bn == 256 ? dispatch_epi<256, false>(plan.epi, plan.ta, plan.tb, plan.tc, plan.args, stream)
+                        : dispatch_epi<128, false>(plan.epi, plan.ta, plan.tb, plan.tc, plan.args, stream);
 }
 
 }  // namespace ff

@@ -21,7 +21,7 @@ struct GemmProblem {
 };
 
 struct GemmPlan {
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tc;  // tc: fp16 output, for the epilogues that store through TMA
   GemmArgs args;
   int bn;
   bool f16;

@@ -102,7 +102,9 @@ __device__ __forceinline__ void dequant32(const uint32_t (&r)[32], float rs, con
 template <int BN, int STAGES, bool F16IN, int EPI>
 __global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const GemmArgs args) {
+                   const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
+  // fp16 outputs of these epilogues leave through TMA stores of the swizzled staging buffer (tmC).
+  constexpr bool kTmaStore = EPI == EPI_BIAS || EPI == EPI_QKV_ROPE || EPI == EPI_SWIGLU;
   using C = GemmCfg<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -285,27 +287,18 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
             packed[sub * 16 + j / 2] = pack_half2(silu_mul(g[j], u[j]), silu_mul(g[j + 1], u[j + 1]));
         }
         const int col0 = (n_tile >> 1) + (BN == 256 ? half * 64 : half * 32);
+        // The staging buffer is free once this warp's previous TMA store has read it.
+        if (lane == 0) bulk_wait_read_all();
         __syncwarp();
-        if constexpr (OUTS == 64) {
+        if constexpr (OUTS == 64)
           stage_row128(stg, lane, packed);
-          __syncwarp();
-#pragma unroll
-          for (int it = 0; it < 8; ++it) {
-            const int r = it * 4 + (lane >> 3), c = lane & 7;
-            const uint4 v = staged_chunk128(stg, r, c);
-            if (m_block + r < args.M)
-              *reinterpret_cast<uint4*>(out16 + static_cast<size_t>(m_block + r) * args.ldo + col0 + c * 8) = v;
-          }
-        } else {
+        else
           stage_row64(stg, lane, packed);
-          __syncwarp();
-#pragma unroll
-          for (int it = 0; it < 4; ++it) {
-            const int r = it * 8 + (lane >> 2), c = lane & 3;
-            const uint4 v = staged_chunk64(stg, r, c);
-            if (m_block + r < args.M)
-              *reinterpret_cast<uint4*>(out16 + static_cast<size_t>(m_block + r) * args.ldo + col0 + c * 8) = v;
-          }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, stg, col0, m_block);
+          bulk_commit_group();
         }
       } else if constexpr (EPI == EPI_BIAS || EPI == EPI_QKV_ROPE) {
         // 64 fp16 output columns per chunk; the warp owns HALF columns.
@@ -357,15 +350,14 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
 #pragma unroll
             for (int j = 0; j < 32; j += 2) packed[sub * 16 + j / 2] = pack_half2(y[j], y[j + 1]);
           }
+          if (lane == 0) bulk_wait_read_all();
           __syncwarp();
           stage_row128(stg, lane, packed);
+          fence_async_smem();
           __syncwarp();
-#pragma unroll
-          for (int it = 0; it < 8; ++it) {
-            const int r = it * 4 + (lane >> 3), c = lane & 7;
-            const uint4 v = staged_chunk128(stg, r, c);
-            if (m_block + r < args.M)
-              *reinterpret_cast<uint4*>(out16 + static_cast<size_t>(m_block + r) * args.ldo + n0 + c * 8) = v;
+          if (lane == 0) {
+            tma_store_2d(&tmC, stg, n0, m_block);
+            bulk_commit_group();
           }
         }
       } else if constexpr (EPI == EPI_RESIDUAL) {
@@ -463,6 +455,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
     }
   }
 
+  if constexpr (kTmaStore)
+    if (warp >= 2 && lane == 0) bulk_wait_all();  // this warp's output stores are complete
   __syncwarp();
   tc_fence_before();
   __syncthreads();
