@@ -194,14 +194,15 @@ def run_reference(args) -> None:
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic: seeded uint8 images U[0,255], random-init N(0,0.02) weights",
-        "config": workload(cfg, 1, 1),
+        "config": workload(cfg, args.batch, world),
         "cpu_baseline": {
             "value": value,
             "unit": UNIT,
             "cores": cores,
             "kind": "port",
-            "sample": f"{args.steps} steps of 1 image each: fp32 PyTorch CPU forward (oracle restatement of the "
-            "reference's PixAITorch forward with the EVA02 block), median step",
+            "sample": f"{args.steps} steps of 1 image each (a bounded sample of the {args.batch}-image step): fp32 "
+            "PyTorch CPU forward (oracle restatement of the reference's PixAITorch forward with the EVA02 block), "
+            "median step, on rank 0 only",
         },
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
