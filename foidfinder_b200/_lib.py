@@ -60,6 +60,7 @@ class ModelConfig(C.Structure):
 
 
 HEAD_CLS, HEAD_TREE = 0, 1
+RESAMPLE_BILINEAR, RESAMPLE_BICUBIC = 0, 1
 POOL_FIELDS = (
     "pool_norm_w", "pool_norm_b", "pool_kv_w", "pool_kv_b", "q_coarse", "q_coarse_bias", "q_child", "q_child_bias",
     "trunk_norm_w", "trunk_norm_b", "child_q_norm_w", "child_q_norm_b", "leaf_norm_w", "leaf_norm_b", "leaf_w", "leaf_b",
@@ -107,6 +108,8 @@ _SIGNATURES = {
     "ff_layernorm": (i32, [vp, i64, vp, vp, f32, i32, i32, vp, vp]),
     "ff_topk": (i32, [vp, i32, i32, i32, vp, vp, vp]),
     "ff_tree_pool": (i32, [C.POINTER(ModelConfig), C.POINTER(ModelWeights), vp, i32, vp, i64, vp, vp]),
+    "ff_resize_pad": (i32, [vp, i32, i32, i32, i32, i32, i32, i32, vp, vp, i64, vp]),
+    "ff_resize_pad_workspace_bytes": (i64, [i32, i32, i32, i32, i32]),
     "ff_tree_pool_workspace_bytes": (i64, [C.POINTER(ModelConfig), i32]),
     "ff_engine_create": (i32, [C.POINTER(ModelConfig), C.POINTER(ModelWeights), i32, C.POINTER(vp)]),
     "ff_engine_forward": (i32, [vp, vp, i32, vp, vp, vp, vp]),

@@ -39,6 +39,8 @@ class ModelConfig:
     rot_block_dim: int = 1024  # Hadamard block of the dim-wide GEMM inputs (qkv, proj, fc1)
     rot_block_hidden: int = 128  # Hadamard block of the hidden-wide GEMM input (fc2)
     topk: int = 50
+    resample: str = "bilinear"  # letterbox filter: PixAI's antialiased bilinear on black
+    pad: int = 0  # letterbox canvas value
     head: str = "cls"  # "cls": class-token linear head; "tree": the Haruka tree attention pool
     pool_heads: int = 16
     coarse_queries: int = 6
@@ -106,6 +108,8 @@ EVA02_B = ModelConfig(
     mean=IMAGENET_MEAN,
     std=IMAGENET_STD,
     rot_block_dim=256,
+    resample="bicubic",  # the model card's preprocessing: bicubic, composited and padded on white
+    pad=255,
     head="tree",
 )
 

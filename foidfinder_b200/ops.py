@@ -16,7 +16,7 @@ from ._lib import EPI_BIAS, EPI_LOGITS, EPI_QKV_ROPE, EPI_RESIDUAL, EPI_S32, EPI
 __all__ = [
     "EPI_QKV_ROPE", "EPI_RESIDUAL", "EPI_SWIGLU", "EPI_BIAS", "EPI_S32", "EPI_STEM", "EPI_LOGITS",
     "gemm_s8", "gemm_f16", "rot_q8", "rot_q8_1024", "rot_q8_h128", "attention", "patchify", "fill_cls",
-    "layernorm", "topk", "tree_pool",
+    "layernorm", "topk", "tree_pool", "resize_pad",
 ]
 
 
@@ -226,3 +226,21 @@ def tree_pool(cfg, weights: dict[str, torch.Tensor], x: torch.Tensor, leaf_out: 
         check(lib().ff_tree_pool(C.byref(c), C.byref(mw), _ptr(x), B, _ptr(ws), nbytes, _ptr(leaf_out), _stream(x)),
               "tree_pool")
         torch.cuda.current_stream(x.device).synchronize()  # keeps the workspace alive until the pool has run
+
+
+def resize_pad(image: torch.Tensor, new_h: int, new_w: int, size: int, out: torch.Tensor, *, bicubic: bool = True,
+               fill: int = 255) -> None:
+    """uint8 [h, w, 3] CUDA image -> out uint8 [size, size, 3]: Pillow-exact resize (bicubic or bilinear) to
+    (new_h, new_w), centred on a `fill` canvas."""
+    _cuda(image, out)
+    _need(image.dtype == torch.uint8 and image.dim() == 3 and image.shape[2] == 3, "resize_pad: uint8 [h, w, 3]")
+    _need(out.dtype == torch.uint8 and tuple(out.shape) == (size, size, 3), "resize_pad: out must be [size, size, 3]")
+    h, w = image.shape[:2]
+    flt = _lib.RESAMPLE_BICUBIC if bicubic else _lib.RESAMPLE_BILINEAR
+    nbytes = int(lib().ff_resize_pad_workspace_bytes(h, w, new_h, new_w, flt))
+    _need(nbytes > 0, "resize_pad: bad geometry")
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=image.device)
+    with torch.cuda.device(image.device):
+        check(lib().ff_resize_pad(_ptr(image), h, w, new_h, new_w, size, flt, fill, _ptr(out), _ptr(ws), nbytes,
+                                  _stream(image)), "resize_pad")
+        torch.cuda.current_stream(image.device).synchronize()  # the workspace is freed on return

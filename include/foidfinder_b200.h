@@ -221,6 +221,22 @@ int ff_tree_pool(const ff_model_config* cfg, const struct ff_model_weights* w, c
                  void* workspace, int64_t workspace_bytes, uint16_t* leaf_out, void* stream);
 int64_t ff_tree_pool_workspace_bytes(const ff_model_config* cfg, int B);
 
+/* ---------------------------------------------------------------- preprocessing */
+#define FF_RESAMPLE_BILINEAR 0
+#define FF_RESAMPLE_BICUBIC 1 /* a = -0.5 */
+/*
+ * Letterbox on the GPU: src [h, w, 3] uint8 RGB -> dst [size, size, 3] uint8, the image resized to
+ * (new_h, new_w) with Pillow's 8-bit separable resampling (filter FF_RESAMPLE_*, antialiased when
+ * reducing) and centred at ((size - new_h) / 2, (size - new_w) / 2) on a canvas of value `fill`.
+ * Bit-exact with PIL.Image.resize(filter) pasted on Image.new("RGB", (size, size), fill). The image step
+ * before the engine: foidfinder/backends/cuda/preprocess.py:16-32 (PixAI, on black) and
+ * foidfinder/backends/mlx/kernels.py:75-186 (Haruka, bicubic on white). workspace: device memory of at
+ * least ff_resize_pad_workspace_bytes(...) bytes, 256-byte aligned (intermediate image + coefficients).
+ */
+int ff_resize_pad(const uint8_t* src, int h, int w, int new_h, int new_w, int size, int filter, int fill, uint8_t* dst,
+                  void* workspace, int64_t workspace_bytes, void* stream);
+int64_t ff_resize_pad_workspace_bytes(int h, int w, int new_h, int new_w, int filter);
+
 typedef struct ff_engine ff_engine;
 
 /* Validates the config, keeps the weight pointers (the caller keeps them alive) and binds to `device`. */
