@@ -73,14 +73,6 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
       : "memory");
 }
 
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-      : "memory");
-}
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -98,7 +90,6 @@ __device__ __forceinline__ void tmem_ld1(uint32_t taddr, uint32_t& r) {
 __device__ __forceinline__ void tmem_st1(uint32_t taddr, uint32_t r) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(r) : "memory");
 }
-__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // (2^x.x, 2^x.y) as fp16x2 through MUFU ex2 and the f32->f16x2 conversion (both on the XU pipe);
 // exact zeros for x = -inf.
@@ -497,12 +488,12 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
                 pk[e] = fa::exp2_mufu(x);  // exact zeros for masked keys
               }
             }
-            fa::tmem_st16(ts + 16 * c, pk);
+            tmem_st16(ts + 16 * c, pk);
           }
         }
         __syncwarp();
         if (has1 && lane == 0) mbar_arrive(&order[g ^ 1]);
-        fa::tmem_st_wait();
+        tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[g]);

@@ -75,11 +75,12 @@ int gemm_prepare(const GemmProblem& p, GemmPlan* plan) {
   rc = make_tmap_2d(&plan->tb, p.W, dt, elt, static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.N), box_k,
                     static_cast<uint32_t>(bn));
   if (rc != FF_OK) return rc;
-  // Output map for the TMA-store epilogues: fp16 [M, out_cols] with row pitch ldo, boxes of 32 rows x
+  // Output map for the TMA-store (and, for the residual, TMA add-reduce) epilogues: fp16 [M, out_cols] with
+  // row pitch ldo, boxes of 32 rows x
   // 64 columns (128-byte swizzle) or, for the 128-wide SwiGLU tile, 32 columns (64-byte swizzle) — the
   // layouts the epilogue's staging buffer is written in.
   plan->tc = plan->ta;
-  if (p.epi == EPI_BIAS || p.epi == EPI_QKV_ROPE || p.epi == EPI_SWIGLU) {
+  if (p.epi == EPI_BIAS || p.epi == EPI_QKV_ROPE || p.epi == EPI_SWIGLU || p.epi == EPI_RESIDUAL) {
     const int out_cols = p.epi == EPI_SWIGLU ? p.N / 2 : p.N;
     const int ldo = p.args.ldo;
     FF_REQUIRE(ldo >= out_cols && ldo % 8 == 0, "gemm: output row stride %d for %d columns", ldo, out_cols);

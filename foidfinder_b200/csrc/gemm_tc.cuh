@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
   // fp16 outputs of these epilogues leave through TMA stores of the swizzled staging buffer (tmC).
-  constexpr bool kTmaStore = EPI == EPI_BIAS || EPI == EPI_QKV_ROPE || EPI == EPI_SWIGLU;
+  constexpr bool kTmaStore = EPI == EPI_BIAS || EPI == EPI_QKV_ROPE || EPI == EPI_SWIGLU || EPI == EPI_RESIDUAL;
   using C = GemmCfg<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -300,8 +300,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
           tma_store_2d(&tmC, stg, col0, m_block);
           bulk_commit_group();
         }
-      } else if constexpr (EPI == EPI_BIAS || EPI == EPI_QKV_ROPE) {
-        // 64 fp16 output columns per chunk; the warp owns HALF columns.
+      } else if constexpr (EPI == EPI_BIAS || EPI == EPI_QKV_ROPE || EPI == EPI_RESIDUAL) {
+        // 64 fp16 output columns per chunk; the warp owns HALF columns. The residual epilogue adds the
+        // fp16-rounded y to the fp16 stream with a TMA add-reduction (x = fp16(x + fp16(y)), the reference's
+        // __hadd2 of the staged fp16 result, foidfinder/backends/cuda/csrc/gemm.cuh:163-169).
 #pragma unroll 1
         for (int ch = 0; ch < HALF / 64; ++ch) {
           const int c0 = half * HALF + ch * 64;  // tile column of this chunk
@@ -356,49 +358,11 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
           fence_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmC, stg, n0, m_block);
+            if constexpr (EPI == EPI_RESIDUAL)
+              tma_reduce_add_2d(&tmC, stg, n0, m_block);
+            else
+              tma_store_2d(&tmC, stg, n0, m_block);
             bulk_commit_group();
-          }
-        }
-      } else if constexpr (EPI == EPI_RESIDUAL) {
-        // fp16 residual stream: x = fp16(float(x) + y). y is staged in f32 (32 columns = 128 B per row)
-        // so the sum is rounded once; the old x is read in the coalesced phase.
-#pragma unroll 1
-        for (int ch = 0; ch < HALF / 32; ++ch) {
-          const int c0 = half * HALF + ch * 32;
-          const int n0 = n_tile + c0;
-          uint32_t r[32];
-          __syncwarp();
-          tmem_ld32(tbase + c0, r);
-          tmem_ld_wait();
-          float y[32];
-          dequant32(r, rs, args.col_scale + n0, args.bias + n0, y);
-          uint32_t yw[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) yw[j] = __float_as_uint(y[j]);
-          __syncwarp();
-          stage_row128(stg, lane, yw);
-          __syncwarp();
-          // All eight reads of the old stream first (independent, in flight together), then the stores.
-          const int c = lane & 7;
-          uint2 old[8];
-#pragma unroll
-          for (int it = 0; it < 8; ++it) {
-            const int rr = it * 4 + (lane >> 3);
-            old[it] = m_block + rr < args.M
-                          ? *reinterpret_cast<const uint2*>(out16 + static_cast<size_t>(m_block + rr) * args.ldo + n0 + c * 4)
-                          : make_uint2(0u, 0u);
-          }
-#pragma unroll
-          for (int it = 0; it < 8; ++it) {
-            const int rr = it * 4 + (lane >> 3);
-            const uint4 v = staged_chunk128(stg, rr, c);
-            if (m_block + rr < args.M) {
-              const float2 o0 = unpack_half2(old[it].x), o1 = unpack_half2(old[it].y);
-              *reinterpret_cast<uint2*>(out16 + static_cast<size_t>(m_block + rr) * args.ldo + n0 + c * 4) =
-                  make_uint2(pack_half2(o0.x + __uint_as_float(v.x), o0.y + __uint_as_float(v.y)),
-                             pack_half2(o1.x + __uint_as_float(v.z), o1.y + __uint_as_float(v.w)));
-            }
           }
         }
       } else {

@@ -5,8 +5,9 @@
 
 namespace ff {
 
+// err: device error word for bounded waits (nullptr: the library's per-device word).
 int rot_q8(const void* x, const float* g, const float* b, float eps, int rows, int cols, int valid, int block,
-           int8_t* out, float* rs, cudaStream_t s);
+           int8_t* out, float* rs, cudaStream_t s, int* err = nullptr);
 int attention(const void* qkv, void* out, int num_seqs, int seq_len, int heads, const float* rope_cos,
               const float* rope_sin, float scale, cudaStream_t s);
 int attention_tc(const void* qkv, void* out, int num_seqs, int seq_len, int heads, float scale, cudaStream_t s);

@@ -85,7 +85,7 @@ extern "C" int ff_linear_w8a8_noalloc(const uint16_t* x, const float* gamma, con
   float* row_scale = reinterpret_cast<float*>(scratch + kScaleOffset);
   int* err_word = err != nullptr ? err : reinterpret_cast<int*>(scratch + kErrOffset);
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  rc = rot_q8(x, gamma, beta, eps, rows, cols, valid_cols, block, codes, row_scale, s);
+  rc = rot_q8(x, gamma, beta, eps, rows, cols, valid_cols, block, codes, row_scale, s, err_word);
   if (rc != FF_OK) return rc;
   GemmProblem p{};
   p.A = codes;

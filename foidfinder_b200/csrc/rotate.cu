@@ -20,39 +20,44 @@
 //
 // The LayerNorm runs over the first valid_cols columns: columns past it are zeroed at load, their
 // (0 - mean)^2 terms are taken back out of the variance, and they are zeroed again after the affine step.
+#include <algorithm>
+
 #include "common.h"
+#include "kernels.h"
 #include "ptx.cuh"
 
 namespace ff {
 
-constexpr int kRotWarps = 4;  // small CTAs: the 2816-column rows need ~134 registers per thread
+constexpr int kRotWarps = 4;  // per-row grid: small CTAs (the 2816-column rows need ~134 registers per thread)
 
-template <int NCH, int BLOCK, bool NORM>
-__global__ void __launch_bounds__(kRotWarps * 32)
-    rot_q8_kernel(const __half* __restrict__ x, const float* __restrict__ gamma, const float* __restrict__ beta,
-                  float eps, int rows, int valid_cols, int8_t* __restrict__ out, float* __restrict__ row_scale) {
-  constexpr int LB = BLOCK == 128 ? 7 : BLOCK == 256 ? 8 : BLOCK == 512 ? 9 : 10;
-  constexpr int TB = LB - 3 < 5 ? LB - 3 : 5;  // column bits 3..3+TB-1 run in the transposed layout
-  constexpr int G = 1 << TB;                   // values per lane in the transposed layout
-  constexpr int UNIT = G / 8;                  // 256-column chunks per transpose
-  constexpr int NCHP = (NCH + UNIT - 1) / UNIT * UNIT;
-  constexpr int COLS = NCH * 256;
-  constexpr int QB = 8 * G;  // columns per transposed lane group (padding period)
-  constexpr int SW = UNIT * 256 + 8 * (UNIT * 256 / QB);
+template <int NCH, int BLOCK>
+struct RotShape {
+  static constexpr int LB = BLOCK == 128 ? 7 : BLOCK == 256 ? 8 : BLOCK == 512 ? 9 : 10;
+  static constexpr int TB = LB - 3 < 5 ? LB - 3 : 5;  // column bits 3..3+TB-1 run in the transposed layout
+  static constexpr int G = 1 << TB;                   // values per lane in the transposed layout
+  static constexpr int UNIT = G / 8;                  // 256-column chunks per transpose
+  static constexpr int NCHP = (NCH + UNIT - 1) / UNIT * UNIT;
+  static constexpr int COLS = NCH * 256;
+  static constexpr int QB = 8 * G;  // columns per transposed lane group (padding period)
+  static constexpr int SW = UNIT * 256 + 8 * (UNIT * 256 / QB);  // floats of one warp's transpose buffer
   static_assert((1 << LB) == BLOCK && BLOCK / 256 <= UNIT, "unsupported Hadamard block");
-  __shared__ __align__(16) float smem[kRotWarps][SW];
+};
 
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int row = blockIdx.x * kRotWarps + wid;
-  if (row >= rows) return;
-  float* sw = smem[wid];
-  const __half* xr = x + static_cast<size_t>(row) * COLS;
+// One row by one warp; xr is the row's fp16 input (global memory, or shared memory when SRC_SMEM).
+// gb(i, g, b) supplies this lane's 8 gamma and 8 beta values of chunk i.
+template <int NCH, int BLOCK, bool NORM, bool SRC_SMEM, class GammaBeta>
+__device__ __forceinline__ void rot_row(const __half* __restrict__ xr, float eps, int row, int valid_cols,
+                                        int8_t* __restrict__ out, float* __restrict__ row_scale, float* sw, int lane,
+                                        GammaBeta gb) {
+  using S = RotShape<NCH, BLOCK>;
+  constexpr int G = S::G, UNIT = S::UNIT, NCHP = S::NCHP, COLS = S::COLS, QB = S::QB;
 
   float2 v[NCHP][4];
 #pragma unroll
   for (int i = 0; i < NCHP; ++i) {
     if (i < NCH) {
-      const uint4 u = __ldg(reinterpret_cast<const uint4*>(xr + i * 256 + lane * 8));
+      const uint4* src = reinterpret_cast<const uint4*>(xr + i * 256 + lane * 8);
+      const uint4 u = SRC_SMEM ? *src : __ldg(src);
       v[i][0] = unpack_half2(u.x);
       v[i][1] = unpack_half2(u.y);
       v[i][2] = unpack_half2(u.z);
@@ -105,15 +110,11 @@ __global__ void __launch_bounds__(kRotWarps * 32)
 #pragma unroll
       for (int i = c0; i < c0 + UNIT; ++i) {
         if (i < NCH) {
-          const int c = i * 256 + lane * 8;
-          const float4 g0 = __ldg(reinterpret_cast<const float4*>(gamma + c));
-          const float4 g1 = __ldg(reinterpret_cast<const float4*>(gamma + c + 4));
-          const float4 b0 = __ldg(reinterpret_cast<const float4*>(beta + c));
-          const float4 b1 = __ldg(reinterpret_cast<const float4*>(beta + c + 4));
-          v[i][0] = fma2(v[i][0], mul2(r2, make_float2(g0.x, g0.y)), make_float2(b0.x, b0.y));
-          v[i][1] = fma2(v[i][1], mul2(r2, make_float2(g0.z, g0.w)), make_float2(b0.z, b0.w));
-          v[i][2] = fma2(v[i][2], mul2(r2, make_float2(g1.x, g1.y)), make_float2(b1.x, b1.y));
-          v[i][3] = fma2(v[i][3], mul2(r2, make_float2(g1.z, g1.w)), make_float2(b1.z, b1.w));
+          float g[8], b[8];
+          gb(i, g, b);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            v[i][k] = fma2(v[i][k], mul2(r2, make_float2(g[2 * k], g[2 * k + 1])), make_float2(b[2 * k], b[2 * k + 1]));
           zero_ragged(i);
         }
       }
@@ -234,11 +235,181 @@ __global__ void __launch_bounds__(kRotWarps * 32)
   if (lane == 0) row_scale[row] = scale;
 }
 
+// Per-row grid (one warp per row); gamma/beta, when used, come through L1 for every row.
+template <int NCH, int BLOCK, bool NORM>
+__global__ void __launch_bounds__(kRotWarps * 32)
+    rot_q8_kernel(const __half* __restrict__ x, const float* __restrict__ gamma, const float* __restrict__ beta,
+                  float eps, int rows, int valid_cols, int8_t* __restrict__ out, float* __restrict__ row_scale) {
+  using S = RotShape<NCH, BLOCK>;
+  __shared__ __align__(16) float smem[kRotWarps][S::SW];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int row = blockIdx.x * kRotWarps + wid;
+  if (row >= rows) return;
+  rot_row<NCH, BLOCK, NORM, false>(x + static_cast<size_t>(row) * S::COLS, eps, row, valid_cols, out, row_scale,
+                                   smem[wid], lane,
+                            [&](int i, float (&g)[8], float (&b)[8]) {
+                              const int c = i * 256 + lane * 8;
+                              const float4 g0 = __ldg(reinterpret_cast<const float4*>(gamma + c));
+                              const float4 g1 = __ldg(reinterpret_cast<const float4*>(gamma + c + 4));
+                              const float4 b0 = __ldg(reinterpret_cast<const float4*>(beta + c));
+                              const float4 b1 = __ldg(reinterpret_cast<const float4*>(beta + c + 4));
+                              g[0] = g0.x, g[1] = g0.y, g[2] = g0.z, g[3] = g0.w;
+                              g[4] = g1.x, g[5] = g1.y, g[6] = g1.z, g[7] = g1.w;
+                              b[0] = b0.x, b[1] = b0.y, b[2] = b0.z, b[3] = b0.w;
+                              b[4] = b1.x, b[5] = b1.y, b[6] = b1.z, b[7] = b1.w;
+                            });
+}
+
+// Persistent grid, one CTA per SM, each warp walking rows with a grid stride. Two things the per-row grid
+// pays for every row are moved off the L1 data pipe (the limiter, see above) and off the critical path:
+//  - the row itself arrives by a bulk asynchronous copy (cp.async.bulk, no multicast) into a per-warp
+//    double buffer in shared memory, issued one row ahead, so HBM latency overlaps the previous row;
+//  - with the LayerNorm, gamma and beta live in TMEM: each CTA writes every lane's 8 + 8 values per
+//    chunk once (16 columns per chunk, one copy per TMEM sub-partition, so warp w reads lane quarter
+//    w % 4 as any tcgen05.ld does) and each row reads them back with tcgen05.ld instead of reloading
+//    them through L1, where they cost twice the wavefronts of the row's own input.
+// Every wait is bounded; on a timeout the warp records kDevTimeoutRotate, drains its copy and stops.
+template <int NCH, int BLOCK, int WARPS, bool NORM>
+__global__ void __launch_bounds__(WARPS * 32, 1)
+    rot_q8_persistent_kernel(const __half* __restrict__ x, const float* __restrict__ gamma,
+                             const float* __restrict__ beta, float eps, int rows, int valid_cols,
+                             int8_t* __restrict__ out, float* __restrict__ row_scale, int* err) {
+  using S = RotShape<NCH, BLOCK>;
+  constexpr uint32_t kRowBytes = S::COLS * 2;
+  constexpr uint32_t kCols = NCH * 16 <= 32 ? 32 : NCH * 16 <= 64 ? 64 : NCH * 16 <= 128 ? 128 : 256;
+  static_assert(NCH * 16 <= 256, "gamma/beta do not fit the TMEM allocation");
+  extern __shared__ float4 rot_dyn[];
+  __shared__ uint32_t tmem_slot;
+  __shared__ uint64_t bars[WARPS][2];
+  __shared__ int abort_flag;
+  // [WARPS][2] row buffers, then [WARPS] transpose buffers
+  uint8_t* rowbuf = reinterpret_cast<uint8_t*>(rot_dyn);
+  float* tbuf = reinterpret_cast<float*>(rowbuf + static_cast<size_t>(WARPS) * 2 * kRowBytes);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    for (int w = 0; w < WARPS; ++w) {
+      mbar_init(&bars[w][0], 1);
+      mbar_init(&bars[w][1], 1);
+    }
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if constexpr (NORM) {
+    if (wid == 0) {
+      tmem_alloc(&tmem_slot, kCols);
+      tmem_relinquish();
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  uint32_t tmem = 0;
+  if constexpr (NORM) {
+    tmem = tmem_slot + (static_cast<uint32_t>(32 * (wid & 3)) << 16);
+    if (wid < 4) {
+#pragma unroll 1
+      for (int i = 0; i < NCH; ++i) {
+        const int c = i * 256 + lane * 8;
+        uint32_t r[16];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          r[e] = __float_as_uint(__ldg(gamma + c + e));
+          r[8 + e] = __float_as_uint(__ldg(beta + c + e));
+        }
+        tmem_st16(tmem + 16 * i, r);
+      }
+      tmem_st_wait();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  }
+  volatile int* abort_v = &abort_flag;
+  const int stride = gridDim.x * WARPS;
+  auto buf = [&](int b) { return reinterpret_cast<const __half*>(rowbuf + (2 * wid + b) * kRowBytes); };
+  auto issue = [&](int r, int b) {  // lane 0: bring row r into buffer b
+    mbar_arrive_expect_tx(&bars[wid][b], kRowBytes);
+    bulk_load(buf(b), x + static_cast<size_t>(r) * S::COLS, kRowBytes, &bars[wid][b]);
+  };
+  int row = blockIdx.x * WARPS + wid;
+  int issued = 0, waited = 0;  // copies issued / waited for (buffer of copy n: n & 1)
+  if (row < rows) {
+    if (lane == 0) issue(row, 0);
+    issued = 1;
+  }
+  for (int k = 0; row < rows; ++k, row += stride) {
+    const int b = k & 1;
+    const int next = row + stride;
+    if (next < rows) {
+      fence_async_smem();  // this warp's reads of the buffer being refilled (two rows ago) come first
+      __syncwarp();
+      if (lane == 0) issue(next, b ^ 1);
+      ++issued;
+    }
+    if (!mbar_wait(&bars[wid][b], static_cast<uint32_t>(k >> 1) & 1u, abort_v, err, kDevTimeoutRotate)) break;
+    ++waited;
+    rot_row<NCH, BLOCK, NORM, true>(buf(b), eps, row, valid_cols, out, row_scale, tbuf + wid * S::SW, lane,
+                                    [&](int i, float (&g)[8], float (&bb)[8]) {
+                                      uint32_t r[16];
+                                      tmem_ld16(tmem + 16 * i, r);
+                                      tmem_ld_wait();
+#pragma unroll
+                                      for (int e = 0; e < 8; ++e) {
+                                        g[e] = __uint_as_float(r[e]);
+                                        bb[e] = __uint_as_float(r[8 + e]);
+                                      }
+                                    });
+    __syncwarp();
+  }
+  // Copies can only still be in flight after a timeout: let them land (bounded) before the CTA exits.
+  // Copy n goes to buffer n & 1 and completes that barrier's phase (n >> 1).
+  if (lane == 0) {
+    const unsigned long long t0 = globaltimer();
+    for (int n = waited; n < issued; ++n)
+      while (!mbar_try_wait(smem_u32(&bars[wid][n & 1]), static_cast<uint32_t>(n >> 1) & 1u) &&
+             globaltimer() - t0 < kWaitLimitNs) {
+      }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if constexpr (NORM)
+    if (wid == 0) tmem_dealloc(tmem_slot, kCols);
+}
+
 namespace {
+
+template <int NCH, int BLOCK, bool NORM>
+int launch_persistent(const __half* x, const float* g, const float* b, float eps, int rows, int valid, int8_t* out,
+                      float* rs, int* err, cudaStream_t s) {
+  // One CTA per SM: 12 warps for the wide rows (registers), 16 otherwise.
+  constexpr int WARPS = NCH > 8 ? 12 : 16;
+  constexpr size_t smem = static_cast<size_t>(WARPS) * (2 * NCH * 256 * 2 + sizeof(float) * RotShape<NCH, BLOCK>::SW);
+  static_assert(smem <= 200 * 1024, "rotation staging does not fit shared memory");
+  auto kernel = rot_q8_persistent_kernel<NCH, BLOCK, WARPS, NORM>;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+        cudaSuccess)
+      return check_launch("rot_q8: cudaFuncSetAttribute");
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  const int ctas = std::min(sm_count(), (rows + WARPS - 1) / WARPS);
+  kernel<<<ctas, WARPS * 32, smem, s>>>(x, g, b, eps, rows, valid, out, rs, err);
+  return check_launch("rot_q8_persistent_kernel");
+}
 
 template <int NCH, int BLOCK>
 int launch_rot(const __half* x, const float* g, const float* b, float eps, int rows, int valid, int8_t* out,
-               float* rs, cudaStream_t s) {
+               float* rs, int* err, cudaStream_t s) {
+  // LayerNorm rows take the persistent kernel (gamma/beta in TMEM). Rows without a norm need no per-row
+  // constants and run faster on the per-row grid, whose higher occupancy hides the HBM latency (measured:
+  // 48 vs 64 us for 65,600 x 1024). The widest rows (4096) do not fit the persistent kernel's staging.
+  if constexpr (NCH <= 11) {
+    if (g != nullptr) return launch_persistent<NCH, BLOCK, true>(x, g, b, eps, rows, valid, out, rs, err, s);
+  }
   const dim3 grid((rows + kRotWarps - 1) / kRotWarps);
   if (g != nullptr)
     rot_q8_kernel<NCH, BLOCK, true><<<grid, kRotWarps * 32, 0, s>>>(x, g, b, eps, rows, valid, out, rs);
@@ -249,15 +420,15 @@ int launch_rot(const __half* x, const float* g, const float* b, float eps, int r
 
 template <int NCH>
 int dispatch_block(int block, const __half* x, const float* g, const float* b, float eps, int rows, int valid,
-                   int8_t* out, float* rs, cudaStream_t s) {
+                   int8_t* out, float* rs, int* err, cudaStream_t s) {
   switch (block) {
-    case 128: return launch_rot<NCH, 128>(x, g, b, eps, rows, valid, out, rs, s);
-    case 256: return launch_rot<NCH, 256>(x, g, b, eps, rows, valid, out, rs, s);
+    case 128: return launch_rot<NCH, 128>(x, g, b, eps, rows, valid, out, rs, err, s);
+    case 256: return launch_rot<NCH, 256>(x, g, b, eps, rows, valid, out, rs, err, s);
     case 512:
-      if constexpr (NCH % 2 == 0) return launch_rot<NCH, 512>(x, g, b, eps, rows, valid, out, rs, s);
+      if constexpr (NCH % 2 == 0) return launch_rot<NCH, 512>(x, g, b, eps, rows, valid, out, rs, err, s);
       break;
     case 1024:
-      if constexpr (NCH % 4 == 0) return launch_rot<NCH, 1024>(x, g, b, eps, rows, valid, out, rs, s);
+      if constexpr (NCH % 4 == 0) return launch_rot<NCH, 1024>(x, g, b, eps, rows, valid, out, rs, err, s);
       break;
   }
   set_error("ff_rot_q8: block %d does not divide %d columns", block, NCH * 256);
@@ -267,7 +438,7 @@ int dispatch_block(int block, const __half* x, const float* g, const float* b, f
 }  // namespace
 
 int rot_q8(const void* x, const float* g, const float* b, float eps, int rows, int cols, int valid, int block,
-           int8_t* out, float* rs, cudaStream_t s) {
+           int8_t* out, float* rs, cudaStream_t s, int* err) {
   FF_REQUIRE(x && out && rs, "ff_rot_q8: NULL pointer");
   FF_REQUIRE(rows >= 0, "ff_rot_q8: rows %d", rows);
   FF_REQUIRE(valid >= 1 && valid <= cols, "ff_rot_q8: valid_cols %d not in [1, %d]", valid, cols);
@@ -275,13 +446,17 @@ int rot_q8(const void* x, const float* g, const float* b, float eps, int rows, i
   FF_REQUIRE(aligned16(x) && (g == nullptr || (aligned16(g) && aligned16(b))), "ff_rot_q8: pointers must be 16-byte aligned");
   FF_REQUIRE((reinterpret_cast<uintptr_t>(out) & 7u) == 0, "ff_rot_q8: out must be 8-byte aligned");
   if (rows == 0) return FF_OK;
+  FF_REQUIRE(cols == 768 || cols == 1024 || cols == 2048 || cols == 2816 || cols == 4096,
+             "ff_rot_q8: %d columns is not one of 768, 1024, 2048, 2816, 4096", cols);
+  if (err == nullptr && g != nullptr) err = device_error_word();  // the LayerNorm kernel's bounded waits
+  FF_REQUIRE(err != nullptr || g == nullptr, "ff_rot_q8: no device error word");
   const __half* xh = static_cast<const __half*>(x);
   switch (cols) {
-    case 768: return dispatch_block<3>(block, xh, g, b, eps, rows, valid, out, rs, s);
-    case 1024: return dispatch_block<4>(block, xh, g, b, eps, rows, valid, out, rs, s);
-    case 2048: return dispatch_block<8>(block, xh, g, b, eps, rows, valid, out, rs, s);
-    case 2816: return dispatch_block<11>(block, xh, g, b, eps, rows, valid, out, rs, s);
-    case 4096: return dispatch_block<16>(block, xh, g, b, eps, rows, valid, out, rs, s);
+    case 768: return dispatch_block<3>(block, xh, g, b, eps, rows, valid, out, rs, err, s);
+    case 1024: return dispatch_block<4>(block, xh, g, b, eps, rows, valid, out, rs, err, s);
+    case 2048: return dispatch_block<8>(block, xh, g, b, eps, rows, valid, out, rs, err, s);
+    case 2816: return dispatch_block<11>(block, xh, g, b, eps, rows, valid, out, rs, err, s);
+    case 4096: return dispatch_block<16>(block, xh, g, b, eps, rows, valid, out, rs, err, s);
   }
   set_error("ff_rot_q8: %d columns is not one of 768, 1024, 2048, 2816, 4096", cols);
   return FF_ERR_INVALID_ARGUMENT;

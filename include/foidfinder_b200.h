@@ -43,7 +43,7 @@ int ff_device_error(int device, int* code, int clear);
 
 /* ---------------------------------------------------------------- GEMM epilogues */
 #define FF_EPI_QKV_ROPE 0 /* fp16 out [M, N]; 2-D RoPE on columns [0, rope_cols) */
-#define FF_EPI_RESIDUAL 1 /* fp16 out [M, N] += y (the residual stream) */
+#define FF_EPI_RESIDUAL 1 /* fp16 out [M, N] = fp16(out + fp16(y)) (the residual stream) */
 #define FF_EPI_SWIGLU 3   /* W rows interleaved [gate 64 | up 64]; fp16 out [M, N/2] = silu(gate) * up */
 #define FF_EPI_BIAS 4     /* fp16 out [M, N] = y */
 #define FF_EPI_S32 5      /* int32 out [M, N] = raw accumulators */

@@ -122,6 +122,12 @@ def tree_pool(x: torch.Tensor, w: dict, cfg, half: bool, eps: float | None = Non
     return f(leaf.reshape(B, Qn * L))
 
 
+def _residual(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+    """fp16 residual stream: x + fp16(y), rounded to fp16 (the reference stages y as fp16 and adds with
+    __hadd2, foidfinder/backends/cuda/csrc/gemm.cuh:153-169)."""
+    return (x.float() + y.half().float()).half()
+
+
 def _lin(a8: torch.Tensor, rs: torch.Tensor, conv: dict, name: str) -> torch.Tensor:
     acc = Q.gemm_s8_acc(a8, conv[name + ".qweight"])
     return Q.dequant(acc, rs, conv[name + ".wscale"], conv[name + ".bias"])
@@ -157,7 +163,7 @@ def forward_int8(
         qkv = _rope_qk(_lin(a8, rs, conv, p + "qkv"), cos, sin, T, D).half()
         o = _attention(qkv, B, T, H).half()
         a8o, rso = rot_q8(o, None, None, block=cfg.rot_block_dim)
-        x = (x.float() + _lin(a8o, rso, conv, p + "proj")).half()
+        x = _residual(x, _lin(a8o, rso, conv, p + "proj"))
         a8m, rsm = rot_q8(x, conv[p + "norm2.weight"], conv[p + "norm2.bias"], block=cfg.rot_block_dim, eps=eps)
         gu = _lin(a8m, rsm, conv, p + "fc1").view(B * T, Hp // 64, 2, 64)
         h = Q.silu_mul(gu[:, :, 0], gu[:, :, 1]).reshape(B * T, Hp).half()
@@ -166,7 +172,7 @@ def forward_int8(
             valid_cols=cfg.mlp_hidden,
         )
         x_mid = x
-        x = (x.float() + _lin(a8h, rsh, conv, p + "fc2")).half()
+        x = _residual(x, _lin(a8h, rsh, conv, p + "fc2"))
         if trace is not None:
             trace.append(
                 dict(x_in=x_in, a8=a8, rs=rs, qkv=qkv, o=o, a8o=a8o, rso=rso, x_attn=x_mid, a8m=a8m, rsm=rsm, h=h,
