@@ -27,6 +27,7 @@ STATUS = {
 # Epilogue ids (include/foidfinder_b200.h); the first two keep the reference's numbering
 # (foidfinder/backends/cuda/csrc/gemm.cuh:8-12).
 EPI_QKV_ROPE, EPI_RESIDUAL, EPI_SWIGLU, EPI_BIAS, EPI_S32, EPI_STEM, EPI_LOGITS = 0, 1, 3, 4, 5, 6, 7
+EPI_GELU = 2
 
 # ff_engine_profile kernel classes (FF_PROF_*).
 PROF_CLASSES = ("stem_prep", "stem_gemm", "rotate", "gemm_qkv", "attention", "gemm_proj", "gemm_fc1", "gemm_fc2", "head")
@@ -56,14 +57,21 @@ class ModelConfig(C.Structure):
         ("coarse_queries", i32),
         ("leaf_queries", i32),
         ("leaf_dim", i32),
+        ("arch", i32),
+        ("window", i32),
+        ("global_blocks", C.c_uint64),
     ]
 
 
-HEAD_CLS, HEAD_TREE = 0, 1
+HEAD_CLS, HEAD_TREE, HEAD_POOL = 0, 1, 2
+ARCH_EVA02, ARCH_PIXAI = 0, 1
 RESAMPLE_BILINEAR, RESAMPLE_BICUBIC = 0, 1
 POOL_FIELDS = (
     "pool_norm_w", "pool_norm_b", "pool_kv_w", "pool_kv_b", "q_coarse", "q_coarse_bias", "q_child", "q_child_bias",
     "trunk_norm_w", "trunk_norm_b", "child_q_norm_w", "child_q_norm_b", "leaf_norm_w", "leaf_norm_b", "leaf_w", "leaf_b",
+)
+PIXAI_FIELDS = (
+    "ln_pre_w", "ln_pre_b", "rope_cos_global", "rope_sin_global", "pool_pos", "pool_q", "pool_proj_w", "pool_proj_b",
 )
 
 
@@ -89,7 +97,7 @@ class ModelWeights(C.Structure):
         ("norm_b", vp),
         ("head_w", vp),
         ("head_b", vp),
-    ] + [(name, vp) for name in POOL_FIELDS]
+    ] + [(name, vp) for name in POOL_FIELDS + PIXAI_FIELDS]
 
 
 _SIGNATURES = {
@@ -109,6 +117,9 @@ _SIGNATURES = {
     "ff_topk": (i32, [vp, i32, i32, i32, vp, vp, vp]),
     "ff_tree_pool": (i32, [C.POINTER(ModelConfig), C.POINTER(ModelWeights), vp, i32, vp, i64, vp, vp]),
     "ff_resize_pad": (i32, [vp, i32, i32, i32, i32, i32, i32, i32, vp, vp, i64, vp]),
+    "ff_patchify_windowed": (i32, [vp, i32, i32, i32, C.POINTER(f32), C.POINTER(f32), vp, i32, i32, vp]),
+    "ff_layernorm_pos": (i32, [vp, i64, vp, vp, f32, i32, i32, vp, i32, vp, vp]),
+    "ff_pool_query_attention": (i32, [vp, vp, i32, i32, i32, vp, vp]),
     "ff_resize_pad_workspace_bytes": (i64, [i32, i32, i32, i32, i32]),
     "ff_tree_pool_workspace_bytes": (i64, [C.POINTER(ModelConfig), i32]),
     "ff_engine_create": (i32, [C.POINTER(ModelConfig), C.POINTER(ModelWeights), i32, C.POINTER(vp)]),

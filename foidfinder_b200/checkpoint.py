@@ -57,7 +57,7 @@ def load(model_dir: str | Path, device: str | torch.device = "cpu") -> tuple[Mod
         if meta.get("format") != FORMAT:
             raise ValueError(f"{path}: format {meta.get('format')!r}, expected {FORMAT!r}")
         fields = json.loads(meta["config"])
-        fields["mean"], fields["std"] = tuple(fields["mean"]), tuple(fields["std"])
+        fields = {k: tuple(v) if isinstance(v, list) else v for k, v in fields.items()}  # JSON lists -> tuples
         cfg = ModelConfig(**fields)
         conv = {k: f.get_tensor(k) for k in f.keys()}
     return cfg, conv

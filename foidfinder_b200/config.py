@@ -39,9 +39,13 @@ class ModelConfig:
     rot_block_dim: int = 1024  # Hadamard block of the dim-wide GEMM inputs (qkv, proj, fc1)
     rot_block_hidden: int = 128  # Hadamard block of the hidden-wide GEMM input (fc2)
     topk: int = 50
+    arch: str = "eva02"  # "eva02": class token, SwiGLU + hidden LN, EVA02 RoPE; "pixai": see PIXAI_1008
+    window: int = 0  # window attention size in patches (0: every block global)
+    global_blocks: tuple[int, ...] = ()  # blocks that attend over the whole image when window > 0
     resample: str = "bilinear"  # letterbox filter: PixAI's antialiased bilinear on black
     pad: int = 0  # letterbox canvas value
-    head: str = "cls"  # "cls": class-token linear head; "tree": the Haruka tree attention pool
+    head: str = "cls"  # "cls": class-token linear head; "tree": the Haruka tree attention pool; "pool": PixAI's
+    # one-query attention pool (LN + position embedding -> kv -> attention -> proj)
     pool_heads: int = 16
     coarse_queries: int = 6
     leaf_queries: int = 18
@@ -49,8 +53,8 @@ class ModelConfig:
 
     @property
     def head_in(self) -> int:
-        """K of the tag head: dim (class token) or leaf_queries * leaf_dim (tree pool)."""
-        return self.dim if self.head == "cls" else self.leaf_queries * self.leaf_dim
+        """K of the tag head: dim (class token, attention pool) or leaf_queries * leaf_dim (tree pool)."""
+        return self.leaf_queries * self.leaf_dim if self.head == "tree" else self.dim
 
     @property
     def grid(self) -> int:
@@ -61,8 +65,15 @@ class ModelConfig:
         return self.grid * self.grid
 
     @property
+    def cls_token(self) -> bool:
+        return self.arch == "eva02"
+
+    @property
     def tokens(self) -> int:
-        return self.patches + 1
+        return self.patches + (1 if self.cls_token else 0)
+
+    def is_global(self, block: int) -> bool:
+        return self.window == 0 or block in self.global_blocks
 
     @property
     def head_dim(self) -> int:
@@ -85,13 +96,18 @@ class ModelConfig:
         return _ceil(self.k_patch, 64)
 
     def gemm_ops_per_image(self, padded: bool = False) -> int:
-        """Int8 multiply-adds x 2 of the four block GEMMs per image (qkv, proj, gate|up, down)."""
+        """Int8 multiply-adds x 2 of the four block GEMMs per image (qkv, proj, gate|up or fc1, down)."""
         h = self.mlp_hidden_pad if padded else self.mlp_hidden
-        per_token = self.dim * 3 * self.dim + self.dim * self.dim + self.dim * 2 * h + h * self.dim
+        up = 2 * h if self.arch == "eva02" else h
+        per_token = self.dim * 3 * self.dim + self.dim * self.dim + self.dim * up + h * self.dim
         return 2 * self.tokens * self.depth * per_token
 
     def attention_flops_per_image(self) -> int:
-        return 4 * self.heads * self.tokens * self.tokens * self.head_dim * self.depth
+        total = 0
+        for i in range(self.depth):
+            n = self.tokens if self.is_global(i) else self.window * self.window
+            total += 4 * self.heads * self.tokens * n * self.head_dim
+        return total
 
     def with_(self, **kw) -> ModelConfig:
         return replace(self, **kw)
@@ -113,4 +129,22 @@ EVA02_B = ModelConfig(
     head="tree",
 )
 
-CONFIGS = {c.name: c for c in (EVA02_L, EVA02_B)}
+# The reference's real `cuda` workload, PixAI Tagger v1.0 (foidfinder/backends/cuda/reference.py:12-17):
+# 1008 px, patch 14 -> 72 x 72 = 5184 tokens in window order (no class token), 32 blocks of dim 1024 with
+# 24 x 24 windowed attention except blocks 7, 15, 23, 31 (global), axial 2-D RoPE, GELU MLP 4736,
+# LayerNorm eps 1e-5 and an ln_pre after the stem, a one-query attention-pool head, 30,877 tags.
+PIXAI_1008 = ModelConfig(
+    "pixai-1008",
+    image_size=1008,
+    depth=32,
+    mlp_hidden=4736,
+    ln_eps=1e-5,
+    rot_block_dim=1024,
+    rot_block_hidden=128,
+    arch="pixai",
+    window=24,
+    global_blocks=(7, 15, 23, 31),
+    head="pool",
+)
+
+CONFIGS = {c.name: c for c in (EVA02_L, EVA02_B, PIXAI_1008)}

@@ -8,6 +8,9 @@
 //              down GEMM (+bias, residual)
 // followed by the head — the final LayerNorm of the class tokens (FF_HEAD_CLS) or the Haruka tree
 // attention pool over all tokens (FF_HEAD_TREE, pool.cu) — the fp16 tag head and a device top-k.
+// FF_ARCH_PIXAI runs PixAICuda._forward itself: window-ordered patches, ln_pre, window attention with the
+// window RoPE table except in the global blocks, GELU fc1 epilogue, H128 of the 4736-wide hidden, and the
+// one-query attention pool (reference.py:133-140) before the tag head.
 // Graph capture per batch size replaces the torch.cuda.graph capture of engine.py:163-184.
 #include <cuda_fp16.h>
 
@@ -37,7 +40,7 @@ struct ff_engine {
     float* logits = nullptr;
     int32_t* top_idx = nullptr;
     float* top_val = nullptr;
-    ff::GemmPlan stem, head, pool_kv;
+    ff::GemmPlan stem, head, pool_kv, pool_proj;
     ff::PoolBuffers pool;
     std::vector<ff::GemmPlan> qkv_p, proj_p, fc1_p, fc2_p;
     cudaGraphExec_t exec = nullptr;
@@ -72,8 +75,19 @@ struct Layout {
 
 int head_in(const ff_model_config& c) { return c.head_kind == FF_HEAD_TREE ? c.leaf_queries * c.leaf_dim : c.dim; }
 
+bool pixai(const ff_model_config& c) { return c.arch == FF_ARCH_PIXAI; }
+
+int tokens_of(const ff_model_config& c) {
+  const int G = c.image_size / c.patch;
+  return G * G + (pixai(c) ? 0 : 1);
+}
+
+bool is_global(const ff_model_config& c, int block) {
+  return !pixai(c) || (block < 64 && ((c.global_blocks >> block) & 1ull) != 0);
+}
+
 Layout layout_for(const ff_model_config& c, int B) {
-  const size_t G = c.image_size / c.patch, P = G * G, T = P + 1, M = static_cast<size_t>(B) * T;
+  const size_t G = c.image_size / c.patch, P = G * G, T = tokens_of(c), M = static_cast<size_t>(B) * T;
   const size_t kpad = align_up(static_cast<size_t>(c.patch) * c.patch * 3, 64);
   const size_t wide = std::max<size_t>(c.dim, c.mlp_hidden_pad);
   Layout l{};
@@ -107,13 +121,24 @@ int validate(const ff_model_config& c) {
   FF_REQUIRE(c.depth >= 1, "engine: depth %d", c.depth);
   FF_REQUIRE(c.mlp_hidden >= 1 && c.mlp_hidden <= c.mlp_hidden_pad && c.mlp_hidden_pad % 128 == 0,
              "engine: mlp_hidden %d / pad %d", c.mlp_hidden, c.mlp_hidden_pad);
-  FF_REQUIRE(c.mlp_hidden_pad == 2048 || c.mlp_hidden_pad == 2816 || c.mlp_hidden_pad == 4096,
-             "engine: mlp_hidden_pad %d has no rotation kernel", c.mlp_hidden_pad);
+  FF_REQUIRE(c.arch == FF_ARCH_EVA02 || c.arch == FF_ARCH_PIXAI, "engine: arch %d", c.arch);
+  if (pixai(c)) {
+    const int G = c.image_size / c.patch;
+    FF_REQUIRE(c.head_kind == FF_HEAD_POOL, "engine: the PixAI architecture needs head_kind FF_HEAD_POOL");
+    FF_REQUIRE(c.window >= 1 && G % c.window == 0, "engine: window %d does not tile the %d-patch grid", c.window, G);
+    FF_REQUIRE(c.mlp_hidden == c.mlp_hidden_pad && c.rot_block_hidden == 128,
+               "engine: the PixAI GELU hidden must be a multiple of 128 with an H128 rotation");
+  } else {
+    FF_REQUIRE(c.head_kind != FF_HEAD_POOL, "engine: FF_HEAD_POOL needs the PixAI architecture");
+    FF_REQUIRE(c.mlp_hidden_pad == 2048 || c.mlp_hidden_pad == 2816 || c.mlp_hidden_pad == 4096,
+               "engine: mlp_hidden_pad %d has no rotation kernel", c.mlp_hidden_pad);
+  }
   FF_REQUIRE(c.num_tags >= 1 && c.num_tags <= c.num_tags_pad && c.num_tags_pad % 256 == 0,
              "engine: num_tags %d / pad %d", c.num_tags, c.num_tags_pad);
   FF_REQUIRE(c.dim % c.rot_block_dim == 0 && c.mlp_hidden_pad % c.rot_block_hidden == 0, "engine: rotation blocks");
   FF_REQUIRE(c.topk >= 0 && c.topk <= 64 && c.topk <= c.num_tags, "engine: topk %d", c.topk);
-  FF_REQUIRE(c.head_kind == FF_HEAD_CLS || c.head_kind == FF_HEAD_TREE, "engine: head_kind %d", c.head_kind);
+  FF_REQUIRE(c.head_kind == FF_HEAD_CLS || c.head_kind == FF_HEAD_TREE || c.head_kind == FF_HEAD_POOL,
+             "engine: head_kind %d", c.head_kind);
   return FF_OK;
 }
 
@@ -185,12 +210,46 @@ int build_batch(ff_engine* e, int B, ff_engine::Batch** out) {
     rc = gemm_prepare(p, &b->head);
   }
   if (rc == FF_OK && c.head_kind == FF_HEAD_TREE) rc = pool_prepare(c, e->w, B, e->tokens, b->pool, &b->pool_kv);
+  if (rc == FF_OK && c.head_kind == FF_HEAD_POOL) {
+    // PixAI pool (reference.py:133-140): pool-normed tokens (+ pos) in o, keys|values in qkv, the attended
+    // [B, dim] rows in h, the projected rows in cls (the tag head's input).
+    GemmProblem p{};
+    p.A = b->o;
+    p.W = e->w.pool_kv_w;
+    p.out = b->qkv;
+    p.M = M;
+    p.N = 2 * D;
+    p.K = D;
+    p.epi = EPI_BIAS;
+    p.f16 = true;
+    p.args.bias = e->w.pool_kv_b;
+    p.args.ldo = 2 * D;
+    rc = gemm_prepare(p, &b->pool_kv);
+    if (rc == FF_OK) {
+      GemmProblem q{};
+      q.A = b->h;
+      q.W = e->w.pool_proj_w;
+      q.out = b->cls;
+      q.M = B;
+      q.N = D;
+      q.K = D;
+      q.epi = EPI_BIAS;
+      q.f16 = true;
+      q.args.bias = e->w.pool_proj_b;
+      q.args.ldo = D;
+      rc = gemm_prepare(q, &b->pool_proj);
+    }
+  }
   b->qkv_p.resize(c.depth);
   b->proj_p.resize(c.depth);
   b->fc1_p.resize(c.depth);
   b->fc2_p.resize(c.depth);
   for (int i = 0; i < c.depth && rc == FF_OK; ++i) {
     const ff_layer_weights& lw = e->layers[i];
+    const bool glob = is_global(c, i);
+    const float* rcos = pixai(c) && glob ? e->w.rope_cos_global : e->w.rope_cos;
+    const float* rsin = pixai(c) && glob ? e->w.rope_sin_global : e->w.rope_sin;
+    const int rope_tokens = glob ? e->tokens : c.window * c.window;  // the RoPE table's rows
     auto prep = [&](GemmPlan* plan, const int8_t* W, const float* s, const float* bias, void* out, int N, int K, int epi) {
       GemmProblem p{};
       p.A = b->a8;
@@ -205,15 +264,16 @@ int build_batch(ff_engine* e, int B, ff_engine::Batch** out) {
       p.args.col_scale = s;
       p.args.bias = bias;
       p.args.ldo = epi == EPI_SWIGLU ? N / 2 : N;
-      p.args.rope_cos = e->w.rope_cos;
-      p.args.rope_sin = e->w.rope_sin;
+      p.args.rope_cos = rcos;
+      p.args.rope_sin = rsin;
       p.args.rope_cols = epi == EPI_QKV_ROPE ? 2 * D : 0;
-      p.args.tokens = e->tokens;
+      p.args.tokens = rope_tokens;
       return gemm_prepare(p, plan);
     };
     rc = prep(&b->qkv_p[i], lw.qkv_w, lw.qkv_s, lw.qkv_b, b->qkv, 3 * D, D, EPI_QKV_ROPE);
     if (rc == FF_OK) rc = prep(&b->proj_p[i], lw.proj_w, lw.proj_s, lw.proj_b, b->x, D, D, EPI_RESIDUAL);
-    if (rc == FF_OK) rc = prep(&b->fc1_p[i], lw.fc1_w, lw.fc1_s, lw.fc1_b, b->h, 2 * H, D, EPI_SWIGLU);
+    if (rc == FF_OK && pixai(c)) rc = prep(&b->fc1_p[i], lw.fc1_w, lw.fc1_s, lw.fc1_b, b->h, H, D, EPI_GELU_F16);
+    if (rc == FF_OK && !pixai(c)) rc = prep(&b->fc1_p[i], lw.fc1_w, lw.fc1_s, lw.fc1_b, b->h, 2 * H, D, EPI_SWIGLU);
     if (rc == FF_OK) rc = prep(&b->fc2_p[i], lw.fc2_w, lw.fc2_s, lw.fc2_b, b->x, D, H, EPI_RESIDUAL);
   }
   if (rc != FF_OK) {
@@ -258,25 +318,39 @@ struct Profiler {
 int run_forward(ff_engine* e, ff_engine::Batch* b, cudaStream_t s, Profiler* prof = nullptr) {
   const ff_model_config& c = e->cfg;
   const int B = b->B, M = B * e->tokens, D = c.dim, H = c.mlp_hidden_pad;
-  FF_LAUNCH(FF_PROF_STEM_PREP, patchify(b->images, B, c.image_size, c.patch, c.mean, c.std, b->patches, e->k_pad, s));
+  FF_LAUNCH(FF_PROF_STEM_PREP, patchify(b->images, B, c.image_size, c.patch, c.mean, c.std, b->patches, e->k_pad, s,
+                                        pixai(c) ? c.window : 0));
   FF_LAUNCH(FF_PROF_STEM_GEMM, gemm_launch(b->stem, s));
-  FF_LAUNCH(FF_PROF_STEM_PREP, fill_cls(e->w.cls_row, b->x, B, e->tokens, D, s));
+  if (pixai(c))  // ln_pre, in place (engine.py:148)
+    FF_LAUNCH(FF_PROF_STEM_PREP, layernorm(b->x, D, e->w.ln_pre_w, e->w.ln_pre_b, c.ln_eps, M, D, b->x, s));
+  else
+    FF_LAUNCH(FF_PROF_STEM_PREP, fill_cls(e->w.cls_row, b->x, B, e->tokens, D, s));
   for (int i = 0; i < c.depth; ++i) {
     const ff_layer_weights& lw = e->layers[i];
+    const int seq = is_global(c, i) ? e->tokens : c.window * c.window;  // engine.py:152
     FF_LAUNCH(FF_PROF_ROTATE, rot_q8(b->x, lw.norm1_w, lw.norm1_b, c.ln_eps, M, D, D, c.rot_block_dim, b->a8, b->rs, s));
     FF_LAUNCH(FF_PROF_GEMM_QKV, gemm_launch(b->qkv_p[i], s));
-    FF_LAUNCH(FF_PROF_ATTENTION, attention(b->qkv, b->o, B, e->tokens, c.heads, nullptr, nullptr, 1.f, s));
+    FF_LAUNCH(FF_PROF_ATTENTION, attention(b->qkv, b->o, M / seq, seq, c.heads, nullptr, nullptr, 1.f, s));
     FF_LAUNCH(FF_PROF_ROTATE, rot_q8(b->o, nullptr, nullptr, 0.f, M, D, D, c.rot_block_dim, b->a8, b->rs, s));
     FF_LAUNCH(FF_PROF_GEMM_PROJ, gemm_launch(b->proj_p[i], s));
     FF_LAUNCH(FF_PROF_ROTATE, rot_q8(b->x, lw.norm2_w, lw.norm2_b, c.ln_eps, M, D, D, c.rot_block_dim, b->a8, b->rs, s));
     FF_LAUNCH(FF_PROF_GEMM_FC1, gemm_launch(b->fc1_p[i], s));
-    FF_LAUNCH(FF_PROF_ROTATE, rot_q8(b->h, lw.mlp_norm_w, lw.mlp_norm_b, c.ln_eps, M, H, c.mlp_hidden,
-                                     c.rot_block_hidden, b->a8, b->rs, s));
+    if (pixai(c))
+      FF_LAUNCH(FF_PROF_ROTATE, rot_q8(b->h, nullptr, nullptr, 0.f, M, H, H, c.rot_block_hidden, b->a8, b->rs, s));
+    else
+      FF_LAUNCH(FF_PROF_ROTATE, rot_q8(b->h, lw.mlp_norm_w, lw.mlp_norm_b, c.ln_eps, M, H, c.mlp_hidden,
+                                       c.rot_block_hidden, b->a8, b->rs, s));
     FF_LAUNCH(FF_PROF_GEMM_FC2, gemm_launch(b->fc2_p[i], s));
   }
-  if (c.head_kind == FF_HEAD_TREE)
+  if (c.head_kind == FF_HEAD_TREE) {
     FF_LAUNCH(FF_PROF_HEAD, pool_run(c, e->w, b->x, B, e->tokens, b->pool, b->pool_kv, b->cls, s));
-  else
+  } else if (c.head_kind == FF_HEAD_POOL) {
+    FF_LAUNCH(FF_PROF_HEAD, layernorm(b->x, D, e->w.pool_norm_w, e->w.pool_norm_b, c.ln_eps, M, D, b->o, s,
+                                      e->w.pool_pos, e->tokens));
+    FF_LAUNCH(FF_PROF_HEAD, gemm_launch(b->pool_kv, s));
+    FF_LAUNCH(FF_PROF_HEAD, pool_query_attention(e->w.pool_q, b->qkv, B, e->tokens, c.heads, b->h, s));
+    FF_LAUNCH(FF_PROF_HEAD, gemm_launch(b->pool_proj, s));
+  } else
     FF_LAUNCH(FF_PROF_HEAD, layernorm(b->x, static_cast<int64_t>(e->tokens) * D, e->w.norm_w, e->w.norm_b, c.ln_eps, B,
                                       D, b->cls, s));
   FF_LAUNCH(FF_PROF_HEAD, gemm_launch(b->head, s));
@@ -285,7 +359,8 @@ int run_forward(ff_engine* e, ff_engine::Batch* b, cudaStream_t s, Profiler* pro
 }
 
 int launches_per_forward(const ff_model_config& c) {
-  return 3 + 9 * c.depth + (c.head_kind == FF_HEAD_TREE ? kPoolLaunches : 1) + 1 + (c.topk > 0 ? 1 : 0);
+  const int head = c.head_kind == FF_HEAD_TREE ? kPoolLaunches : c.head_kind == FF_HEAD_POOL ? 4 : 1;
+  return 3 + 9 * c.depth + head + 1 + (c.topk > 0 ? 1 : 0);
 }
 
 int copy_out(ff_engine* e, ff_engine::Batch* b, float* logits, int32_t* top_idx, float* top_val, cudaStream_t s) {
@@ -336,15 +411,22 @@ extern "C" int64_t ff_engine_workspace_bytes(const ff_model_config* cfg, int B) 
 extern "C" int ff_engine_create(const ff_model_config* cfg, const ff_model_weights* w, int device, ff_engine** out) {
   FF_REQUIRE(cfg && w && out, "ff_engine_create: NULL argument");
   FF_TRY(validate(*cfg));
-  FF_REQUIRE(w->patch_w && w->pos_bias && w->cls_row && w->rope_cos && w->rope_sin && w->layers && w->norm_w &&
-                 w->norm_b && w->head_w && w->head_b,
+  const bool px = pixai(*cfg);
+  FF_REQUIRE(w->patch_w && w->pos_bias && w->rope_cos && w->rope_sin && w->layers && w->head_w && w->head_b,
              "ff_engine_create: a model weight pointer is NULL");
+  if (px)
+    FF_REQUIRE(w->ln_pre_w && w->ln_pre_b && w->rope_cos_global && w->rope_sin_global && w->pool_norm_w &&
+                   w->pool_norm_b && w->pool_pos && w->pool_q && w->pool_kv_w && w->pool_kv_b && w->pool_proj_w &&
+                   w->pool_proj_b,
+               "ff_engine_create: a PixAI weight pointer (ln_pre, global RoPE, attention pool) is NULL");
+  else
+    FF_REQUIRE(w->cls_row && w->norm_w && w->norm_b, "ff_engine_create: class row or final LayerNorm is NULL");
   if (cfg->head_kind == FF_HEAD_TREE) FF_TRY(pool_validate(*cfg, *w));
   for (int i = 0; i < cfg->depth; ++i) {
     const ff_layer_weights& l = w->layers[i];
     FF_REQUIRE(l.norm1_w && l.norm1_b && l.qkv_w && l.qkv_s && l.qkv_b && l.proj_w && l.proj_s && l.proj_b &&
-                   l.norm2_w && l.norm2_b && l.fc1_w && l.fc1_s && l.fc1_b && l.mlp_norm_w && l.mlp_norm_b && l.fc2_w &&
-                   l.fc2_s && l.fc2_b,
+                   l.norm2_w && l.norm2_b && l.fc1_w && l.fc1_s && l.fc1_b && (px || (l.mlp_norm_w && l.mlp_norm_b)) &&
+                   l.fc2_w && l.fc2_s && l.fc2_b,
                "ff_engine_create: layer %d has a NULL weight pointer", i);
   }
   int ndev = 0;
@@ -363,7 +445,7 @@ extern "C" int ff_engine_create(const ff_model_config* cfg, const ff_model_weigh
   e->device = device;
   e->grid = cfg->image_size / cfg->patch;
   e->patches = e->grid * e->grid;
-  e->tokens = e->patches + 1;
+  e->tokens = tokens_of(*cfg);
   e->k_pad = static_cast<int>(align_up(static_cast<size_t>(cfg->patch) * cfg->patch * 3, 64));
   *out = e;
   return FF_OK;

@@ -42,6 +42,7 @@ int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CU
       case EPI_RESIDUAL: return launch_one<BN, STAGES, false, EPI_RESIDUAL>(ta, tb, tc, a, s);
       case EPI_SWIGLU: return launch_one<BN, STAGES, false, EPI_SWIGLU>(ta, tb, tc, a, s);
       case EPI_BIAS: return launch_one<BN, STAGES, false, EPI_BIAS>(ta, tb, tc, a, s);
+      case EPI_GELU_F16: return launch_one<BN, STAGES, false, EPI_GELU_F16>(ta, tb, tc, a, s);
       case EPI_S32: return launch_one<BN, STAGES, false, EPI_S32>(ta, tb, tc, a, s);
     }
   }
@@ -80,7 +81,8 @@ int gemm_prepare(const GemmProblem& p, GemmPlan* plan) {
   // 64 columns (128-byte swizzle) or, for the 128-wide SwiGLU tile, 32 columns (64-byte swizzle) — the
   // layouts the epilogue's staging buffer is written in.
   plan->tc = plan->ta;
-  if (p.epi == EPI_BIAS || p.epi == EPI_QKV_ROPE || p.epi == EPI_SWIGLU || p.epi == EPI_RESIDUAL) {
+  if (p.epi == EPI_BIAS || p.epi == EPI_QKV_ROPE || p.epi == EPI_SWIGLU || p.epi == EPI_RESIDUAL ||
+      p.epi == EPI_GELU_F16) {
     const int out_cols = p.epi == EPI_SWIGLU ? p.N / 2 : p.N;
     const int ldo = p.args.ldo;
     FF_REQUIRE(ldo >= out_cols && ldo % 8 == 0, "gemm: output row stride %d for %d columns", ldo, out_cols);
@@ -121,7 +123,8 @@ using namespace ff;
 extern "C" int ff_gemm_s8(const int8_t* A, const int8_t* W, const float* row_scale, const float* col_scale,
                           const float* bias, void* out, int M, int N, int K, int epi, const float* rope_cos,
                           const float* rope_sin, int rope_cols, int tokens, int tile_n, void* stream) {
-  FF_REQUIRE(epi == EPI_QKV_ROPE || epi == EPI_RESIDUAL || epi == EPI_SWIGLU || epi == EPI_BIAS || epi == EPI_S32,
+  FF_REQUIRE(epi == EPI_QKV_ROPE || epi == EPI_RESIDUAL || epi == EPI_SWIGLU || epi == EPI_BIAS || epi == EPI_S32 ||
+                 epi == EPI_GELU_F16,
              "ff_gemm_s8: unknown epilogue %d", epi);
   if (epi != EPI_S32) FF_REQUIRE(row_scale && col_scale && bias, "ff_gemm_s8: scales and bias are required");
   FF_REQUIRE(N % 128 == 0, "ff_gemm_s8: N=%d must be a multiple of 128", N);
@@ -160,7 +163,8 @@ extern "C" int ff_gemm_f16(const uint16_t* A, const uint16_t* W, const float* bi
   if (epi == EPI_BIAS) {
     FF_REQUIRE(bias != nullptr && ldo >= N && ldo % 8 == 0, "ff_gemm_f16: bias epilogue needs bias and ldo >= N, ldo %% 8 == 0");
   } else if (epi == EPI_STEM) {
-    FF_REQUIRE(pos_bias != nullptr && patches >= 1 && tokens >= patches + 1, "ff_gemm_f16: stem needs pos_bias, patches, tokens");
+    FF_REQUIRE(pos_bias != nullptr && patches >= 1 && (tokens == patches || tokens == patches + 1),
+               "ff_gemm_f16: stem needs pos_bias, patches and tokens = patches (+ 1 with a class token)");
     FF_REQUIRE(ldo >= N && ldo % 8 == 0, "ff_gemm_f16: stem ldo %d", ldo);
   } else {
     FF_REQUIRE(bias != nullptr && n_valid >= 1 && n_valid <= N && ldo >= n_valid, "ff_gemm_f16: logits need bias, n_valid <= N, ldo >= n_valid");

@@ -9,7 +9,7 @@ namespace ff {
 enum Epi : int {
   EPI_QKV_ROPE = 0,  // s8: fp16 out; 2-D RoPE on the q and k column ranges (columns < rope_cols)
   EPI_RESIDUAL = 1,  // s8: fp16 out[m, n] = fp16(float(out[m, n]) + y)
-  EPI_GELU_F16 = 2,  // s8: fp16 out = gelu(y)   (PixAI-1008 fc1; not instantiated yet)
+  EPI_GELU_F16 = 2,  // s8: fp16 out = gelu_tanh(y)   (PixAI-1008 fc1)
   EPI_SWIGLU = 3,    // s8: W rows are [gate 64 | up 64] pairs; fp16 out[m, n/2] = silu(gate) * up
   EPI_BIAS = 4,      // s8: fp16 out = y
   EPI_S32 = 5,       // s8: raw int32 accumulators (bit-exactness checks)

@@ -50,6 +50,14 @@ __device__ __forceinline__ float rcp_newton(float d) {
   return y;
 }
 
+// tanh GELU as the reference's fc1 epilogue computes it (foidfinder/backends/cuda/csrc/common.cuh:50-56),
+// with the hardware tanh.approx.
+__device__ __forceinline__ float gelu_tanh(float x) {
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.7978845608f * (x + 0.044715f * x * x * x)));
+  return 0.5f * x * (1.f + t);
+}
+
 // silu(g) * u with sigmoid(g) = 1 / (1 + 2^(-g log2 e)): one ex2 on the XU pipe, the rest on the FMA pipe.
 __device__ __forceinline__ float silu_mul(float g, float u) {
   const float e = ex2_approx(fminf(-g * 1.4426950408889634f, 64.f));
@@ -104,7 +112,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
   // fp16 outputs of these epilogues leave through TMA stores of the swizzled staging buffer (tmC).
-  constexpr bool kTmaStore = EPI == EPI_BIAS || EPI == EPI_QKV_ROPE || EPI == EPI_SWIGLU || EPI == EPI_RESIDUAL;
+  constexpr bool kTmaStore =
+      EPI == EPI_BIAS || EPI == EPI_QKV_ROPE || EPI == EPI_SWIGLU || EPI == EPI_RESIDUAL || EPI == EPI_GELU_F16;
   using C = GemmCfg<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -300,7 +309,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
           tma_store_2d(&tmC, stg, col0, m_block);
           bulk_commit_group();
         }
-      } else if constexpr (EPI == EPI_BIAS || EPI == EPI_QKV_ROPE || EPI == EPI_RESIDUAL) {
+      } else if constexpr (EPI == EPI_BIAS || EPI == EPI_QKV_ROPE || EPI == EPI_RESIDUAL || EPI == EPI_GELU_F16) {
         // 64 fp16 output columns per chunk; the warp owns HALF columns. The residual epilogue adds the
         // fp16-rounded y to the fp16 stream with a TMA add-reduction (x = fp16(x + fp16(y)), the reference's
         // __hadd2 of the staged fp16 result, foidfinder/backends/cuda/csrc/gemm.cuh:163-169).
@@ -349,6 +358,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
                 }
               }
             }
+            if constexpr (EPI == EPI_GELU_F16) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) y[j] = gelu_tanh(y[j]);
+            }
 #pragma unroll
             for (int j = 0; j < 32; j += 2) packed[sub * 16 + j / 2] = pack_half2(y[j], y[j + 1]);
           }
@@ -391,8 +404,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
               if (n < args.n_valid) dst[n] = __uint_as_float(r[j]) + args.bias[n];
             }
           } else if constexpr (EPI == EPI_STEM) {
-            // Patch row m of image b = m / patches goes to token b * tokens + 1 + (m % patches)
-            // (token 0 of each image is the class token). pos_bias = patch bias + position embedding.
+            // Patch row m of image b = m / patches goes to token b * tokens + (tokens - patches) + (m % patches)
+            // (with a class token, token 0 of each image). pos_bias = patch bias + position embedding.
             const int b = m / args.patches, p = m - b * args.patches;
             const float* pb = args.pos_bias + static_cast<size_t>(p) * args.N + n0;
             uint32_t packed[16];
@@ -402,7 +415,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
               packed[j / 2] = pack_half2(__uint_as_float(r[j]) + pv.x, __uint_as_float(r[j + 1]) + pv.y);
               packed[j / 2 + 1] = pack_half2(__uint_as_float(r[j + 2]) + pv.z, __uint_as_float(r[j + 3]) + pv.w);
             }
-            uint4* d4 = reinterpret_cast<uint4*>(out16 + (static_cast<size_t>(b) * args.tokens + 1 + p) * args.ldo + n0);
+            uint4* d4 = reinterpret_cast<uint4*>(out16 + (static_cast<size_t>(b) * args.tokens + (args.tokens - args.patches) + p) * args.ldo + n0);
 #pragma unroll
             for (int v = 0; v < 4; ++v)
               d4[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);

@@ -13,10 +13,15 @@ int attention(const void* qkv, void* out, int num_seqs, int seq_len, int heads, 
 int attention_tc(const void* qkv, void* out, int num_seqs, int seq_len, int heads, float scale, cudaStream_t s);
 int topk(const float* logits, int B, int n, int k, int32_t* idx, float* val, cudaStream_t s);
 int patchify(const uint8_t* img, int B, int S, int p, const float* mean, const float* stdv, void* out, int k_pad,
-             cudaStream_t s);
+             cudaStream_t s, int win = 0);
 int fill_cls(const void* cls, void* x, int B, int tokens, int dim, cudaStream_t s);
 int layernorm(const void* x, int64_t stride, const float* g, const float* b, float eps, int rows, int cols, void* out,
-              cudaStream_t s);
+              cudaStream_t s, const void* pos = nullptr, int period = 0);
+// H128 rotation + int8 of rows of any width that is a multiple of 128 (no LayerNorm): two passes per row.
+int rot_q8_h128_wide(const void* x, int rows, int cols, int8_t* out, float* rs, cudaStream_t s);
+// Attention of one learned query per head over all tokens: q [heads * 64] f32 (scale folded in),
+// kv [B * tokens, 2 * dim] fp16 (keys | values) -> out [B, dim] fp16.
+int pool_query_attention(const float* q, const void* kv, int B, int tokens, int heads, void* out, cudaStream_t s);
 int slot_attend(const float* q, int64_t q_img_stride, const float* bias, int M, const void* kv, int B, int tokens,
                 int dim, int heads, float* z, float* mass_part, cudaStream_t s);
 int pool_trunk(const float* z, int B, int coarse, int leaves, int dim, const float* trunk_w, const float* trunk_b,

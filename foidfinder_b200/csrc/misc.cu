@@ -1,5 +1,6 @@
 // Stem input preparation, the final LayerNorm and the device top-k of the tag logits.
 #include "common.h"
+#include "kernels.h"
 #include "ptx.cuh"
 
 namespace ff {
@@ -7,9 +8,12 @@ namespace ff {
 // ---------------------------------------------------------------- patchify
 // images [B, S, S, 3] uint8 -> patches [B * G * G, k_pad] fp16, column k = (kh * p + kw) * 3 + c
 // (the (kh, kw, c) order of reference.py:103-107 and mlx/haruka.py:78), value (px / 255 - mean) / std.
+// Patch rows in row-major grid order, or (win > 0) window order: the grid cut into win x win windows,
+// windows row-major, patches row-major inside each (foidfinder/backends/cuda/reference.py:21-24, 103-107).
 __global__ void patchify_kernel(const uint8_t* __restrict__ img, int B, int S, int p, float m0, float m1, float m2,
-                                float is0, float is1, float is2, __half* __restrict__ out, int k_pad) {
+                                float is0, float is1, float is2, __half* __restrict__ out, int k_pad, int win) {
   const int G = S / p, P = G * G, kreal = p * p * 3;
+  const int nw = win > 0 ? G / win : 1;
   const int64_t total = static_cast<int64_t>(B) * P * k_pad;
   for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
        t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -18,7 +22,12 @@ __global__ void patchify_kernel(const uint8_t* __restrict__ img, int B, int S, i
     float v = 0.f;
     if (k < kreal) {
       const int b = static_cast<int>(row / P), pi = static_cast<int>(row % P);
-      const int py = pi / G, px = pi % G;
+      int py = pi / G, px = pi % G;
+      if (win > 0) {
+        const int w = pi / (win * win), r = (pi / win) % win, c = pi % win;
+        py = (w / nw) * win + r;
+        px = (w % nw) * win + c;
+      }
       const int kh = k / (p * 3), rem = k % (p * 3);
       const int y = py * p + kh;
       const int c = rem % 3;
@@ -37,8 +46,11 @@ __global__ void fill_cls_kernel(const __half* __restrict__ cls, __half* __restri
 }
 
 // ---------------------------------------------------------------- LayerNorm (one warp per row)
+// LayerNorm of fp16 rows (f32 statistics) to fp16; with `pos`, the fp16 row pos[row % period] is added to
+// the fp16 result (the PixAI attention pool's LN + position embedding, reference.py:135).
 __global__ void layernorm_kernel(const __half* __restrict__ x, int64_t stride, const float* __restrict__ g,
-                                 const float* __restrict__ b, float eps, int rows, int cols, __half* __restrict__ out) {
+                                 const float* __restrict__ b, float eps, int rows, int cols, __half* __restrict__ out,
+                                 const __half* __restrict__ pos, int period) {
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -53,7 +65,12 @@ __global__ void layernorm_kernel(const __half* __restrict__ x, int64_t stride, c
   }
   const float rstd = rsqrtf(warp_sum(q) / static_cast<float>(cols) + eps);
   __half* orow = out + static_cast<size_t>(row) * cols;
-  for (int c = lane; c < cols; c += 32) orow[c] = __float2half_rn((__half2float(xr[c]) - mean) * rstd * g[c] + b[c]);
+  const __half* prow = pos != nullptr ? pos + static_cast<size_t>(row % period) * cols : nullptr;
+  for (int c = lane; c < cols; c += 32) {
+    __half y = __float2half_rn((__half2float(xr[c]) - mean) * rstd * g[c] + b[c]);
+    if (prow != nullptr) y = __float2half_rn(__half2float(y) + __half2float(prow[c]));
+    orow[c] = y;
+  }
 }
 
 // ---------------------------------------------------------------- top-k per row
@@ -194,14 +211,16 @@ int topk(const float* logits, int B, int n, int k, int32_t* idx, float* val, cud
 }
 
 int patchify(const uint8_t* img, int B, int S, int p, const float* mean, const float* stdv, void* out, int k_pad,
-             cudaStream_t s) {
+             cudaStream_t s, int win) {
   FF_REQUIRE(img && out && mean && stdv, "ff_patchify: NULL pointer");
   FF_REQUIRE(p >= 1 && S % p == 0 && k_pad >= p * p * 3, "ff_patchify: bad geometry S=%d p=%d k_pad=%d", S, p, k_pad);
+  FF_REQUIRE(win >= 0 && (win == 0 || (S / p) % win == 0), "ff_patchify: window %d does not tile the %d-patch grid",
+             win, S / p);
   if (B == 0) return FF_OK;
   const int64_t total = static_cast<int64_t>(B) * (S / p) * (S / p) * k_pad;
   const int grid = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 16));
   patchify_kernel<<<grid, 256, 0, s>>>(img, B, S, p, mean[0], mean[1], mean[2], 1.f / stdv[0], 1.f / stdv[1],
-                                       1.f / stdv[2], static_cast<__half*>(out), k_pad);
+                                       1.f / stdv[2], static_cast<__half*>(out), k_pad, win);
   return check_launch("patchify_kernel");
 }
 
@@ -213,11 +232,12 @@ int fill_cls(const void* cls, void* x, int B, int tokens, int dim, cudaStream_t 
 }
 
 int layernorm(const void* x, int64_t stride, const float* g, const float* b, float eps, int rows, int cols, void* out,
-              cudaStream_t s) {
+              cudaStream_t s, const void* pos, int period) {
   FF_REQUIRE(x && g && b && out && cols >= 1 && stride >= cols, "ff_layernorm: bad arguments");
+  FF_REQUIRE(pos == nullptr || period >= 1, "ff_layernorm: position rows need a period");
   if (rows == 0) return FF_OK;
   layernorm_kernel<<<(rows + 7) / 8, 256, 0, s>>>(static_cast<const __half*>(x), stride, g, b, eps, rows, cols,
-                                                  static_cast<__half*>(out));
+                                                  static_cast<__half*>(out), static_cast<const __half*>(pos), period);
   return check_launch("layernorm_kernel");
 }
 
@@ -230,6 +250,17 @@ extern "C" int ff_patchify(const uint8_t* images, int B, int image_size, int pat
 
 extern "C" int ff_fill_cls(const uint16_t* cls_row, uint16_t* x, int B, int tokens, int dim, void* stream) {
   return ff::fill_cls(cls_row, x, B, tokens, dim, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ff_patchify_windowed(const uint8_t* images, int B, int image_size, int patch, const float* mean3,
+                                    const float* std3, uint16_t* patches, int k_pad, int window, void* stream) {
+  return ff::patchify(images, B, image_size, patch, mean3, std3, patches, k_pad, static_cast<cudaStream_t>(stream),
+                      window);
+}
+
+extern "C" int ff_layernorm_pos(const uint16_t* x, int64_t row_stride, const float* gamma, const float* beta, float eps,
+                                int rows, int cols, const uint16_t* pos, int period, uint16_t* out, void* stream) {
+  return ff::layernorm(x, row_stride, gamma, beta, eps, rows, cols, out, static_cast<cudaStream_t>(stream), pos, period);
 }
 
 extern "C" int ff_layernorm(const uint16_t* x, int64_t row_stride, const float* gamma, const float* beta, float eps,

@@ -273,6 +273,83 @@ int slot_launch(const float* q, int64_t q_stride, const float* bias, const __hal
   return check_launch("slot_attend_kernel");
 }
 
+// PixAI attention-pool head (foidfinder/backends/cuda/reference.py:133-140): one learned query per head
+// attends over all tokens of an image. One CTA per (head, image); each quarter-warp (8 lanes x 8 dims =
+// one 128-byte key/value row) walks a share of the tokens with its own online softmax, four rows in
+// flight, and the 40 partial (max, sum, output) triples are merged through shared memory.
+constexpr int kPqThreads = 320;
+__global__ void __launch_bounds__(kPqThreads) pool_query_kernel(const float* __restrict__ q, const __half* __restrict__ kv,
+                                                               int tokens, int dim, __half* __restrict__ out) {
+  constexpr int HD = 64, NQ = kPqThreads / 8, UNR = 4;
+  __shared__ float part_m[NQ], part_l[NQ];
+  __shared__ float part_o[NQ][HD];
+  const int h = blockIdx.x, b = blockIdx.y, t = threadIdx.x, qw = t >> 3, ql = t & 7;
+  const unsigned qmask = 0xFFu << (t & 24);
+  float qr[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) qr[e] = q[h * HD + 8 * ql + e] * 1.4426950408889634f;  // log2 units
+  const size_t row0 = static_cast<size_t>(b) * tokens;
+  float m = -INFINITY, l = 0.f, o[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) o[e] = 0.f;
+  for (int k0 = qw; k0 < tokens; k0 += NQ * UNR) {
+    uint4 kr[UNR], vr[UNR];
+#pragma unroll
+    for (int i = 0; i < UNR; ++i) {
+      const int key = k0 + i * NQ;
+      if (key < tokens) {
+        const __half* base = kv + (row0 + key) * 2 * dim + h * HD;
+        kr[i] = __ldg(reinterpret_cast<const uint4*>(base) + ql);
+        vr[i] = __ldg(reinterpret_cast<const uint4*>(base + dim) + ql);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < UNR; ++i) {
+      if (k0 + i * NQ >= tokens) break;  // uniform within the quarter-warp
+      const uint32_t kw[4] = {kr[i].x, kr[i].y, kr[i].z, kr[i].w};
+      float sc = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = unpack_half2(kw[e]);
+        sc = fmaf(qr[2 * e], f.x, fmaf(qr[2 * e + 1], f.y, sc));
+      }
+      sc += __shfl_xor_sync(qmask, sc, 1, 8);
+      sc += __shfl_xor_sync(qmask, sc, 2, 8);
+      sc += __shfl_xor_sync(qmask, sc, 4, 8);
+      const float m_new = fmaxf(m, sc);
+      const float corr = ex2_approx(m - m_new);
+      const float pk = ex2_approx(sc - m_new);
+      m = m_new;
+      l = l * corr + pk;
+      const uint32_t vw[4] = {vr[i].x, vr[i].y, vr[i].z, vr[i].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = unpack_half2(vw[e]);
+        o[2 * e] = fmaf(pk, f.x, o[2 * e] * corr);
+        o[2 * e + 1] = fmaf(pk, f.y, o[2 * e + 1] * corr);
+      }
+    }
+  }
+  if (ql == 0) {
+    part_m[qw] = m;
+    part_l[qw] = l;
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) part_o[qw][8 * ql + e] = o[e];
+  __syncthreads();
+  if (t < HD) {
+    float mm = -INFINITY;
+    for (int i = 0; i < NQ; ++i) mm = fmaxf(mm, part_m[i]);
+    float ll = 0.f, acc = 0.f;
+    for (int i = 0; i < NQ; ++i) {
+      const float w = part_m[i] == -INFINITY ? 0.f : ex2_approx(part_m[i] - mm);
+      ll = fmaf(part_l[i], w, ll);
+      acc = fmaf(part_o[i][t], w, acc);
+    }
+    out[static_cast<size_t>(b) * dim + h * HD + t] = __float2half_rn(acc / ll);
+  }
+}
+
 template <int HD>
 int slot_dispatch(int M, const float* q, int64_t q_stride, const float* bias, const __half* kv, int B, int tokens,
                   int dim, int heads, float* z, float* mass, cudaStream_t s) {
@@ -299,6 +376,15 @@ int slot_attend(const float* q, int64_t q_img_stride, const float* bias, int M, 
   }
   set_error("pool: head dim %d (supported: 48, 64)", dim / heads);
   return FF_ERR_INVALID_ARGUMENT;
+}
+
+int pool_query_attention(const float* q, const void* kv, int B, int tokens, int heads, void* out, cudaStream_t s) {
+  FF_REQUIRE(q && kv && out && heads >= 1 && tokens >= 1, "pool query: bad arguments");
+  FF_REQUIRE(aligned16(kv), "pool query: key/value must be 16-byte aligned");
+  if (B == 0) return FF_OK;
+  pool_query_kernel<<<dim3(heads, B), kPqThreads, 0, s>>>(q, static_cast<const __half*>(kv), tokens, heads * 64,
+                                                          static_cast<__half*>(out));
+  return check_launch("pool_query_kernel");
 }
 
 int pool_trunk(const float* z, int B, int coarse, int leaves, int dim, const float* trunk_w, const float* trunk_b,
@@ -407,6 +493,11 @@ int pool_run(const ff_model_config& c, const ff_model_weights& w, const __half* 
 }  // namespace ff
 
 using namespace ff;
+
+extern "C" int ff_pool_query_attention(const float* q, const uint16_t* kv, int B, int tokens, int heads,
+                                       uint16_t* out, void* stream) {
+  return pool_query_attention(q, kv, B, tokens, heads, out, static_cast<cudaStream_t>(stream));
+}
 
 extern "C" int64_t ff_tree_pool_workspace_bytes(const ff_model_config* cfg, int B) {
   if (cfg == nullptr || B < 1) return -1;

@@ -446,8 +446,11 @@ int rot_q8(const void* x, const float* g, const float* b, float eps, int rows, i
   FF_REQUIRE(aligned16(x) && (g == nullptr || (aligned16(g) && aligned16(b))), "ff_rot_q8: pointers must be 16-byte aligned");
   FF_REQUIRE((reinterpret_cast<uintptr_t>(out) & 7u) == 0, "ff_rot_q8: out must be 8-byte aligned");
   if (rows == 0) return FF_OK;
-  FF_REQUIRE(cols == 768 || cols == 1024 || cols == 2048 || cols == 2816 || cols == 4096,
-             "ff_rot_q8: %d columns is not one of 768, 1024, 2048, 2816, 4096", cols);
+  const bool standard = cols == 768 || cols == 1024 || cols == 2048 || cols == 2816 || cols == 4096;
+  if (!standard && g == nullptr && block == 128 && valid == cols && cols % 128 == 0)
+    return rot_q8_h128_wide(x, rows, cols, out, rs, s);  // e.g. PixAI's 4736-wide GELU hidden
+  FF_REQUIRE(standard, "ff_rot_q8: %d columns is not one of 768, 1024, 2048, 2816, 4096 (or, for H128 without a "
+             "LayerNorm, a multiple of 128)", cols);
   if (err == nullptr && g != nullptr) err = device_error_word();  // the LayerNorm kernel's bounded waits
   FF_REQUIRE(err != nullptr || g == nullptr, "ff_rot_q8: no device error word");
   const __half* xh = static_cast<const __half*>(x);
@@ -460,6 +463,90 @@ int rot_q8(const void* x, const float* g, const float* b, float eps, int rows, i
   }
   set_error("ff_rot_q8: %d columns is not one of 768, 1024, 2048, 2816, 4096", cols);
   return FF_ERR_INVALID_ARGUMENT;
+}
+
+// H128 rotation + per-row int8 for rows of any multiple of 128 columns without a LayerNorm (the PixAI GELU
+// hidden, 4736 = 37 x 128, foidfinder/backends/cuda/engine.py:158-159). One warp per row; each 256-column
+// chunk holds two whole 128-blocks (lanes 0-15 and 16-31, 8 columns each; a trailing 128-column block uses
+// lanes 0-15), so the transform is chunk-local: column bits 0-2 in registers, 3-6 by shuffles inside each
+// half-warp. The row maximum is needed before any code, and a whole wide row does not fit in registers, so
+// the row is transformed twice: once for the maximum, once to quantise (the second read hits L1/L2).
+__global__ void __launch_bounds__(256) rot_q8_wide_kernel(const __half* __restrict__ x, int rows, int cols,
+                                                          int8_t* __restrict__ out, float* __restrict__ row_scale) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const __half* xr = x + static_cast<size_t>(row) * cols;
+  const int nch = (cols + 255) / 256;
+  auto transform = [&](int i, float (&v)[8]) -> bool {  // false: this lane holds no columns of chunk i
+    const int c = i * 256 + lane * 8;
+    const bool have = c < cols;
+    if (have) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(xr + c));
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = unpack_half2(w[e]);
+        v[2 * e] = f.x;
+        v[2 * e + 1] = f.y;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = 0.f;
+    }
+#pragma unroll
+    for (int h = 1; h < 8; h <<= 1)
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (!(e & h)) {
+          const float a = v[e], b = v[e + h];
+          v[e] = a + b;
+          v[e + h] = a - b;
+        }
+#pragma unroll
+    for (int m = 1; m < 16; m <<= 1) {
+      const bool upper = lane & m;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float o = __shfl_xor_sync(0xffffffffu, v[e], m);
+        v[e] = upper ? o - v[e] : v[e] + o;
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] *= 0.08838834764831845f;  // 1 / sqrt(128)
+    return have;
+  };
+  float amax = 0.f;
+  for (int i = 0; i < nch; ++i) {
+    float v[8];
+    transform(i, v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[e]));
+  }
+  amax = warp_max(amax);
+  const float scale = fmaxf(amax, 1e-12f) / 127.f;
+  const float inv = 1.f / scale;
+  int8_t* orow = out + static_cast<size_t>(row) * cols;
+  for (int i = 0; i < nch; ++i) {
+    float v[8];
+    if (!transform(i, v)) continue;
+    uint32_t t[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) t[e] = __float_as_uint(__fadd_rn(__fmul_rn(v[e], inv), 12582912.f));
+    const uint32_t w0 = __byte_perm(__byte_perm(t[0], t[1], 0x0040), __byte_perm(t[2], t[3], 0x0040), 0x5410);
+    const uint32_t w1 = __byte_perm(__byte_perm(t[4], t[5], 0x0040), __byte_perm(t[6], t[7], 0x0040), 0x5410);
+    *reinterpret_cast<uint2*>(orow + i * 256 + lane * 8) = make_uint2(w0, w1);
+  }
+  if (lane == 0) row_scale[row] = scale;
+}
+
+int rot_q8_h128_wide(const void* x, int rows, int cols, int8_t* out, float* rs, cudaStream_t s) {
+  FF_REQUIRE(x && out && rs, "rot_q8 (wide): NULL pointer");
+  FF_REQUIRE(cols >= 128 && cols % 128 == 0, "rot_q8 (wide): %d columns is not a multiple of 128", cols);
+  FF_REQUIRE(aligned16(x) && (reinterpret_cast<uintptr_t>(out) & 7u) == 0, "rot_q8 (wide): alignment");
+  if (rows == 0) return FF_OK;
+  rot_q8_wide_kernel<<<(rows + 7) / 8, 256, 0, s>>>(static_cast<const __half*>(x), rows, cols, out, rs);
+  return check_launch("rot_q8_wide_kernel");
 }
 
 }  // namespace ff
@@ -476,5 +563,8 @@ extern "C" int ff_rot_q8_1024(const uint16_t* x, const float* gamma, const float
 }
 
 extern "C" int ff_rot_q8_h128(const uint16_t* x, int rows, int cols, int8_t* out, float* row_scale, void* stream) {
-  return ff::rot_q8(x, nullptr, nullptr, 0.f, rows, cols, cols, 128, out, row_scale, static_cast<cudaStream_t>(stream));
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cols == 768 || cols == 1024 || cols == 2048 || cols == 2816 || cols == 4096)
+    return ff::rot_q8(x, nullptr, nullptr, 0.f, rows, cols, cols, 128, out, row_scale, s);
+  return ff::rot_q8_h128_wide(x, rows, cols, out, row_scale, s);  // e.g. PixAI's 4736
 }

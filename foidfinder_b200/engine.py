@@ -46,9 +46,12 @@ def c_config(cfg: ModelConfig) -> _lib.ModelConfig:
     c.rot_block_dim, c.rot_block_hidden, c.topk, c.ln_eps = cfg.rot_block_dim, cfg.rot_block_hidden, cfg.topk, cfg.ln_eps
     c.mean = (C.c_float * 3)(*cfg.mean)
     c.std = (C.c_float * 3)(*cfg.std)
-    c.head_kind = _lib.HEAD_TREE if cfg.head == "tree" else _lib.HEAD_CLS
+    c.head_kind = {"cls": _lib.HEAD_CLS, "tree": _lib.HEAD_TREE, "pool": _lib.HEAD_POOL}[cfg.head]
     c.pool_heads, c.coarse_queries, c.leaf_queries, c.leaf_dim = (
         cfg.pool_heads, cfg.coarse_queries, cfg.leaf_queries, cfg.leaf_dim)
+    c.arch = _lib.ARCH_PIXAI if cfg.arch == "pixai" else _lib.ARCH_EVA02
+    c.window = cfg.window
+    c.global_blocks = sum(1 << i for i in cfg.global_blocks if i < 64)
     return c
 
 
@@ -71,21 +74,40 @@ _POOL_KEYS = {
     "leaf_b": "pool.leaf.bias",
 }
 
+_PIXAI_KEYS = {
+    "ln_pre_w": "ln_pre.weight",
+    "ln_pre_b": "ln_pre.bias",
+    "rope_cos_global": "rope_cos_global",
+    "rope_sin_global": "rope_sin_global",
+    "pool_norm_w": "pool.norm.weight",
+    "pool_norm_b": "pool.norm.bias",
+    "pool_kv_w": "pool.kv.weight",
+    "pool_kv_b": "pool.kv.bias",
+    "pool_pos": "pool.pos",
+    "pool_q": "pool.q",
+    "pool_proj_w": "pool.proj.weight",
+    "pool_proj_b": "pool.proj.bias",
+}
+
 
 def c_weights(cfg: ModelConfig, L: dict[str, torch.Tensor], layers) -> _lib.ModelWeights:
     """Device tensors in the engine format -> the C weight struct (pointers only; `L` must stay alive)."""
+    def ptr(key: str) -> int | None:
+        t = L.get(key)
+        return t.data_ptr() if t is not None else None
+
     for i in range(cfg.depth):
         for field, key in _LAYER_KEYS.items():
-            setattr(layers[i], field, L[f"blocks.{i}.{key}"].data_ptr())
+            setattr(layers[i], field, ptr(f"blocks.{i}.{key}"))
     mw = _lib.ModelWeights()
-    mw.patch_w, mw.pos_bias, mw.cls_row = L["patch_w"].data_ptr(), L["pos_bias"].data_ptr(), L["cls_row"].data_ptr()
-    mw.rope_cos, mw.rope_sin = L["rope_cos"].data_ptr(), L["rope_sin"].data_ptr()
+    mw.patch_w, mw.pos_bias, mw.cls_row = ptr("patch_w"), ptr("pos_bias"), ptr("cls_row")
+    mw.rope_cos, mw.rope_sin = ptr("rope_cos"), ptr("rope_sin")
     mw.layers = C.cast(layers, C.POINTER(_lib.LayerWeights))
-    mw.norm_w, mw.norm_b = L["norm.weight"].data_ptr(), L["norm.bias"].data_ptr()
-    mw.head_w, mw.head_b = L["head.weight"].data_ptr(), L["head.bias"].data_ptr()
-    if cfg.head == "tree":
-        for field, key in _POOL_KEYS.items():
-            setattr(mw, field, L[key].data_ptr())
+    mw.norm_w, mw.norm_b = ptr("norm.weight"), ptr("norm.bias")
+    mw.head_w, mw.head_b = ptr("head.weight"), ptr("head.bias")
+    extra = {"tree": _POOL_KEYS, "pool": _PIXAI_KEYS}.get(cfg.head, {})
+    for field, key in extra.items():
+        setattr(mw, field, ptr(key))
     return mw
 
 

@@ -11,12 +11,12 @@ import ctypes as C
 import torch
 
 from . import _lib
-from ._lib import EPI_BIAS, EPI_LOGITS, EPI_QKV_ROPE, EPI_RESIDUAL, EPI_S32, EPI_STEM, EPI_SWIGLU, check, lib
+from ._lib import EPI_BIAS, EPI_GELU, EPI_LOGITS, EPI_QKV_ROPE, EPI_RESIDUAL, EPI_S32, EPI_STEM, EPI_SWIGLU, check, lib
 
 __all__ = [
-    "EPI_QKV_ROPE", "EPI_RESIDUAL", "EPI_SWIGLU", "EPI_BIAS", "EPI_S32", "EPI_STEM", "EPI_LOGITS",
+    "EPI_QKV_ROPE", "EPI_RESIDUAL", "EPI_SWIGLU", "EPI_BIAS", "EPI_S32", "EPI_STEM", "EPI_LOGITS", "EPI_GELU",
     "gemm_s8", "gemm_f16", "rot_q8", "rot_q8_1024", "rot_q8_h128", "attention", "patchify", "fill_cls",
-    "layernorm", "topk", "tree_pool", "resize_pad",
+    "layernorm", "topk", "tree_pool", "resize_pad", "patchify_windowed", "layernorm_pos", "pool_query_attention",
 ]
 
 
@@ -244,3 +244,32 @@ def resize_pad(image: torch.Tensor, new_h: int, new_w: int, size: int, out: torc
         check(lib().ff_resize_pad(_ptr(image), h, w, new_h, new_w, size, flt, fill, _ptr(out), _ptr(ws), nbytes,
                                   _stream(image)), "resize_pad")
         torch.cuda.current_stream(image.device).synchronize()  # the workspace is freed on return
+
+
+def patchify_windowed(images: torch.Tensor, patch: int, mean, std, window: int, out: torch.Tensor) -> None:
+    """uint8 [B, S, S, 3] -> fp16 patch rows [B * (S/patch)^2, k_pad] in window order (window x window tiles)."""
+    _cuda(images, out)
+    B, S = images.shape[:2]
+    m = (C.c_float * 3)(*map(float, mean))
+    s = (C.c_float * 3)(*map(float, std))
+    with torch.cuda.device(images.device):
+        check(lib().ff_patchify_windowed(_ptr(images), B, S, patch, m, s, _ptr(out), out.shape[1], window,
+                                         _stream(images)), "patchify_windowed")
+
+
+def layernorm_pos(x: torch.Tensor, gamma, beta, eps: float, pos: torch.Tensor, out: torch.Tensor) -> None:
+    """LayerNorm of fp16 rows to fp16, then + pos[row % pos.shape[0]] in fp16."""
+    _cuda(x, gamma, beta, pos, out)
+    rows, cols = x.shape
+    with torch.cuda.device(x.device):
+        check(lib().ff_layernorm_pos(_ptr(x), cols, _ptr(gamma), _ptr(beta), eps, rows, cols, _ptr(pos), pos.shape[0],
+                                     _ptr(out), _stream(x)), "layernorm_pos")
+
+
+def pool_query_attention(q: torch.Tensor, kv: torch.Tensor, B: int, tokens: int, out: torch.Tensor) -> None:
+    """q [heads * 64] f32 (scaled), kv [B * tokens, 2 * dim] fp16 -> out [B, dim] fp16."""
+    _cuda(q, kv, out)
+    heads = q.numel() // 64
+    with torch.cuda.device(kv.device):
+        check(lib().ff_pool_query_attention(_ptr(q), _ptr(kv), B, tokens, heads, _ptr(out), _stream(kv)),
+              "pool_query_attention")

@@ -1,4 +1,4 @@
-"""Checkpoint handling: synthetic EVA02 weights, RoPE tables, and the int8 conversion the kernels read.
+"""Checkpoint handling: synthetic EVA02 and PixAI weights, RoPE tables, and the int8 conversion the kernels read.
 
 `convert` plays the role of the reference's `convert_checkpoint` (foidfinder/backends/cuda/engine.py:49-62):
 each block linear becomes `<name>.qweight` (int8, W' = W · blockdiag(H_n)), `<name>.wscale` (f32 per
@@ -203,7 +203,145 @@ def convert(raw: dict[str, torch.Tensor], cfg: ModelConfig, device: str | torch.
 
 def synthetic(cfg: ModelConfig, seed: int = 0, device: str | torch.device = "cuda") -> dict[str, torch.Tensor]:
     """Random-init model converted to the engine format, generated on `device`."""
+    if cfg.arch == "pixai":
+        return convert_pixai(pixai_random_raw(cfg, seed, device), cfg, device)
     return convert(random_raw(cfg, seed, device), cfg, device)
+
+
+# ---------------------------------------------------------------- PixAI Tagger v1.0
+
+
+def window_order(grid: int, window: int) -> torch.Tensor:
+    """Position i of the window-ordered token sequence -> its row-major grid index: windows row-major, the
+    window's patches row-major inside (foidfinder/backends/cuda/reference.py:21-24)."""
+    nw = grid // window
+    wr, wc, r, c = torch.meshgrid(*(torch.arange(n) for n in (nw, nw, window, window)), indexing="ij")
+    return ((wr * window + r) * grid + wc * window + c).reshape(-1)
+
+
+def axial_rope(end: int, scale: float, head_dim: int = 64) -> tuple[torch.Tensor, torch.Tensor]:
+    """PixAI's axial 2-D RoPE (reference.py:27-34): for position t of an end x end grid, the head_dim/4
+    frequencies times x = (t % end) * scale, then times y = (t // end) * scale. cos/sin [end^2, head_dim/2] f32."""
+    freqs = 1.0 / (10000.0 ** (torch.arange(0, head_dim, 4)[: head_dim // 4].float() / head_dim))
+    t = torch.arange(end * end, dtype=torch.float32)
+    tx = (t % end) * scale
+    ty = torch.div(t, end, rounding_mode="floor") * scale
+    ang = torch.cat([torch.outer(tx, freqs), torch.outer(ty, freqs)], dim=-1)
+    return torch.cos(ang), torch.sin(ang)
+
+
+def pixai_random_raw(cfg: ModelConfig, seed: int = 0, device: str | torch.device = "cpu",
+                     pre_grid: int | None = None) -> dict[str, torch.Tensor]:
+    """Seeded random-init weights under the official PixAI checkpoint's names and shapes (the tensors
+    reference.py:68-98 reads). Linear weights, biases and embeddings ~ N(0, 0.02), LayerNorm weights
+    1 + N(0, 0.02); the pool's learned query ~ N(0, 1) so its softmax is not uniform. pre_grid: the
+    pretraining grid of pos_embed (24 for the real checkpoint; it must divide the grid)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    D, H, G, p = cfg.dim, cfg.mlp_hidden, cfg.grid, cfg.patch
+    pre = pre_grid or (24 if G % 24 == 0 else G)
+
+    def n(*shape, std=0.02):
+        return torch.randn(*shape, generator=g, device=device) * std
+
+    raw = {
+        "patch_embed.proj.weight": n(D, 3, p, p),
+        "pos_embed": n(1, 1 + pre * pre, D),
+        "ln_pre.weight": 1.0 + n(D),
+        "ln_pre.bias": n(D),
+        "head_pool.norm.weight": 1.0 + n(D),
+        "head_pool.norm.bias": n(D),
+        "head_pool.pos_embed": n(cfg.patches, D),
+        "head_pool.q": n(1, 1, D, std=1.0),
+        "head_pool.kv.weight": n(2 * D, D),
+        "head_pool.kv.bias": n(2 * D),
+        "head_pool.proj.weight": n(D, D),
+        "head_pool.proj.bias": n(D),
+        "head.weight": n(cfg.num_tags, D),
+        "head.bias": n(cfg.num_tags),
+    }
+    for i in range(cfg.depth):
+        b = f"blocks.{i}."
+        raw.update({
+            b + "norm1.weight": 1.0 + n(D), b + "norm1.bias": n(D),
+            b + "attn.qkv.weight": n(3 * D, D), b + "attn.qkv.bias": n(3 * D),
+            b + "attn.proj.weight": n(D, D), b + "attn.proj.bias": n(D),
+            b + "norm2.weight": 1.0 + n(D), b + "norm2.bias": n(D),
+            b + "mlp.fc1.weight": n(H, D), b + "mlp.fc1.bias": n(H),
+            b + "mlp.fc2.weight": n(D, H), b + "mlp.fc2.bias": n(D),
+        })
+    return raw
+
+
+def convert_pixai(raw: dict[str, torch.Tensor], cfg: ModelConfig,
+                  device: str | torch.device | None = None) -> dict[str, torch.Tensor]:
+    """Official PixAI fp32 checkpoint -> the engine format.
+
+    Block linears as `convert_checkpoint` (foidfinder/backends/cuda/engine.py:49-62): W' = W · blockdiag(H)
+    (H1024 for qkv, proj, fc1; H128 for fc2), per-output-channel int8, f32 bias; the attention scale
+    1/sqrt(64) of F.scaled_dot_product_attention (reference.py:125) is folded into the q rows and bias (a
+    power of two, so the codes are those of the unscaled rows). The stem and tables follow
+    PixAITorch.__init__ (reference.py:70-98): patch weight in (kh, kw, c) column order, the pretraining
+    position embedding tiled over the grid and put in window order, window and global RoPE tables (the
+    global one at positions scaled by window / grid, window-ordered), stored angle-major [32, n]; the pool's
+    position embedding in window order and its query carrying the 1/8 scale. The patch embedding's bias, if
+    the checkpoint has one, is not used — the reference's stem has none (reference.py:112)."""
+    dev = torch.device(device) if device is not None else raw["pos_embed"].device
+    D, G, L, win = cfg.dim, cfg.grid, cfg.patches, cfg.window
+    perm = window_order(G, win).to(raw["pos_embed"].device)
+    out: dict[str, torch.Tensor] = {}
+
+    def put(name: str, t: torch.Tensor) -> None:
+        out[name] = t.to(dev).contiguous()
+
+    pw = torch.zeros(D, cfg.k_pad, device=perm.device)
+    pw[:, : cfg.k_patch] = raw["patch_embed.proj.weight"].float().permute(0, 2, 3, 1).reshape(D, -1)
+    put("patch_w", pw.half())
+    pos = raw["pos_embed"].float()[0, 1:]
+    pre = math.isqrt(pos.shape[0])
+    put("pos_bias", pos.reshape(pre, pre, D).repeat(G // pre, G // pre, 1).reshape(L, D)[perm])
+    put("ln_pre.weight", raw["ln_pre.weight"].float())
+    put("ln_pre.bias", raw["ln_pre.bias"].float())
+    cw, sw = axial_rope(win, 1.0, cfg.head_dim)
+    cg, sg = axial_rope(G, win / G, cfg.head_dim)
+    put("rope_cos", cw.t())
+    put("rope_sin", sw.t())
+    put("rope_cos_global", cg[perm.cpu()].t())
+    put("rope_sin_global", sg[perm.cpu()].t())
+    scale = cfg.head_dim**-0.5
+    put("pool.norm.weight", raw["head_pool.norm.weight"].float())
+    put("pool.norm.bias", raw["head_pool.norm.bias"].float())
+    put("pool.pos", raw["head_pool.pos_embed"].float()[perm].half())
+    put("pool.q", raw["head_pool.q"].float().reshape(D) * scale)
+    put("pool.kv.weight", raw["head_pool.kv.weight"].half())
+    put("pool.kv.bias", raw["head_pool.kv.bias"].float())
+    put("pool.proj.weight", raw["head_pool.proj.weight"].half())
+    put("pool.proj.bias", raw["head_pool.proj.bias"].float())
+    hw = torch.zeros(cfg.num_tags_pad, D, device=perm.device)
+    hw[: cfg.num_tags] = raw["head.weight"].float()
+    hb = torch.zeros(cfg.num_tags_pad, device=perm.device)
+    hb[: cfg.num_tags] = raw["head.bias"].float()
+    put("head.weight", hw.half())
+    put("head.bias", hb)
+    for i in range(cfg.depth):
+        p = f"blocks.{i}."
+        for n in ("norm1", "norm2"):
+            put(p + n + ".weight", raw[p + n + ".weight"].float())
+            put(p + n + ".bias", raw[p + n + ".bias"].float())
+        qkv_w, qkv_b = raw[p + "attn.qkv.weight"].float().clone(), raw[p + "attn.qkv.bias"].float().clone()
+        qkv_w[:D] *= scale
+        qkv_b[:D] *= scale
+        lin = {
+            "qkv": (qkv_w, qkv_b, cfg.rot_block_dim),
+            "proj": (raw[p + "attn.proj.weight"].float(), raw[p + "attn.proj.bias"].float(), cfg.rot_block_dim),
+            "fc1": (raw[p + "mlp.fc1.weight"].float(), raw[p + "mlp.fc1.bias"].float(), cfg.rot_block_dim),
+            "fc2": (raw[p + "mlp.fc2.weight"].float(), raw[p + "mlp.fc2.bias"].float(), cfg.rot_block_hidden),
+        }
+        for name, (w, b, block) in lin.items():
+            q, s = quantize_rows_int8(fwht_rows(w, block))
+            put(f"{p}{name}.qweight", q)
+            put(f"{p}{name}.wscale", s)
+            put(f"{p}{name}.bias", b.contiguous())
+    return out
 
 
 def from_folded(folded: dict, cfg: ModelConfig, device: str | torch.device = "cpu") -> dict[str, torch.Tensor]:

@@ -45,6 +45,7 @@ int ff_device_error(int device, int* code, int clear);
 #define FF_EPI_QKV_ROPE 0 /* fp16 out [M, N]; 2-D RoPE on columns [0, rope_cols) */
 #define FF_EPI_RESIDUAL 1 /* fp16 out [M, N] = fp16(out + fp16(y)) (the residual stream) */
 #define FF_EPI_SWIGLU 3   /* W rows interleaved [gate 64 | up 64]; fp16 out [M, N/2] = silu(gate) * up */
+#define FF_EPI_GELU 2     /* fp16 out [M, N] = gelu_tanh(y) (PixAI fc1, csrc/common.cuh:50-56) */
 #define FF_EPI_BIAS 4     /* fp16 out [M, N] = y */
 #define FF_EPI_S32 5      /* int32 out [M, N] = raw accumulators */
 
@@ -66,7 +67,9 @@ int ff_gemm_s8(const int8_t* A, const int8_t* W, const float* row_scale, const f
 /*
  * fp16 GEMM on tcgen05 with f32 accumulation, for the stem and the tag head.
  *   FF_EPI_STEM:   A = patches [M = images * patches, K] fp16, W [N = dim, K] fp16;
- *                  x[(m / patches) * tokens + 1 + m % patches, n] = fp16(acc + pos_bias[m % patches, n]).
+ *                  x[(m / patches) * tokens + (tokens - patches) + m % patches, n] = fp16(acc + pos_bias[m % patches, n]);
+ *                  tokens = patches + 1 leaves row 0 of each image to the class token, tokens = patches (PixAI)
+ *                  does not.
  *   FF_EPI_LOGITS: A [M, K] fp16, W [N, K] fp16; out[m, n] = acc + bias[n] (f32) for n < n_valid,
  *                  out row stride ldo.
  *   FF_EPI_BIAS:   A [M, K] fp16, W [N, K] fp16; out[m, n] = fp16(acc + bias[n]), out row stride ldo
@@ -168,10 +171,21 @@ typedef struct ff_model_config {
   int coarse_queries; /* 6 */
   int leaf_queries;   /* 18, a multiple of coarse_queries */
   int leaf_dim;       /* 64 */
+  /* Architecture. FF_ARCH_EVA02: class token, SwiGLU with the hidden LayerNorm, every block global.
+   * FF_ARCH_PIXAI: PixAI Tagger v1.0 (foidfinder/backends/cuda/reference.py:109-140): no class token, tokens
+   * in window order, ln_pre after the stem, GELU MLP (mlp_hidden == mlp_hidden_pad, H128 on the hidden),
+   * window x window attention except in the blocks whose bit is set in global_blocks, head_kind
+   * FF_HEAD_POOL. */
+  int arch;
+  int window;                      /* window size in patches (PixAI: 24); the grid must be a multiple */
+  unsigned long long global_blocks; /* bit i: block i attends over the whole image (PixAI: 7, 15, 23, 31) */
 } ff_model_config;
 
 #define FF_HEAD_CLS 0
 #define FF_HEAD_TREE 1
+#define FF_HEAD_POOL 2 /* PixAI: LN + pos -> kv -> one learned query per head -> proj (reference.py:133-140) */
+#define FF_ARCH_EVA02 0
+#define FF_ARCH_PIXAI 1
 
 typedef struct ff_layer_weights {
   const float *norm1_w, *norm1_b;
@@ -196,7 +210,8 @@ typedef struct ff_model_weights {
   const float *norm_w, *norm_b;     /* final LayerNorm */
   const uint16_t* head_w;           /* [num_tags_pad, dim] (CLS) or [num_tags_pad, leaf_queries * leaf_dim] fp16 */
   const float* head_b;              /* [num_tags_pad] */
-  /* FF_HEAD_TREE only (NULL otherwise); layout of foidfinder/haruka.py:fold, f32 unless noted. */
+  /* FF_HEAD_TREE (and, for pool_norm_* and pool_kv_*, FF_HEAD_POOL, where the key rows are not pre-scaled)
+   * only, NULL otherwise; layout of foidfinder/haruka.py:fold, f32 unless noted. */
   const float *pool_norm_w, *pool_norm_b;     /* [dim] */
   const uint16_t* pool_kv_w;                  /* [2*dim, dim] fp16, key rows pre-scaled by head_dim^-0.5 */
   const float* pool_kv_b;                     /* [2*dim] */
@@ -206,6 +221,15 @@ typedef struct ff_model_weights {
   const float *child_q_norm_w, *child_q_norm_b;
   const float *leaf_norm_w, *leaf_norm_b;
   const float *leaf_w, *leaf_b;               /* [leaves, dim, leaf_dim], [leaves, leaf_dim] */
+  /* FF_ARCH_PIXAI only (NULL otherwise). cls_row, norm_w/b and the layers' mlp_norm_w/b are unused; fc1_w is
+   * [hidden, dim] in the checkpoint's row order with the GELU in the epilogue; rope_cos/sin hold the
+   * window table [32, window^2] and pos_bias the window-ordered position embedding [patches, dim]. */
+  const float *ln_pre_w, *ln_pre_b;                /* [dim] */
+  const float *rope_cos_global, *rope_sin_global;  /* [32, patches], angle-major, window order */
+  const uint16_t* pool_pos;                        /* [patches, dim] fp16, window order */
+  const float* pool_q;                             /* [dim], the 1/8 attention scale folded in */
+  const uint16_t* pool_proj_w;                     /* [dim, dim] fp16 */
+  const float* pool_proj_b;                        /* [dim] */
 } ff_model_weights;
 
 /*
@@ -220,6 +244,20 @@ typedef struct ff_model_weights {
 int ff_tree_pool(const ff_model_config* cfg, const struct ff_model_weights* w, const uint16_t* x, int B,
                  void* workspace, int64_t workspace_bytes, uint16_t* leaf_out, void* stream);
 int64_t ff_tree_pool_workspace_bytes(const ff_model_config* cfg, int B);
+
+/* Window-ordered patch rows (window > 0: the grid in window x window tiles, windows row-major, patches
+ * row-major inside; foidfinder/backends/cuda/reference.py:21-24). window = 0 is ff_patchify. */
+int ff_patchify_windowed(const uint8_t* images, int B, int image_size, int patch, const float* mean3, const float* std3,
+                         uint16_t* patches, int k_pad, int window, void* stream);
+/* LayerNorm (f32 statistics) to fp16, then + fp16 pos[row % period] in fp16 (the PixAI pool's
+ * LN + position embedding, reference.py:135). */
+int ff_layernorm_pos(const uint16_t* x, int64_t row_stride, const float* gamma, const float* beta, float eps, int rows,
+                     int cols, const uint16_t* pos, int period, uint16_t* out, void* stream);
+/* One learned query per head over all tokens of each image (the PixAI attention pool, reference.py:136-138):
+ * q [heads * 64] f32 with the 1/8 scale folded in, kv [B * tokens, 2 * heads * 64] fp16 (keys | values)
+ * -> out [B, heads * 64] fp16, f32 softmax. */
+int ff_pool_query_attention(const float* q, const uint16_t* kv, int B, int tokens, int heads, uint16_t* out,
+                            void* stream);
 
 /* ---------------------------------------------------------------- preprocessing */
 #define FF_RESAMPLE_BILINEAR 0

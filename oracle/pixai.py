@@ -1,7 +1,11 @@
 """Oracle restatement of the reference's PixAI layout helpers (CPU, torch) — test infrastructure only.
 
-- `axial_rope`   foidfinder/backends/cuda/reference.py:27-34 (x bands then y bands, fp32)
+- `window_perm`  foidfinder/backends/cuda/reference.py:21-24 (window order -> row-major grid index)
+- `axial_rope`   reference.py:27-34 (x bands then y bands, fp32)
 - `apply_rope`   reference.py:37-41 (interleaved pairs, fp32, cast back)
+- `gelu_tanh`    foidfinder/backends/cuda/csrc/common.cuh:55-56 (the fc1 epilogue's tanh GELU)
+- `forward_fp32` reference.py:109-140 (PixAITorch.forward + pool_head, f32, official checkpoint names)
+- `forward_int8` foidfinder/backends/cuda/engine.py:142-161 (PixAICuda._forward: int8 blocks, fp16 storage)
 """
 
 from __future__ import annotations
@@ -9,6 +13,20 @@ from __future__ import annotations
 import torch
 
 D = 64
+
+
+def window_perm(grid: int, window: int) -> torch.Tensor:
+    """Index i of the window-ordered sequence -> row-major grid index: windows row-major, then the
+    window's patches row-major (reference.py:21-24 with grid 72, window 24)."""
+    nw = grid // window
+    wr, wc, r, c = torch.meshgrid(*(torch.arange(n) for n in (nw, nw, window, window)), indexing="ij")
+    return ((wr * window + r) * grid + wc * window + c).reshape(-1)
+
+
+def gelu_tanh(x: torch.Tensor) -> torch.Tensor:
+    """0.5 x (1 + tanh(0.7978845608 (x + 0.044715 x^3))) in f32."""
+    x = x.float()
+    return 0.5 * x * (1.0 + torch.tanh(0.7978845608 * (x + 0.044715 * x * x * x)))
 
 
 def axial_rope(end: int, scale: float) -> tuple[torch.Tensor, torch.Tensor]:
@@ -25,3 +43,132 @@ def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.T
     x0, x1 = xf[..., 0], xf[..., 1]
     return torch.stack([x0 * cos - x1 * sin, x0 * sin + x1 * cos], dim=-1).flatten(-2).to(x.dtype)
 
+
+
+# ---------------------------------------------------------------- whole model
+
+
+def patch_rows(images: torch.Tensor, cfg) -> torch.Tensor:
+    """uint8 [B, S, S, 3] -> normalised f32 patches [B, L, p*p*3] in window order, (kh, kw, c) columns
+    (PixAITorch.patchify, reference.py:103-107, on the normalised pixels of preprocess.py:30)."""
+    from . import eva02 as E
+
+    return E.patchify(images, cfg.patch, cfg.mean, cfg.std)[:, window_perm(cfg.grid, cfg.window)]
+
+
+def _window_tables(cfg) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """(window cos, sin) [window^2, 32] and (global cos, sin) [L, 32] in window order (reference.py:95-98)."""
+    cw, sw = axial_rope(cfg.window, 1.0)
+    cg, sg = axial_rope(cfg.grid, cfg.window / cfg.grid)
+    perm = window_perm(cfg.grid, cfg.window)
+    return cw, sw, cg[perm], sg[perm]
+
+
+def _sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float) -> torch.Tensor:
+    return torch.softmax((q @ k.transpose(-1, -2)) * scale, dim=-1) @ v
+
+
+def forward_fp32(raw: dict[str, torch.Tensor], cfg, images: torch.Tensor) -> torch.Tensor:
+    """PixAITorch.forward (reference.py:109-130) and pool_head (:132-140) in f32 on the official checkpoint
+    layout, from uint8 images -> logits [B, num_tags]. Erf GELU (F.gelu's default, reference.py:129)."""
+    from . import quant as Q
+
+    B, G, D, nh, L, win = images.shape[0], cfg.grid, cfg.dim, cfg.heads, cfg.patches, cfg.window
+    nw, eps = G // win, cfg.ln_eps
+    g = lambda k: raw[k].float()  # noqa: E731
+    perm = window_perm(G, win)
+    pw = g("patch_embed.proj.weight").permute(0, 2, 3, 1).reshape(D, -1)
+    pos = g("pos_embed")[0, 1:]
+    pre = int(round(pos.shape[0] ** 0.5))
+    pos = pos.reshape(pre, pre, D).repeat(G // pre, G // pre, 1).reshape(L, D)[perm]
+    x = (patch_rows(images, cfg) @ pw.t() + pos).reshape(B * L, D)
+    x = Q.layer_norm(x, g("ln_pre.weight"), g("ln_pre.bias"), eps)
+    cw, sw, cg, sg = _window_tables(cfg)
+    for i in range(cfg.depth):
+        p = f"blocks.{i}."
+        h = Q.layer_norm(x, g(p + "norm1.weight"), g(p + "norm1.bias"), eps)
+        qkv = h @ g(p + "attn.qkv.weight").t() + g(p + "attn.qkv.bias")
+        nb, n, cos, sin = (B, L, cg, sg) if cfg.is_global(i) else (B * nw * nw, win * win, cw, sw)
+        q, k, v = qkv.view(nb, n, 3, nh, D // nh).permute(2, 0, 3, 1, 4)
+        o = _sdpa(apply_rope(q, cos, sin), apply_rope(k, cos, sin), v, (D // nh) ** -0.5)
+        x = x + o.transpose(1, 2).reshape(B * L, D) @ g(p + "attn.proj.weight").t() + g(p + "attn.proj.bias")
+        h = Q.layer_norm(x, g(p + "norm2.weight"), g(p + "norm2.bias"), eps)
+        h = torch.nn.functional.gelu(h @ g(p + "mlp.fc1.weight").t() + g(p + "mlp.fc1.bias"))
+        x = x + h @ g(p + "mlp.fc2.weight").t() + g(p + "mlp.fc2.bias")
+    return pool_head_fp32(x.view(B, L, D), raw, cfg)
+
+
+def pool_head_fp32(x: torch.Tensor, raw: dict[str, torch.Tensor], cfg) -> torch.Tensor:
+    """PixAITorch.pool_head (reference.py:132-140) in f32: x [B, L, D] window-ordered -> logits."""
+    from . import quant as Q
+
+    B, L, D = x.shape
+    nh = cfg.heads
+    g = lambda k: raw[k].float()  # noqa: E731
+    h = Q.layer_norm(x, g("head_pool.norm.weight"), g("head_pool.norm.bias"), cfg.ln_eps)
+    h = h + g("head_pool.pos_embed")[window_perm(cfg.grid, cfg.window)]
+    k, v = (h @ g("head_pool.kv.weight").t() + g("head_pool.kv.bias")).view(B, L, 2, nh, D // nh).permute(2, 0, 3, 1, 4)
+    q = g("head_pool.q").reshape(1, nh, 1, D // nh).expand(B, nh, 1, D // nh)
+    o = _sdpa(q, k, v, (D // nh) ** -0.5).reshape(B, D)
+    o = o @ g("head_pool.proj.weight").t() + g("head_pool.proj.bias")
+    return o @ g("head.weight").t() + g("head.bias")
+
+
+def forward_int8(conv: dict[str, torch.Tensor], cfg, images: torch.Tensor, trace: list | None = None) -> torch.Tensor:
+    """The GPU engine's PixAI arithmetic on the CPU, from the converted checkpoint -> logits [B, num_tags].
+
+    PixAICuda._forward (foidfinder/backends/cuda/engine.py:142-161) step by step: fp16 stem (+ window-ordered
+    position embedding), ln_pre to fp16, then per block LN1+H1024+q8 -> QKV GEMM + RoPE (window table, or
+    the global one in the global blocks) -> attention per window / per image -> H1024+q8 -> proj + residual
+    -> LN2+H1024+q8 -> fc1 + tanh GELU (csrc/common.cuh:56) -> H128+q8 -> fc2 + residual, and the pool head
+    of reference.py:132-140 with fp16 storage between its steps. If `trace` is a list it receives one dict
+    per block (every stage's inputs and outputs) and a final dict (stem, pool stages, logits)."""
+    from . import eva02 as E
+    from . import quant as Q
+
+    conv = {k: v.cpu() for k, v in conv.items()}
+    B, L, D, nh, win = images.shape[0], cfg.patches, cfg.dim, cfg.heads, cfg.window
+    M, eps = B * L, cfg.ln_eps
+    patches = patch_rows(images, cfg).half()
+    x = (patches.float() @ conv["patch_w"].float()[:, : cfg.k_patch].t() + conv["pos_bias"].float()).half()
+    x_stem = x.reshape(M, D)
+    x = Q.layer_norm(x_stem.float(), conv["ln_pre.weight"], conv["ln_pre.bias"], eps).half()
+    x_pre = x
+    tables = {
+        False: (conv["rope_cos"].float().t(), conv["rope_sin"].float().t(), win * win),
+        True: (conv["rope_cos_global"].float().t(), conv["rope_sin_global"].float().t(), L),
+    }
+
+    def lin(a8, rs, name):
+        return Q.dequant(Q.gemm_s8_acc(a8, conv[name + ".qweight"]), rs, conv[name + ".wscale"], conv[name + ".bias"])
+
+    for i in range(cfg.depth):
+        p = f"blocks.{i}."
+        x_in = x
+        cos, sin, n = tables[cfg.is_global(i)]
+        a8, rs = Q.rot_q8(x, conv[p + "norm1.weight"], conv[p + "norm1.bias"], block=cfg.rot_block_dim, eps=eps)
+        qkv = Q.apply_rope_pairs(lin(a8, rs, p + "qkv"), cos, sin, torch.arange(M) % n, 2 * D).half()
+        o = E._attention(qkv, M // n, n, nh).half()
+        a8o, rso = Q.rot_q8(o, None, None, block=cfg.rot_block_dim)
+        x = E._residual(x, lin(a8o, rso, p + "proj"))
+        x_attn = x
+        a8m, rsm = Q.rot_q8(x, conv[p + "norm2.weight"], conv[p + "norm2.bias"], block=cfg.rot_block_dim, eps=eps)
+        h = gelu_tanh(lin(a8m, rsm, p + "fc1")).half()
+        a8h, rsh = Q.rot_q8(h, None, None, block=cfg.rot_block_hidden)
+        x = E._residual(x, lin(a8h, rsh, p + "fc2"))
+        if trace is not None:
+            trace.append(dict(x_in=x_in, a8=a8, rs=rs, qkv=qkv, o=o, a8o=a8o, rso=rso, x_attn=x_attn, a8m=a8m, rsm=rsm,
+                              h=h, a8h=a8h, rsh=rsh, x_out=x, seq=n))
+    xn = (Q.layer_norm(x.float(), conv["pool.norm.weight"], conv["pool.norm.bias"], eps).half().view(B, L, D)
+          + conv["pool.pos"]).view(M, D)
+    kv = (xn.float() @ conv["pool.kv.weight"].float().t() + conv["pool.kv.bias"]).half()
+    k = kv[:, :D].float().view(B, L, nh, D // nh).permute(0, 2, 1, 3)
+    v = kv[:, D:].float().view(B, L, nh, D // nh).permute(0, 2, 1, 3)
+    q = conv["pool.q"].float().view(1, nh, 1, D // nh)
+    att = _sdpa(q, k, v, 1.0).reshape(B, D).half()
+    z = (att.float() @ conv["pool.proj.weight"].float().t() + conv["pool.proj.bias"]).half()
+    logits = z.float() @ conv["head.weight"].float()[: cfg.num_tags].t() + conv["head.bias"][: cfg.num_tags]
+    if trace is not None:
+        trace.append(dict(patches=patches.reshape(M, -1), x_stem=x_stem, x_pre=x_pre, x_final=x, xn=xn, kv=kv,
+                          att=att, z=z, logits=logits))
+    return logits

@@ -17,7 +17,12 @@ What it records (inputs are seeded; every function is the reference's, unmodifie
   `MODEL` dict): the folded patch embedding (pixel normalisation inside the weights), the fused qkv with
   the q scale and zero k bias, and the tree-pool tensors (key rows scaled);
 - the model card's tree attention pool `MHAttnPool` (defined inside the `haruka` fixture of
-  `tests/test_haruka.py`, executed from its source text) on seeded tokens with the same checkpoint.
+  `tests/test_haruka.py`, executed from its source text) on seeded tokens with the same checkpoint;
+- `PixAITorch` of `foidfinder.backends.cuda.reference` (f32, CPU) on a seeded tiny PixAI checkpoint under
+  the official tensor names: the whole forward (window-ordered patchify, tiled position embedding, ln_pre,
+  window and global blocks with their RoPE tables, GELU MLP, attention-pool head) on seeded images, and
+  `pool_head` alone on seeded tokens. The module's shape constants are set to the tiny model (`PIXAI`)
+  for the call and restored after.
 """
 
 from __future__ import annotations
@@ -117,6 +122,24 @@ def main(ref_root: str) -> None:
     with torch.no_grad():
         out["tree_leaf"] = pool(torch.from_numpy(tree_input())).numpy()
 
+    # PixAI Tagger v1.0 (reference.py), shrunk through its module constants.
+    px = PIXAI
+    consts = {"S": px["S"], "P": px["P"], "C": px["C"], "H": px["H"], "DEPTH": px["DEPTH"], "WIN": px["WIN"],
+              "G": px["S"] // px["P"], "NW": px["S"] // px["P"] // px["WIN"], "L": (px["S"] // px["P"]) ** 2,
+              "LW": px["WIN"] ** 2, "GLOBAL": frozenset(px["GLOBAL"]), "PRE": px["PRE"]}
+    saved = {k: getattr(reference, k) for k in consts}
+    for k, v in consts.items():
+        setattr(reference, k, v)
+    try:
+        sd = {k: torch.from_numpy(v) for k, v in pixai_checkpoint().items()}
+        model = reference.PixAITorch(".", dtype=torch.float32, device="cpu", raw=sd)
+        with torch.no_grad():
+            out["pixai_logits"] = model(torch.from_numpy(pixai_pixels())).numpy()
+            out["pixai_pool_logits"] = model.pool_head(torch.from_numpy(pixai_pool_input())).numpy()
+    finally:
+        for k, v in saved.items():
+            setattr(reference, k, v)
+
     dst = Path(__file__).resolve().parent / "reference_vectors.npz"
     np.savez_compressed(dst, **out)
     print(f"wrote {dst} ({dst.stat().st_size} bytes, {len(out)} arrays)")
@@ -169,6 +192,60 @@ def fold_inputs() -> dict[str, np.ndarray]:
     for nm in ("norm1", "norm2"):
         sd[bb + f"blocks.0.{nm}.weight"], sd[bb + f"blocks.0.{nm}.bias"] = r(D), r(D)
     return sd
+
+
+PIXAI = {"S": 336, "P": 14, "C": 128, "H": 2, "DEPTH": 2, "WIN": 8, "GLOBAL": (1,), "PRE": 12, "hidden": 256,
+         "tags": 50, "images": 2}
+
+
+def pixai_checkpoint() -> dict[str, np.ndarray]:
+    """A seeded tiny PixAI checkpoint under the official names (the tensors reference.py:68-98 reads)."""
+    rng = np.random.default_rng(21)
+    px = PIXAI
+    C, Hd, p, L = px["C"], px["hidden"], px["P"], (px["S"] // px["P"]) ** 2
+
+    def r(*shape, std=0.02, base=0.0):
+        return (base + rng.standard_normal(shape) * std).astype(np.float32)
+
+    sd = {
+        "patch_embed.proj.weight": r(C, 3, p, p),
+        "pos_embed": r(1, 1 + px["PRE"] ** 2, C, std=0.1),
+        "ln_pre.weight": r(C, base=1.0), "ln_pre.bias": r(C),
+        "head_pool.norm.weight": r(C, base=1.0), "head_pool.norm.bias": r(C),
+        "head_pool.pos_embed": r(L, C, std=0.1), "head_pool.q": r(1, 1, C, std=1.0),
+        "head_pool.kv.weight": r(2 * C, C, std=0.1), "head_pool.kv.bias": r(2 * C),
+        "head_pool.proj.weight": r(C, C, std=0.1), "head_pool.proj.bias": r(C),
+        "head.weight": r(px["tags"], C, std=0.1), "head.bias": r(px["tags"]),
+    }
+    for i in range(px["DEPTH"]):
+        b = f"blocks.{i}."
+        sd.update({
+            b + "norm1.weight": r(C, base=1.0), b + "norm1.bias": r(C),
+            b + "attn.qkv.weight": r(3 * C, C, std=0.1), b + "attn.qkv.bias": r(3 * C),
+            b + "attn.proj.weight": r(C, C, std=0.1), b + "attn.proj.bias": r(C),
+            b + "norm2.weight": r(C, base=1.0), b + "norm2.bias": r(C),
+            b + "mlp.fc1.weight": r(Hd, C, std=0.1), b + "mlp.fc1.bias": r(Hd),
+            b + "mlp.fc2.weight": r(C, Hd, std=0.1), b + "mlp.fc2.bias": r(C),
+        })
+    return sd
+
+
+def pixai_images() -> np.ndarray:
+    """Seeded uint8 images [images, S, S, 3]."""
+    rng = np.random.default_rng(22)
+    return rng.integers(0, 256, (PIXAI["images"], PIXAI["S"], PIXAI["S"], 3), dtype=np.uint8)
+
+
+def pixai_pixels() -> np.ndarray:
+    """The images normalised as the engine's patchify does: (u8 * f32(1/255) - 0.5) * (1 / 0.5), f32."""
+    x = pixai_images().astype(np.float32) * np.float32(1.0 / 255.0)
+    return ((x - np.float32(0.5)) * np.float32(2.0)).astype(np.float32)
+
+
+def pixai_pool_input() -> np.ndarray:
+    """Seeded window-ordered tokens [images, L, C] for the pool head alone."""
+    rng = np.random.default_rng(23)
+    return rng.standard_normal((PIXAI["images"], (PIXAI["S"] // PIXAI["P"]) ** 2, PIXAI["C"])).astype(np.float32)
 
 
 if __name__ == "__main__":

@@ -129,3 +129,56 @@ def test_fold_matches_engine_patch_convention(gold):
     unfolded = norm @ w.T + b + sd["backbone.pos_embed"][0, 1:]
     folded = px.reshape(4, -1) @ gold["fold_out_patch_w"].T + gold["fold_out_patch_b"]
     np.testing.assert_allclose(folded, unfolded, rtol=1e-4, atol=1e-5)
+
+
+# ---------------------------------------------------------------- PixAI Tagger v1.0
+
+
+def _pixai_cfg():
+    from foidfinder_b200.config import PIXAI_1008
+
+    px = make_golden.PIXAI
+    return PIXAI_1008.with_(name="pixai-golden", image_size=px["S"], dim=px["C"], heads=px["H"], depth=px["DEPTH"],
+                            mlp_hidden=px["hidden"], num_tags=px["tags"], window=px["WIN"],
+                            global_blocks=tuple(px["GLOBAL"]), rot_block_dim=px["C"])
+
+
+def _pixai_raw():
+    return {k: torch.from_numpy(v) for k, v in make_golden.pixai_checkpoint().items()}
+
+
+def test_pixai_window_order_matches_reference_layout():
+    """The window order of reference.py:21-24 (windows row-major, patches row-major inside)."""
+    perm = P.window_perm(6, 3)
+    assert perm[:9].tolist() == [0, 1, 2, 6, 7, 8, 12, 13, 14]
+    assert perm[9:12].tolist() == [3, 4, 5]
+    assert torch.equal(W.window_order(72, 24), P.window_perm(72, 24))
+    assert torch.equal(torch.sort(P.window_perm(72, 24)).values, torch.arange(5184))
+
+
+def test_pixai_forward_fp32_matches_reference(gold):
+    """The oracle's f32 PixAI forward reproduces PixAITorch (reference.py:109-140) on the same checkpoint."""
+    cfg = _pixai_cfg()
+    imgs = torch.from_numpy(make_golden.pixai_images())
+    got = P.forward_fp32(_pixai_raw(), cfg, imgs)
+    np.testing.assert_allclose(got.numpy(), gold["pixai_logits"], atol=2e-5, rtol=1e-4)
+
+
+def test_pixai_pool_head_matches_reference(gold):
+    cfg = _pixai_cfg()
+    got = P.pool_head_fp32(torch.from_numpy(make_golden.pixai_pool_input()), _pixai_raw(), cfg)
+    np.testing.assert_allclose(got.numpy(), gold["pixai_pool_logits"], atol=2e-5, rtol=1e-4)
+
+
+def test_pixai_int8_pipeline_tracks_fp32(gold):
+    """The converted checkpoint through the int8 oracle (the engine's arithmetic) stays within the int8
+    pipeline's error of the reference's f32 logits and keeps their top tags."""
+    cfg = _pixai_cfg()
+    conv = W.convert_pixai(_pixai_raw(), cfg)
+    got = P.forward_int8(conv, cfg, torch.from_numpy(make_golden.pixai_images()))
+    ref = torch.from_numpy(gold["pixai_logits"])
+    err = (got - ref).abs().max().item()
+    assert err < 0.05 * ref.abs().max().item(), err
+    top = lambda t: set(torch.topk(t, 5).indices.tolist())  # noqa: E731
+    for b in range(ref.shape[0]):
+        assert len(top(got[b]) & top(ref[b])) >= 4
