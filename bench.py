@@ -14,6 +14,9 @@ memory and the device->host copy of logits and top-50. The roofline entry covers
 `--impl reference` times the reference's CPU path instead: the fp32 PyTorch forward of the same model
 (the oracle restatement of foidfinder/backends/cuda/reference.py:109-131 with the EVA02 block), on all
 host threads, one image per step; under torchrun only rank 0 runs it.
+
+`--config pixai-1008` runs the reference's own `cuda` workload instead (PixAI Tagger v1.0: 1008 px, 5184
+window-ordered tokens, 32 blocks, GELU 4736, attention-pool head; default batch 16), with the same keys.
 """
 
 from __future__ import annotations
@@ -35,6 +38,13 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "images/sec (1/2/4/8 B200) EVA02-L int8 bs64"
 UNIT = "images/s"
+DEFAULT_BATCH = {"pixai": 16, "eva02": 64}
+
+
+def metric_for(cfg, B: int) -> str:
+    if cfg.name == "eva02-l-448" and B == 64:
+        return METRIC
+    return f"images/sec (1/2/4/8 B200) {cfg.name} int8 bs{B}"
 
 
 def parse() -> argparse.Namespace:
@@ -42,7 +52,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--batch", type=int, default=64, help="images per GPU per step")
+    ap.add_argument("--batch", type=int, default=None, help="images per GPU per step (default 64; pixai-1008: 16)")
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--config", default="eva02-l-448")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -140,12 +150,17 @@ def profiled_traffic(kernel: str) -> int | None:
 
 def cpu_forward_timing(cfg, n_images: int, warmup: int = 1) -> tuple[float, int, str]:
     """Seconds per image of the fp32 CPU forward (oracle restatement), all host threads."""
-    from oracle.eva02 import forward_fp32
+    from foidfinder_b200.weights import pixai_random_raw, random_raw
 
-    from foidfinder_b200.weights import random_raw
+    if cfg.arch == "pixai":
+        from oracle.pixai import forward_fp32
 
+        raw = pixai_random_raw(cfg, seed=0, device="cpu")
+    else:
+        from oracle.eva02 import forward_fp32
+
+        raw = random_raw(cfg, seed=0, device="cpu")
     torch.set_num_threads(os.cpu_count() or 1)
-    raw = random_raw(cfg, seed=0, device="cpu")
     g = torch.Generator().manual_seed(1234)
     imgs = torch.randint(0, 256, (n_images + warmup, cfg.image_size, cfg.image_size, 3), generator=g, dtype=torch.uint8)
     with torch.no_grad():
@@ -160,9 +175,16 @@ def cpu_forward_timing(cfg, n_images: int, warmup: int = 1) -> tuple[float, int,
 
 
 def workload(cfg, B: int, world: int) -> dict:
+    if cfg.arch == "pixai":
+        desc = (f"{cfg.name} int8 forward (the reference's PixAICuda workload): {cfg.image_size}px, {cfg.tokens} "
+                f"window-ordered tokens, {cfg.depth} blocks ({cfg.window}x{cfg.window} windows, global blocks "
+                f"{list(cfg.global_blocks)}), dim {cfg.dim}, GELU {cfg.mlp_hidden}, attention-pool head, "
+                f"{cfg.num_tags} tags, top-{cfg.topk}")
+    else:
+        desc = (f"{cfg.name} int8 forward (BASELINE config 3): {cfg.image_size}px, {cfg.tokens} tokens, "
+                f"{cfg.depth} blocks, dim {cfg.dim}, SwiGLU {cfg.mlp_hidden}, {cfg.num_tags} tags, top-{cfg.topk}")
     return {
-        "workload": f"{cfg.name} int8 forward (BASELINE config 3): {cfg.image_size}px, {cfg.tokens} tokens, "
-        f"{cfg.depth} blocks, dim {cfg.dim}, SwiGLU {cfg.mlp_hidden}, {cfg.num_tags} tags, top-{cfg.topk}",
+        "workload": desc,
         "batch_per_gpu": B,
         "global_batch": B * world,
         "parallelism": f"dp{world} (images sharded by rank, no collective)",
@@ -178,11 +200,12 @@ def run_reference(args) -> None:
     from foidfinder_b200.config import CONFIGS
 
     cfg = CONFIGS[args.config]
+    B = args.batch or DEFAULT_BATCH[cfg.arch]
     sec, cores, _ = cpu_forward_timing(cfg, n_images=max(1, args.steps), warmup=max(1, min(args.warmup, 2)))
     value = 1.0 / sec
     line = {
         "impl": "reference",
-        "metric": METRIC,
+        "metric": metric_for(cfg, B),
         "value": value,
         "unit": UNIT,
         "n_gpus": args.gpus,
@@ -194,15 +217,15 @@ def run_reference(args) -> None:
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic: seeded uint8 images U[0,255], random-init N(0,0.02) weights",
-        "config": workload(cfg, args.batch, world),
+        "config": workload(cfg, B, world),
         "cpu_baseline": {
             "value": value,
             "unit": UNIT,
             "cores": cores,
             "kind": "port",
-            "sample": f"{args.steps} steps of 1 image each (a bounded sample of the {args.batch}-image step): fp32 "
-            "PyTorch CPU forward (oracle restatement of the reference's PixAITorch forward with the EVA02 block), "
-            "median step, on rank 0 only",
+            "sample": f"{args.steps} steps of 1 image each (a bounded sample of the {B}-image step): fp32 "
+            "PyTorch CPU forward (oracle restatement of the reference's PixAITorch forward"
+            + ("" if cfg.arch == "pixai" else " with the EVA02 block") + "), median step, on rank 0 only",
         },
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -223,7 +246,7 @@ def run_ours(args) -> None:
     from foidfinder_b200.engine import Engine
 
     cfg = CONFIGS[args.config]
-    B, K, W = args.batch, args.steps, max(args.warmup, 3)
+    B, K, W = args.batch or DEFAULT_BATCH[cfg.arch], args.steps, max(args.warmup, 3)
     eng = Engine(cfg, device=local, seed=0)
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     imgs = torch.randint(0, 256, (B, cfg.image_size, cfg.image_size, 3), generator=g, dtype=torch.uint8, device=dev)
@@ -310,7 +333,7 @@ def run_ours(args) -> None:
 
     total = world * B * K
     line = {
-        "metric": METRIC,
+        "metric": metric_for(cfg, B),
         "value": total / (dev_ms * 1e-3),
         "unit": UNIT,
         "n_gpus": world,
@@ -328,15 +351,16 @@ def run_ours(args) -> None:
         "gpu_launches": eng.launches_per_forward * K,
         "roofline": {
             "bound": "tensor",
-            "kernel": "gemm_tc_kernel (tcgen05 kind::i8; qkv, proj, gate|up, down)",
+            "kernel": "gemm_tc_kernel (tcgen05 kind::i8; qkv, proj, " + ("fc1" if cfg.arch == "pixai" else "gate|up")
+            + ", down)",
             "achieved": achieved,
             "peak": peak,
             "unit": "TFLOP/s",
             "frac": achieved / peak,
-            "traffic": profiled_traffic("gemm_tc_kernel int8"),
+            "traffic": profiled_traffic("gemm_tc_kernel int8") if cfg.name == "eva02-l-448" and B == 64 else None,
             "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, averaged over the 96 "
             "int8 GEMM launches of one bs64 forward (profiles/launches_eva02l_bs64.md); algorithmic bytes per "
-            "launch average 427 MB",
+            "launch average 427 MB" if cfg.name == "eva02-l-448" and B == 64 else "not captured for this workload",
             "peak_source": f"2 x bf16_tflops_sustained of MEASURED_PEAKS.json ({peaks['source']}): dense int8 runs "
             "at twice the dense bf16 rate on B200; int8 ops counted as 2 per multiply-add",
             "frac_of_nominal_4500": achieved / 4500.0,
@@ -348,7 +372,7 @@ def run_ours(args) -> None:
         "clocks": clocks.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        sec, cores, sample = cpu_forward_timing(cfg, n_images=3)
+        sec, cores, sample = cpu_forward_timing(cfg, n_images=1 if cfg.arch == "pixai" else 3)
         line["cpu_baseline"] = {"value": 1.0 / sec, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
     eng.close()
     if world > 1:
