@@ -81,7 +81,9 @@ class ModelConfig:
 
     @property
     def mlp_hidden_pad(self) -> int:
-        return _ceil(self.mlp_hidden, 128)
+        """Hidden width the GEMMs run at: a multiple of 256 so the up-projection takes 256-wide tiles (zero
+        rows/columns in the padding; 2730 -> 2816, 4736 -> 4864)."""
+        return _ceil(self.mlp_hidden, 256)
 
     @property
     def num_tags_pad(self) -> int:

@@ -126,8 +126,7 @@ int validate(const ff_model_config& c) {
     const int G = c.image_size / c.patch;
     FF_REQUIRE(c.head_kind == FF_HEAD_POOL, "engine: the PixAI architecture needs head_kind FF_HEAD_POOL");
     FF_REQUIRE(c.window >= 1 && G % c.window == 0, "engine: window %d does not tile the %d-patch grid", c.window, G);
-    FF_REQUIRE(c.mlp_hidden == c.mlp_hidden_pad && c.rot_block_hidden == 128,
-               "engine: the PixAI GELU hidden must be a multiple of 128 with an H128 rotation");
+    FF_REQUIRE(c.rot_block_hidden == 128, "engine: the PixAI GELU hidden takes an H128 rotation");
   } else {
     FF_REQUIRE(c.head_kind != FF_HEAD_POOL, "engine: FF_HEAD_POOL needs the PixAI architecture");
     FF_REQUIRE(c.mlp_hidden_pad == 2048 || c.mlp_hidden_pad == 2816 || c.mlp_hidden_pad == 4096,
@@ -336,6 +335,7 @@ int run_forward(ff_engine* e, ff_engine::Batch* b, cudaStream_t s, Profiler* pro
     FF_LAUNCH(FF_PROF_ROTATE, rot_q8(b->x, lw.norm2_w, lw.norm2_b, c.ln_eps, M, D, D, c.rot_block_dim, b->a8, b->rs, s));
     FF_LAUNCH(FF_PROF_GEMM_FC1, gemm_launch(b->fc1_p[i], s));
     if (pixai(c))
+      // zero padding columns (weights padded with zero rows) stay zero through the GELU and the H128 blocks
       FF_LAUNCH(FF_PROF_ROTATE, rot_q8(b->h, nullptr, nullptr, 0.f, M, H, H, c.rot_block_hidden, b->a8, b->rs, s));
     else
       FF_LAUNCH(FF_PROF_ROTATE, rot_q8(b->h, lw.mlp_norm_w, lw.mlp_norm_b, c.ln_eps, M, H, c.mlp_hidden,

@@ -379,11 +379,17 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 
 namespace {
 
+#ifndef FF_ROT_PWARPS
+#define FF_ROT_PWARPS 24
+#endif
+
 template <int NCH, int BLOCK, bool NORM>
 int launch_persistent(const __half* x, const float* g, const float* b, float eps, int rows, int valid, int8_t* out,
                       float* rs, int* err, cudaStream_t s) {
-  // One CTA per SM: 12 warps for the wide rows (registers), 16 otherwise.
-  constexpr int WARPS = NCH > 8 ? 12 : 16;
+  // One CTA per SM: 12 warps for the wide rows (registers), 16 for 2048, FF_ROT_PWARPS (24) for 768/1024
+  // (measured at 82,944 x 1024: 16 warps 94 us, 20 warps 90, 24 warps 88; a per-row grid holding gamma/beta
+  // in registers instead of TMEM measured 107).
+  constexpr int WARPS = NCH > 8 ? 12 : NCH > 4 ? 16 : FF_ROT_PWARPS;
   constexpr size_t smem = static_cast<size_t>(WARPS) * (2 * NCH * 256 * 2 + sizeof(float) * RotShape<NCH, BLOCK>::SW);
   static_assert(smem <= 200 * 1024, "rotation staging does not fit shared memory");
   auto kernel = rot_q8_persistent_kernel<NCH, BLOCK, WARPS, NORM>;
@@ -466,87 +472,184 @@ int rot_q8(const void* x, const float* g, const float* b, float eps, int rows, i
 }
 
 // H128 rotation + per-row int8 for rows of any multiple of 128 columns without a LayerNorm (the PixAI GELU
-// hidden, 4736 = 37 x 128, foidfinder/backends/cuda/engine.py:158-159). One warp per row; each 256-column
-// chunk holds two whole 128-blocks (lanes 0-15 and 16-31, 8 columns each; a trailing 128-column block uses
-// lanes 0-15), so the transform is chunk-local: column bits 0-2 in registers, 3-6 by shuffles inside each
-// half-warp. The row maximum is needed before any code, and a whole wide row does not fit in registers, so
-// the row is transformed twice: once for the maximum, once to quantise (the second read hits L1/L2).
-__global__ void __launch_bounds__(256) rot_q8_wide_kernel(const __half* __restrict__ x, int rows, int cols,
-                                                          int8_t* __restrict__ out, float* __restrict__ row_scale) {
-  const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  const __half* xr = x + static_cast<size_t>(row) * cols;
+// hidden, 4736 padded to 4864 = 19 x 256, foidfinder/backends/cuda/engine.py:158-159). A row is split over
+// WPR warps of the CTA, each holding CPW 256-column chunks of it in registers (4864 columns = 5 warps x 4
+// chunks, the last warp 3), so it is read once and never re-read. Small CPW keeps registers low (~55) and
+// so many rows in flight per SM, which the memory latency needs (measured at 82,944 x 4864: CPW 10 ->
+// 2.5 TB/s, 6 -> 3.6, 4 -> 4.4). Each H128 block lies inside one chunk half (lanes 0-15 or 16-31), so the
+// warps transform independently: column bits 0-2 in registers, bits 3-6 through a per-warp shared-memory
+// transpose (rot_row's layout for BLOCK 128: two chunks per transpose, 8 floats of padding every 128
+// columns). Only the row maximum crosses warps, through shared memory. Chunk columns at or past `cols` load
+// as zero and are not stored.
+template <int CPW, int WPR>
+__global__ void __launch_bounds__((WPR >= 8 ? 1 : 8 / WPR) * WPR * 32)
+    rot_q8_h128_split_kernel(const __half* __restrict__ x, int rows, int cols, int8_t* __restrict__ out,
+                             float* __restrict__ row_scale) {
+  static_assert(CPW % 2 == 0, "chunks are transposed in pairs");
+  constexpr int ROWS = WPR >= 8 ? 1 : 8 / WPR;  // rows per CTA
+  constexpr int QB = 128;             // columns per transposed lane group
+  constexpr int SW = 512 + 8 * 4;     // floats of one warp's transpose buffer (two chunks + padding)
+  __shared__ __align__(16) float tbuf[ROWS * WPR][SW];
+  __shared__ float part[ROWS][WPR];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int rloc = wid / WPR, wpart = wid % WPR;
+  const int row = blockIdx.x * ROWS + rloc;
+  const bool live = row < rows;  // dead warps still reach the barrier below
   const int nch = (cols + 255) / 256;
-  auto transform = [&](int i, float (&v)[8]) -> bool {  // false: this lane holds no columns of chunk i
-    const int c = i * 256 + lane * 8;
-    const bool have = c < cols;
-    if (have) {
-      const uint4 u = __ldg(reinterpret_cast<const uint4*>(xr + c));
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  const int first = wpart * CPW;  // this warp's first chunk
+  const __half* xr = x + static_cast<size_t>(live ? row : 0) * cols;
+  float* sw = tbuf[wid];
+
+  float2 v[CPW][4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = unpack_half2(w[e]);
-        v[2 * e] = f.x;
-        v[2 * e + 1] = f.y;
-      }
+  for (int i = 0; i < CPW; ++i) {
+    const int c = (first + i) * 256 + lane * 8;
+    if (live && c < cols) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(xr + c));
+      v[i][0] = unpack_half2(u.x);
+      v[i][1] = unpack_half2(u.y);
+      v[i][2] = unpack_half2(u.z);
+      v[i][3] = unpack_half2(u.w);
     } else {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = 0.f;
+      for (int k = 0; k < 4; ++k) v[i][k] = make_float2(0.f, 0.f);
     }
+  }
+
+  const bool swap_halves = lane & 4;
+  const int e = lane & 7, q = lane >> 3;
+  float* tp = sw + e + q * (QB + 8);  // transposed element t at tp[8 t]
+#pragma unroll
+  for (int c0 = 0; c0 < CPW; c0 += 2) {
+    if (first + c0 >= nch) break;  // warp-uniform: the rest of this warp's chunks are past the row
+#pragma unroll
+    for (int i = c0; i < c0 + 2; ++i) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) v[i][k] = make_float2(v[i][k].x + v[i][k].y, v[i][k].x - v[i][k].y);
+#pragma unroll
+      for (int h = 1; h < 4; h <<= 1)
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (!(k & h)) {
+            const float2 a = v[i][k], b = v[i][k + h];
+            v[i][k] = add2(a, b);
+            v[i][k + h] = sub2(a, b);
+          }
+    }
+#pragma unroll
+    for (int i = c0; i < c0 + 2; ++i) {
+      const int c = (i - c0) * 256 + lane * 8;
+      float* d = sw + c + 8 * (c / QB);
+      const float4 lo = make_float4(v[i][0].x, v[i][0].y, v[i][1].x, v[i][1].y);
+      const float4 hi = make_float4(v[i][2].x, v[i][2].y, v[i][3].x, v[i][3].y);
+      *reinterpret_cast<float4*>(d + (swap_halves ? 4 : 0)) = swap_halves ? hi : lo;
+      *reinterpret_cast<float4*>(d + (swap_halves ? 0 : 4)) = swap_halves ? lo : hi;
+    }
+    __syncwarp();
+    float2 tv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) tv[j] = make_float2(tp[16 * j], tp[16 * j + 8]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) tv[j] = make_float2(tv[j].x + tv[j].y, tv[j].x - tv[j].y);
 #pragma unroll
     for (int h = 1; h < 8; h <<= 1)
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (!(e & h)) {
-          const float a = v[e], b = v[e + h];
-          v[e] = a + b;
-          v[e + h] = a - b;
+      for (int j = 0; j < 8; ++j)
+        if (!(j & h)) {
+          const float2 a = tv[j], b = tv[j + h];
+          tv[j] = add2(a, b);
+          tv[j + h] = sub2(a, b);
         }
 #pragma unroll
-    for (int m = 1; m < 16; m <<= 1) {
-      const bool upper = lane & m;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float o = __shfl_xor_sync(0xffffffffu, v[e], m);
-        v[e] = upper ? o - v[e] : v[e] + o;
-      }
+    for (int j = 0; j < 8; ++j) {
+      tp[16 * j] = tv[j].x;
+      tp[16 * j + 8] = tv[j].y;
     }
+    __syncwarp();
 #pragma unroll
-    for (int e = 0; e < 8; ++e) v[e] *= 0.08838834764831845f;  // 1 / sqrt(128)
-    return have;
-  };
-  float amax = 0.f;
-  for (int i = 0; i < nch; ++i) {
-    float v[8];
-    transform(i, v);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[e]));
+    for (int i = c0; i < c0 + 2; ++i) {
+      const int c = (i - c0) * 256 + lane * 8;
+      const float* d = sw + c + 8 * (c / QB);
+      const float4 f0 = *reinterpret_cast<const float4*>(d + (swap_halves ? 4 : 0));
+      const float4 f1 = *reinterpret_cast<const float4*>(d + (swap_halves ? 0 : 4));
+      const float4 a = swap_halves ? f1 : f0;
+      const float4 b = swap_halves ? f0 : f1;
+      v[i][0] = make_float2(a.x, a.y);
+      v[i][1] = make_float2(a.z, a.w);
+      v[i][2] = make_float2(b.x, b.y);
+      v[i][3] = make_float2(b.z, b.w);
+    }
+    __syncwarp();
   }
+
+  const float2 n2 = make_float2(0.08838834764831845f, 0.08838834764831845f);  // 1 / sqrt(128)
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < CPW; ++i)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      v[i][k] = mul2(v[i][k], n2);
+      amax = max3(amax, fabsf(v[i][k].x), fabsf(v[i][k].y));
+    }
   amax = warp_max(amax);
+  if (lane == 0) part[rloc][wpart] = amax;
+  __syncthreads();
+#pragma unroll
+  for (int w = 0; w < WPR; ++w) amax = fmaxf(amax, part[rloc][w]);
+  if (!live) return;
   const float scale = fmaxf(amax, 1e-12f) / 127.f;
   const float inv = 1.f / scale;
+  const float2 inv2 = make_float2(inv, inv), magic2 = make_float2(12582912.f, 12582912.f);
   int8_t* orow = out + static_cast<size_t>(row) * cols;
-  for (int i = 0; i < nch; ++i) {
-    float v[8];
-    if (!transform(i, v)) continue;
+#pragma unroll
+  for (int i = 0; i < CPW; ++i) {
+    const int c = (first + i) * 256 + lane * 8;
+    if (c >= cols) continue;
     uint32_t t[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) t[e] = __float_as_uint(__fadd_rn(__fmul_rn(v[e], inv), 12582912.f));
+    for (int k = 0; k < 4; ++k) {
+      const float2 r = add2(mul2(v[i][k], inv2), magic2);
+      t[2 * k] = __float_as_uint(r.x);
+      t[2 * k + 1] = __float_as_uint(r.y);
+    }
     const uint32_t w0 = __byte_perm(__byte_perm(t[0], t[1], 0x0040), __byte_perm(t[2], t[3], 0x0040), 0x5410);
     const uint32_t w1 = __byte_perm(__byte_perm(t[4], t[5], 0x0040), __byte_perm(t[6], t[7], 0x0040), 0x5410);
-    *reinterpret_cast<uint2*>(orow + i * 256 + lane * 8) = make_uint2(w0, w1);
+    *reinterpret_cast<uint2*>(orow + c) = make_uint2(w0, w1);
   }
-  if (lane == 0) row_scale[row] = scale;
+  if (lane == 0 && wpart == 0) row_scale[row] = scale;
+}
+
+#ifndef FF_ROTW_CPW
+#define FF_ROTW_CPW 4
+#endif
+constexpr int kSplitCpw = FF_ROTW_CPW;  // 256-column chunks per warp
+constexpr int kSplitMaxWarps = 8;       // warps per row: rows up to 8 x kSplitCpw x 256 columns
+
+template <int WPR>
+int launch_split(const __half* x, int rows, int cols, int8_t* out, float* rs, cudaStream_t s) {
+  constexpr int ROWS = WPR >= 8 ? 1 : 8 / WPR;
+  rot_q8_h128_split_kernel<kSplitCpw, WPR><<<(rows + ROWS - 1) / ROWS, ROWS * WPR * 32, 0, s>>>(x, rows, cols, out, rs);
+  return check_launch("rot_q8_h128_split_kernel");
 }
 
 int rot_q8_h128_wide(const void* x, int rows, int cols, int8_t* out, float* rs, cudaStream_t s) {
   FF_REQUIRE(x && out && rs, "rot_q8 (wide): NULL pointer");
   FF_REQUIRE(cols >= 128 && cols % 128 == 0, "rot_q8 (wide): %d columns is not a multiple of 128", cols);
+  const int wpr = ((cols + 255) / 256 + kSplitCpw - 1) / kSplitCpw;
+  FF_REQUIRE(wpr <= kSplitMaxWarps, "rot_q8 (wide): %d columns (at most %d)", cols, kSplitMaxWarps * kSplitCpw * 256);
   FF_REQUIRE(aligned16(x) && (reinterpret_cast<uintptr_t>(out) & 7u) == 0, "rot_q8 (wide): alignment");
   if (rows == 0) return FF_OK;
-  rot_q8_wide_kernel<<<(rows + 7) / 8, 256, 0, s>>>(static_cast<const __half*>(x), rows, cols, out, rs);
-  return check_launch("rot_q8_wide_kernel");
+  const __half* xh = static_cast<const __half*>(x);
+  switch (wpr) {
+    case 1: return launch_split<1>(xh, rows, cols, out, rs, s);
+    case 2: return launch_split<2>(xh, rows, cols, out, rs, s);
+    case 3: return launch_split<3>(xh, rows, cols, out, rs, s);
+    case 4: return launch_split<4>(xh, rows, cols, out, rs, s);
+    case 5: return launch_split<5>(xh, rows, cols, out, rs, s);
+    case 6: return launch_split<6>(xh, rows, cols, out, rs, s);
+    case 7: return launch_split<7>(xh, rows, cols, out, rs, s);
+    default: return launch_split<8>(xh, rows, cols, out, rs, s);
+  }
 }
 
 }  // namespace ff

@@ -3,8 +3,11 @@ stream after warm-up. Also the entry point for ncu captures of single kernels.
 
     python -m foidfinder_b200.microbench gemm [--batch 64] [--shape 1024x3072] [--iters 20]
                                               [--epilogue bias|swiglu|residual|qkv_rope]
-    python -m foidfinder_b200.microbench attention [--batch 64] [--rope] [--iters 20]
-    python -m foidfinder_b200.microbench rotate [--batch 64] [--iters 20]
+    python -m foidfinder_b200.microbench attention [--batch 64] [--seq 1025] [--rope] [--iters 20]
+    python -m foidfinder_b200.microbench rotate [--batch 64] [--tokens 1025] [--cols 1024 ...] [--iters 20]
+
+PixAI-1008 shapes: `attention --batch 144 --seq 576` (16 images x 9 windows), `attention --batch 16 --seq
+5184` (global blocks), `rotate --batch 16 --tokens 5184 --cols 1024 --cols 4864`.
 
 Each prints one JSON line per case: shape, ms per launch, and achieved TFLOP/s (GEMM: 2*M*N*K int8 ops;
 attention: 4*B*heads*T^2*64) or GB/s (rotation: algorithmic bytes read + written).
@@ -70,25 +73,33 @@ def bench_gemm(batch: int, shapes: list[str], iters: int, epi: str) -> None:
                           "bytes": M * K + N * K + out.numel() * 2, "gbs": (M * K + N * K + out.numel() * 2) / ms / 1e6}))
 
 
-def bench_attention(batch: int, iters: int, rope: bool, heads: int = 16) -> None:
+def bench_attention(batch: int, iters: int, rope: bool, seq: int = TOKENS, heads: int = 16) -> None:
     from .weights import rope_tables
 
     d = torch.device("cuda")
     g = torch.Generator(device=d).manual_seed(0)
-    qkv = torch.randn(batch * TOKENS, 3 * heads * 64, generator=g, device=d).half()
-    out = torch.empty(batch * TOKENS, heads * 64, device=d, dtype=torch.float16)
-    tables = tuple(t.to(d) for t in rope_tables(32, 16)) if rope else None
-    ms = _time(lambda: ops.attention(qkv, out, TOKENS, heads, rope=tables, scale=0.125), iters)
-    flops = 4 * batch * heads * TOKENS * TOKENS * 64
-    print(json.dumps({"kernel": "attention", "batch": batch, "tokens": TOKENS, "heads": heads, "rope": rope, "ms": ms,
-                      "tflops": flops / ms / 1e9}))
+    qkv = torch.randn(batch * seq, 3 * heads * 64, generator=g, device=d).half()
+    out = torch.empty(batch * seq, heads * 64, device=d, dtype=torch.float16)
+    tables = tuple(t.to(d) for t in rope_tables(32, 16)) if rope and seq == TOKENS else None  # EVA02 tables only
+    ms = _time(lambda: ops.attention(qkv, out, seq, heads, rope=tables, scale=0.125), iters)
+    flops = 4 * batch * heads * seq * seq * 64
+    print(json.dumps({"kernel": "attention", "batch": batch, "tokens": seq, "heads": heads, "rope": tables is not None,
+                      "ms": ms, "tflops": flops / ms / 1e9}))
 
 
-def bench_rotate(batch: int, iters: int) -> None:
+ROT_CASES = {  # cols -> the engine's rotations of that width: (valid, block, LayerNorm)
+    1024: ((1024, 1024, True), (1024, 1024, False)),
+    2816: ((2730, 128, True),),
+    4864: ((4864, 128, False),),  # PixAI GELU hidden 4736 padded to 4864
+}
+
+
+def bench_rotate(batch: int, iters: int, tokens: int = TOKENS, widths: list[int] | None = None) -> None:
     d = torch.device("cuda")
     g = torch.Generator(device=d).manual_seed(0)
-    M = TOKENS * batch
-    for cols, valid, block, norm in ((1024, 1024, 1024, True), (1024, 1024, 1024, False), (2816, 2730, 128, True)):
+    M = tokens * batch
+    cases = [(c, *v) for c in (widths or (1024, 2816)) for v in ROT_CASES[c]]
+    for cols, valid, block, norm in cases:
         x = torch.randn(M, cols, generator=g, device=d).half()
         gamma = torch.ones(cols, device=d) if norm else None
         beta = torch.zeros(cols, device=d) if norm else None
@@ -108,13 +119,16 @@ def main() -> None:
     ap.add_argument("--shape", action="append", choices=sorted(GEMM_SHAPES))
     ap.add_argument("--epilogue", default="bias", choices=("bias", "swiglu", "residual", "qkv_rope"))
     ap.add_argument("--rope", action="store_true")
+    ap.add_argument("--seq", type=int, default=TOKENS, help="attention: sequence length")
+    ap.add_argument("--tokens", type=int, default=TOKENS, help="rotate: rows per image")
+    ap.add_argument("--cols", type=int, action="append", choices=sorted(ROT_CASES), help="rotate: row widths")
     a = ap.parse_args()
     if a.kernel == "gemm":
         bench_gemm(a.batch, a.shape or list(GEMM_SHAPES), a.iters, a.epilogue)
     elif a.kernel == "attention":
-        bench_attention(a.batch, a.iters, a.rope)
+        bench_attention(a.batch, a.iters, a.rope, a.seq)
     else:
-        bench_rotate(a.batch, a.iters)
+        bench_rotate(a.batch, a.iters, a.tokens, a.cols)
     torch.cuda.synchronize()
     err = ops.device_error(0)
     if err:

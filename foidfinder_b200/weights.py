@@ -283,10 +283,12 @@ def convert_pixai(raw: dict[str, torch.Tensor], cfg: ModelConfig,
     PixAITorch.__init__ (reference.py:70-98): patch weight in (kh, kw, c) column order, the pretraining
     position embedding tiled over the grid and put in window order, window and global RoPE tables (the
     global one at positions scaled by window / grid, window-ordered), stored angle-major [32, n]; the pool's
-    position embedding in window order and its query carrying the 1/8 scale. The patch embedding's bias, if
-    the checkpoint has one, is not used — the reference's stem has none (reference.py:112)."""
+    position embedding in window order and its query carrying the 1/8 scale. The hidden is padded with zero
+    fc1 rows / fc2 columns to mlp_hidden_pad (4736 -> 4864) so fc1 runs on 256-wide tiles; the padding
+    stays exactly zero through GELU and the H128 blocks. The patch embedding's bias, if the checkpoint has
+    one, is not used — the reference's stem has none (reference.py:112)."""
     dev = torch.device(device) if device is not None else raw["pos_embed"].device
-    D, G, L, win = cfg.dim, cfg.grid, cfg.patches, cfg.window
+    D, G, L, win, H, Hp = cfg.dim, cfg.grid, cfg.patches, cfg.window, cfg.mlp_hidden, cfg.mlp_hidden_pad
     perm = window_order(G, win).to(raw["pos_embed"].device)
     out: dict[str, torch.Tensor] = {}
 
@@ -333,8 +335,10 @@ def convert_pixai(raw: dict[str, torch.Tensor], cfg: ModelConfig,
         lin = {
             "qkv": (qkv_w, qkv_b, cfg.rot_block_dim),
             "proj": (raw[p + "attn.proj.weight"].float(), raw[p + "attn.proj.bias"].float(), cfg.rot_block_dim),
-            "fc1": (raw[p + "mlp.fc1.weight"].float(), raw[p + "mlp.fc1.bias"].float(), cfg.rot_block_dim),
-            "fc2": (raw[p + "mlp.fc2.weight"].float(), raw[p + "mlp.fc2.bias"].float(), cfg.rot_block_hidden),
+            "fc1": (torch.nn.functional.pad(raw[p + "mlp.fc1.weight"].float(), (0, 0, 0, Hp - H)),
+                    torch.nn.functional.pad(raw[p + "mlp.fc1.bias"].float(), (0, Hp - H)), cfg.rot_block_dim),
+            "fc2": (torch.nn.functional.pad(raw[p + "mlp.fc2.weight"].float(), (0, Hp - H)),
+                    raw[p + "mlp.fc2.bias"].float(), cfg.rot_block_hidden),
         }
         for name, (w, b, block) in lin.items():
             q, s = quantize_rows_int8(fwht_rows(w, block))

@@ -154,7 +154,7 @@ typedef struct ff_model_config {
   int depth;            /* 24 / 12 */
   int heads;            /* dim / 64 */
   int mlp_hidden;       /* 2730 / 2048 real SwiGLU width */
-  int mlp_hidden_pad;   /* 2816 / 2048: multiple of 128 */
+  int mlp_hidden_pad;   /* 2816 / 2048 / 4864 (PixAI's 4736): multiple of 128, zero-padded weights */
   int num_tags;         /* 30877 */
   int num_tags_pad;     /* multiple of 256 */
   int rot_block_dim;    /* Hadamard block for dim-wide activations: 1024 / 256 */

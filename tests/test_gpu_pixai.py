@@ -47,7 +47,7 @@ def test_pixai_teacher_forced(cuda_device, no_device_error, image, window, B):
     PX.forward_int8(conv, cfg, imgs, trace=trace)
     fin = trace[-1]
     W = {k: v.to(d) for k, v in conv.items()}
-    L, D, H, eps = cfg.patches, cfg.dim, cfg.mlp_hidden, cfg.ln_eps
+    L, D, H, eps = cfg.patches, cfg.dim, cfg.mlp_hidden_pad, cfg.ln_eps
     M = B * L
 
     patches = torch.empty(M, cfg.k_pad, dtype=torch.float16, device=d)
@@ -102,7 +102,7 @@ def test_pixai_teacher_forced(cuda_device, no_device_error, image, window, B):
         ops.rot_q8_h128(st["h"].to(d), ah, rs)
         torch.cuda.synchronize()
         _fp16_close(h, st["h"], tag + " fc1 GEMM + GELU", atol=4e-3, rtol=4e-3)
-        _codes_close(ah, st["a8h"], tag + " H128+q8 (4736)")
+        _codes_close(ah, st["a8h"], tag + " H128+q8 (4864 padded)")
         torch.testing.assert_close(rs.cpu(), st["rsh"], rtol=2e-5, atol=0)
         xr = st["x_attn"].to(d).clone()
         ops.gemm_s8(st["a8h"].to(d), W[p + "fc2.qweight"], st["rsh"].to(d), W[p + "fc2.wscale"], W[p + "fc2.bias"], xr,

@@ -40,9 +40,10 @@ def test_gemm_s8_gelu_epilogue(cuda_device, no_device_error, N, tile):
     torch.testing.assert_close(out.float().cpu(), ref.half().float(), atol=4e-3, rtol=4e-3)
 
 
-@pytest.mark.parametrize(("rows", "cols"), [(1, 128), (333, 384), (1030, 4736), (64, 1152)])
+@pytest.mark.parametrize(("rows", "cols"), [(1, 128), (333, 384), (1030, 4736), (64, 1152), (3, 4736), (41, 6272)])
 def test_rot_q8_h128_any_width(cuda_device, no_device_error, rows, cols):
-    """H128 + per-row int8 over widths outside the fixed set (PixAI's 4736 = 37 x 128)."""
+    """H128 + per-row int8 over widths outside the fixed set (PixAI's 4736 = 37 x 128), one, two and four
+    warps per row, row counts that leave warps of the last CTA without a row."""
     from foidfinder_b200 import ops
 
     g = torch.Generator().manual_seed(rows + cols)
