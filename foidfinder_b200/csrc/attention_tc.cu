@@ -4,10 +4,11 @@
 // softmax(q k^T) v per head on the packed QKV activations, scale folded into q), with f32 accumulation and
 // masked ragged tails (EVA02 at 448 px has 1025 tokens).
 //
-// One CTA = up to 256 queries (two 128-row tiles, Q0 and Q1) of one (image, head); 320 threads, one CTA
-// per SM (it owns all 512 TMEM columns):
-//   warp 0     TMA: Q0/Q1 once, then K/V tiles of 128 keys through a 3-stage ring. The tensor map is
-//              3-D [images, tokens, 3*dim], so rows past an image's last token arrive as zeros.
+// Persistent CTAs (one per SM, 320 threads, all 512 TMEM columns) walk work items of up to 256 queries
+// (two 128-row tiles, Q0 and Q1) of one (image, head); consecutive items overlap in the pipeline:
+//   warp 0     TMA: each item's Q0/Q1 into one of two Q buffers, K/V tiles of 128 keys through a 3-stage
+//              ring. The tensor map is 3-D [images, tokens, 3*dim], so rows past an image's last token
+//              arrive as zeros.
 //   warp 1     TMEM allocation and the MMA issuer, ping-ponging the two query tiles:
 //                S_i = Q_i K^T        (SS, M128 N128 K64)                           -> TMEM [128 i, +128)
 //                [O_i | l_i] += P_i [V | 1]  (TS: P_i read from TMEM; B = the V tile plus a constant
@@ -25,7 +26,11 @@
 //              (saturated there) are at most 2^-21 of the row maximum; it cancels in O / l.
 // The row sum l is column 64 of the widened P V product: it costs no extra MMA instruction (every
 // tcgen05.mma costs >= ~56 cycles whatever its N) and is rescaled together with O.
+#include <algorithm>
+#include <mutex>
+
 #include "common.h"
+#include "kernels.h"
 #include "ptx.cuh"
 
 namespace ff {
@@ -33,8 +38,8 @@ namespace fa {
 
 constexpr int BQ = 128, BKV = 128, HD = 64, STAGES = 3;
 constexpr int TILE = 128 * 128;  // 128 rows x 128 bytes (64 fp16)
-constexpr int OFF_Q = 0;         // Q0, Q1
-constexpr int OFF_K = OFF_Q + 2 * TILE;
+constexpr int OFF_Q = 0;         // two buffers of (Q0, Q1): buffer b tile i at OFF_Q + (2 b + i) TILE
+constexpr int OFF_K = OFF_Q + 4 * TILE;
 constexpr int OFF_V = OFF_K + STAGES * TILE;
 constexpr int ONES_LBO = STAGES * TILE;          // V stage s + ONES_LBO: its atom of fp16 1.0
 constexpr int OFF_ONES = OFF_V + ONES_LBO;       // STAGES atoms of 128 rows x 128 B
@@ -131,8 +136,8 @@ constexpr unsigned kPolyChunks = FF_ATTN_POLY_CHUNKS;
 }  // namespace fa
 
 // Query rows past the last full 128-row tile, when there are at most kTailRows of them (EVA02: 1025 =
-// 8 x 128 + 1), go to one extra CTA per (image, head) that computes them on the CUDA cores in f32: a
-// tensor-core CTA for them would run a whole query tile (and all key tiles) for one row. Each
+// 8 x 128 + 1), go to a separate launch with one CTA per (image, head) that computes them on the CUDA
+// cores in f32: a tensor-core item for them would run a whole query tile (and all key tiles) for one row. Each
 // quarter-warp (8 lanes x 8 dims = one 128-byte key/value row, coalesced) walks its share of the keys
 // with its own online softmax (running max m, sum l, o over its 8 dims per lane), four keys in flight;
 // the 40 partial results are then merged through shared memory. Called by every thread of the CTA.
@@ -228,51 +233,71 @@ __device__ __noinline__ void attention_tail_rows(const __half* __restrict__ qkv,
 }
 }  // namespace fa
 
+// Rows past the last full query tile (see attention_tail_rows), one CTA per (head, image).
+__global__ void __launch_bounds__(fa::THREADS)
+    attention_tail_kernel(const __half* __restrict__ qkv, __half* __restrict__ out, int T, int T_main, int heads,
+                          float scale_log2) {
+  fa::attention_tail_rows(qkv, out, T, T_main, heads, scale_log2, blockIdx.y, blockIdx.x);
+}
+
+// Persistent: min(items, SMs) CTAs, each walking work items (image, head, pair of query tiles) with a grid
+// stride, pair index fastest so the items running at once share their keys/values in L2. The pipeline
+// runs across item boundaries: the producer loads the next item's Q into the other Q buffer and its
+// keys/values into the same ring while this item computes; the MMA warp issues the next item's first S
+// right after this item's last P V; the softmax warps drain O (tcgen05.ld) and release it (o_empty) before
+// storing, so the next item's first P V, which overwrites O, waits only for that read. Every barrier
+// phase is counted per CTA (items, tiles), not per item. An item whose second query tile is empty runs
+// that warpgroup's protocol without work (its S and P V are skipped, its barriers still advance).
 __global__ void __launch_bounds__(fa::THREADS, 1)
-    attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __half* __restrict__ qkv,
-                        __half* __restrict__ out, int T, int T_main, int heads, float scale_log2, int* err) {
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, __half* __restrict__ out, int T, int T_main,
+                        int heads, int num_seqs, float scale_log2, int* err) {
   using namespace fa;
-  if (T_main < T && blockIdx.x == gridDim.x - 1) {
-    attention_tail_rows(qkv, out, T, T_main, heads, scale_log2, blockIdx.z, blockIdx.y);
-    return;
-  }
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-  uint64_t* q_full = bar + 0;
-  uint64_t* kv_full = bar + 1;               // [STAGES]
-  uint64_t* kv_empty = bar + 1 + STAGES;     // [STAGES]
-  uint64_t* s_full = bar + 1 + 2 * STAGES;   // [2]
-  uint64_t* p_full = s_full + 2;             // [2]
-  uint64_t* o_full = p_full + 2;
-  uint64_t* order = o_full + 1;             // [2]: warpgroup g may run its exponentials
+  uint64_t* q_full = bar + 0;              // [2] Q buffers
+  uint64_t* q_empty = bar + 2;             // [2]
+  uint64_t* kv_full = bar + 4;             // [STAGES]
+  uint64_t* kv_empty = kv_full + STAGES;   // [STAGES]
+  uint64_t* s_full = kv_empty + STAGES;    // [2] per query tile
+  uint64_t* p_full = s_full + 2;           // [2]
+  uint64_t* o_full = p_full + 2;           // [2]
+  uint64_t* o_empty = o_full + 2;          // [2]
+  uint64_t* order = o_empty + 2;           // [2]: warpgroup g may run its exponentials
   uint64_t* drain = order + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.y, img = blockIdx.z;
   const int dim = heads * HD;
-  const int q0 = blockIdx.x * 2 * BQ;
-  const bool has1 = q0 + BQ < T_main;  // the second query tile holds at least one token
+  const int n_pairs = (T_main + 2 * BQ - 1) / (2 * BQ);
+  const int items = num_seqs * heads * n_pairs;
   const int nkv = (T + BKV - 1) / BKV;
   // The last key tile may be ragged: its S and P V products only cover the first kv_tail_n keys
   // (a multiple of 16; keys past T inside them are masked in the softmax).
   const int kv_tail = T - (nkv - 1) * BKV;
   const int kv_tail_n = (kv_tail + 15) & ~15;
+  auto item_of = [&](int it, int& img, int& h, int& q0) {
+    const int pair = it % n_pairs, r = it / n_pairs;
+    h = r % heads;
+    img = r / heads;
+    q0 = pair * 2 * BQ;
+  };
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
-    }
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_empty[i], 4);
       mbar_init(&order[i], 4);
     }
-    mbar_init(o_full, 1);
+    for (int st = 0; st < STAGES; ++st) {
+      mbar_init(&kv_full[st], 1);
+      mbar_init(&kv_empty[st], 1);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -296,35 +321,53 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, has1 ? 2 * TILE : TILE);
-      tma_load_3d(smem + OFF_Q, &tm_qkv, q_full, h * HD, q0, img);
-      if (has1) tma_load_3d(smem + OFF_Q + TILE, &tm_qkv, q_full, h * HD, q0 + BQ, img);
-      int last_phase[STAGES];
+      int q_phase[2] = {-1, -1}, kv_phase[STAGES];
 #pragma unroll
-      for (int s = 0; s < STAGES; ++s) last_phase[s] = -1;
+      for (int st = 0; st < STAGES; ++st) kv_phase[st] = -1;
       bool ok = true;
-      for (int j = 0; j < nkv; ++j) {
-        const int s = j % STAGES;
-        const uint32_t ph = static_cast<uint32_t>(j / STAGES) & 1u;
-        if (!mbar_wait(&kv_empty[s], ph ^ 1u, abort_flag, err, kDevTimeoutAttn)) {
+      int kv_count = 0, n = 0;
+      for (int it = blockIdx.x; it < items && ok; it += gridDim.x, ++n) {
+        int img, h, q0;
+        item_of(it, img, h, q0);
+        const bool has1 = q0 + BQ < T_main;
+        const int qb = n & 1;
+        if (n >= 2 && !mbar_wait(&q_empty[qb], static_cast<uint32_t>((n >> 1) - 1) & 1u, abort_flag, err,
+                                 kDevTimeoutAttn)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&kv_full[s], 2 * TILE);
-        tma_load_3d(smem + OFF_K + s * TILE, &tm_qkv, &kv_full[s], dim + h * HD, j * BKV, img);
-        tma_load_3d(smem + OFF_V + s * TILE, &tm_qkv, &kv_full[s], 2 * dim + h * HD, j * BKV, img);
-        last_phase[s] = static_cast<int>(ph);
+        mbar_arrive_expect_tx(&q_full[qb], has1 ? 2 * TILE : TILE);
+        tma_load_3d(smem + OFF_Q + 2 * qb * TILE, &tm_qkv, &q_full[qb], h * HD, q0, img);
+        if (has1) tma_load_3d(smem + OFF_Q + (2 * qb + 1) * TILE, &tm_qkv, &q_full[qb], h * HD, q0 + BQ, img);
+        q_phase[qb] = (n >> 1) & 1;
+        for (int j = 0; j < nkv; ++j, ++kv_count) {
+          const int st = kv_count % STAGES;
+          const uint32_t ph = static_cast<uint32_t>(kv_count / STAGES) & 1u;
+          if (!mbar_wait(&kv_empty[st], ph ^ 1u, abort_flag, err, kDevTimeoutAttn)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&kv_full[st], 2 * TILE);
+          tma_load_3d(smem + OFF_K + st * TILE, &tm_qkv, &kv_full[st], dim + h * HD, j * BKV, img);
+          tma_load_3d(smem + OFF_V + st * TILE, &tm_qkv, &kv_full[st], 2 * dim + h * HD, j * BKV, img);
+          kv_phase[st] = static_cast<int>(ph);
+        }
       }
-      // Let every issued copy land before the CTA can exit (bounded).
-      const unsigned long long t0 = globaltimer();
-      while (!mbar_try_wait(smem_u32(q_full), 0) && globaltimer() - t0 < kWaitLimitNs) {
-      }
-      if (!ok)
-        for (int s = 0; s < STAGES; ++s)
-          if (last_phase[s] >= 0)
-            while (!mbar_try_wait(smem_u32(&kv_full[s]), static_cast<uint32_t>(last_phase[s])) &&
+      // Normally the MMA warp has consumed every copy. After an abort, let the issued ones land (bounded)
+      // before the CTA can exit: the last phase of each barrier completes with its last copy.
+      if (!ok) {
+        const unsigned long long t0 = globaltimer();
+        for (int b = 0; b < 2; ++b)
+          if (q_phase[b] >= 0)
+            while (!mbar_try_wait(smem_u32(&q_full[b]), static_cast<uint32_t>(q_phase[b])) &&
                    globaltimer() - t0 < kWaitLimitNs) {
             }
+        for (int st = 0; st < STAGES; ++st)
+          if (kv_phase[st] >= 0)
+            while (!mbar_try_wait(smem_u32(&kv_full[st]), static_cast<uint32_t>(kv_phase[st])) &&
+                   globaltimer() - t0 < kWaitLimitNs) {
+            }
+      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -332,17 +375,17 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
       constexpr uint32_t id_s = idesc_f16(128, BKV);
       const uint32_t id_s_tail = idesc_f16(128, kv_tail_n);
       constexpr uint32_t id_o = idesc_f16(128, HD + 16) | (1u << 16);  // B = [V | ones] is MN-major, N = 80
-      auto issue_s = [&](int i, int j) {
-        const uint64_t qd = sdesc_k_sw128(smem_u32(smem + OFF_Q + i * TILE));
-        const uint64_t kd = sdesc_k_sw128(smem_u32(smem + OFF_K + (j % STAGES) * TILE));
-        const uint32_t id = j == nkv - 1 ? id_s_tail : id_s;
+      auto issue_s = [&](int i, int qb, int c, bool tail) {  // S_i = Q_i K^T for key tile count c
+        const uint64_t qd = sdesc_k_sw128(smem_u32(smem + OFF_Q + (2 * qb + i) * TILE));
+        const uint64_t kd = sdesc_k_sw128(smem_u32(smem + OFF_K + (c % STAGES) * TILE));
+        const uint32_t id = tail ? id_s_tail : id_s;
 #pragma unroll
         for (int k = 0; k < 4; ++k) mma_f16(tmem + t_s(i), qd + 2 * k, kd + 2 * k, id, k > 0);
         tc_commit(&s_full[i]);
       };
-      auto issue_pv = [&](int i, int j) {
-        const uint32_t sv = smem_u32(smem + OFF_V + (j % STAGES) * TILE);
-        const int steps = j == nkv - 1 ? kv_tail_n / 16 : 8;
+      auto issue_pv = [&](int i, int j, int c, bool tail) {
+        const uint32_t sv = smem_u32(smem + OFF_V + (c % STAGES) * TILE);
+        const int steps = tail ? kv_tail_n / 16 : 8;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {  // 16 keys per step: P columns 8k.., V rows 16k..
           if (k < steps) {
@@ -351,36 +394,86 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
           }
         }
       };
-      auto kv_wait = [&](int j) {
-        return mbar_wait(&kv_full[j % STAGES], static_cast<uint32_t>(j / STAGES) & 1u, abort_flag, err,
+      auto kv_wait = [&](int c) {
+        return mbar_wait(&kv_full[c % STAGES], static_cast<uint32_t>(c / STAGES) & 1u, abort_flag, err,
                          kDevTimeoutAttn);
       };
-      bool ok = mbar_wait(q_full, 0, abort_flag, err, kDevTimeoutAttn) && kv_wait(0);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0, 0);
-        if (has1) issue_s(1, 0);
-      }
-      for (int j = 0; j < nkv && ok; ++j) {
-        const uint32_t par = static_cast<uint32_t>(j) & 1u;
-        if (!mbar_wait(&p_full[0], par, abort_flag, err, kDevTimeoutAttn)) break;
-        tc_fence_after();
-        issue_pv(0, j);
-        const bool next = j + 1 < nkv;
-        if (next) {
-          if (!kv_wait(j + 1)) break;
+      // One flat sequence of key tiles over this CTA's items: per tile, P V of query tile 0, then S of query
+      // tile 0 for the next key tile (the next item's first when this tile is an item's last, so the next
+      // item starts while this one drains), then the same for query tile 1.
+      bool ok = true;
+      int kv_count = 0, tiles = 0, n = 0, it = blockIdx.x;
+      int img, h, q0;
+      bool has1 = false;
+      if (it < items) {
+        item_of(it, img, h, q0);
+        has1 = q0 + BQ < T_main;
+        ok = mbar_wait(&q_full[0], 0u, abort_flag, err, kDevTimeoutAttn) && kv_wait(0);
+        if (ok) {
           tc_fence_after();
-          issue_s(0, j + 1);
+          issue_s(0, 0, 0, nkv == 1);
+          if (has1)
+            issue_s(1, 0, 0, nkv == 1);
+          else
+            tc_commit(&s_full[1]);  // warpgroup 1 idles on this item; its barriers still advance
         }
-        if (has1) {
-          if (!mbar_wait(&p_full[1], par, abort_flag, err, kDevTimeoutAttn)) break;
-          tc_fence_after();
-          issue_pv(1, j);
-        }
-        tc_commit(&kv_empty[j % STAGES]);
-        if (has1 && next) issue_s(1, j + 1);
       }
-      tc_commit(o_full);
+      for (; it < items && ok; it += gridDim.x, ++n) {
+        const int qb = n & 1;
+        const int it_next = it + gridDim.x;
+        const bool more = it_next < items;
+        bool has1_next = false;
+        if (more) {
+          int img2, h2, q02;
+          item_of(it_next, img2, h2, q02);
+          has1_next = q02 + BQ < T_main;
+        }
+        for (int j = 0; j < nkv; ++j, ++kv_count, ++tiles) {
+          const bool last = j == nkv - 1;
+          // The key tile after this one: (this item, j + 1), or (next item, 0) with the other Q buffer.
+          const bool next = !last || more;
+          const int nqb = last ? qb ^ 1 : qb;
+          const bool ntail = last ? nkv == 1 : j + 1 == nkv - 1;
+          const bool nhas1 = last ? has1_next : has1;
+          const uint32_t par = static_cast<uint32_t>(tiles) & 1u;
+          const uint32_t opar = static_cast<uint32_t>(n - 1) & 1u;
+          if (last) tc_commit(&q_empty[qb]);  // every S of this item is issued: Q frees when they complete
+          if (!mbar_wait(&p_full[0], par, abort_flag, err, kDevTimeoutAttn) ||
+              (j == 0 && n > 0 && !mbar_wait(&o_empty[0], opar, abort_flag, err, kDevTimeoutAttn))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(0, j, kv_count, last);
+          if (last) tc_commit(&o_full[0]);
+          if (next) {
+            if (!kv_wait(kv_count + 1) ||
+                (last && !mbar_wait(&q_full[nqb], static_cast<uint32_t>((n + 1) >> 1) & 1u, abort_flag, err,
+                                    kDevTimeoutAttn))) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(0, nqb, kv_count + 1, ntail);
+          }
+          if (!mbar_wait(&p_full[1], par, abort_flag, err, kDevTimeoutAttn) ||
+              (has1 && j == 0 && n > 0 && !mbar_wait(&o_empty[1], opar, abort_flag, err, kDevTimeoutAttn))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (has1) issue_pv(1, j, kv_count, last);
+          if (last) tc_commit(&o_full[1]);
+          tc_commit(&kv_empty[kv_count % STAGES]);
+          if (next) {
+            if (nhas1)
+              issue_s(1, nqb, kv_count + 1, ntail);
+            else
+              tc_commit(&s_full[1]);
+          }
+        }
+        has1 = has1_next;
+      }
       tc_commit(drain);
       const unsigned long long t0 = globaltimer();
       while (!mbar_try_wait(smem_u32(drain), 0)) {
@@ -395,177 +488,158 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
     const int g = (warp - 2) >> 2;  // query tile of this warpgroup
     const int q = warp & 3;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-    const int row = q0 + g * BQ + q * 32 + lane;
-    if (g == 0 || has1) {
+    const uint32_t ts = tmem + lane_base + t_s(g);
+    bool ok = true;
+    int tiles = 0, n = 0;
+    for (int it = blockIdx.x; it < items && ok; it += gridDim.x, ++n) {
+      int img, h, q0;
+      item_of(it, img, h, q0);
+      const bool active = g == 0 || q0 + BQ < T_main;  // warp-uniform
+      const int row = q0 + g * BQ + q * 32 + lane;
       float m_ref = -INFINITY;
-      bool ok = true;
-      for (int j = 0; j < nkv && ok; ++j) {
-        if (!mbar_wait(&s_full[g], static_cast<uint32_t>(j) & 1u, abort_flag, err, kDevTimeoutAttn)) {
+      for (int j = 0; j < nkv; ++j, ++tiles) {
+        if (!mbar_wait(&s_full[g], static_cast<uint32_t>(tiles) & 1u, abort_flag, err, kDevTimeoutAttn)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t ts = tmem + lane_base + t_s(g);
         const int valid = T - j * BKV;  // keys at columns >= valid belong to no token of this image
         const bool full_tile = valid >= BKV;
-        // Pass 1: row maximum; the whole 128-key row of S in registers, four loads, one wait.
-        float mx = -INFINITY;
-#if FF_ATTN_S_REGS
-        uint32_t raw[4][32];  // kept for pass 2
-#endif
-        {
-#if !FF_ATTN_S_REGS
-          uint32_t raw[4][32];
-#endif
+        if (active) {
+          // Pass 1: row maximum, 64 keys (two loads, one wait) at a time: holding all 128 in registers
+          // pushed the kernel to the 168-register cap with spills (measured 5-10% slower).
+          float mx = -INFINITY;
 #pragma unroll
-          for (int c = 0; c < 4; ++c) tmem_ld32(ts + 32 * c, raw[c]);
-          tmem_ld_wait();
-          if (full_tile) {
+          for (int hf = 0; hf < 2; ++hf) {
+            uint32_t raw[2][32];
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
-#pragma unroll
-              for (int e = 0; e < 32; e += 2) mx = max3(mx, __uint_as_float(raw[c][e]), __uint_as_float(raw[c][e + 1]));
-          } else {
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-#pragma unroll
-              for (int e = 0; e < 32; ++e)
-                if (32 * c + e < valid) mx = fmaxf(mx, __uint_as_float(raw[c][e]));
-          }
-        }
-        const float m_new = fmaxf(m_ref, mx * scale_log2);
-        bool rescale = false;
-        float corr = 1.f;
-        if (j == 0) {
-          m_ref = m_new;
-        } else if (m_new > m_ref + kRescaleThreshold) {
-          corr = ex2_approx(m_ref - m_new);
-          m_ref = m_new;
-          rescale = true;
-        }
-        if (__any_sync(0xffffffffu, rescale)) {
-#if FF_ATTN_S_REGS
-          uint32_t o[16];  // S occupies 128 registers: rescale in 16-column pieces
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            tmem_ld16(tmem + lane_base + t_o(g) + 16 * c, o);
+            for (int c = 0; c < 2; ++c) tmem_ld32(ts + 64 * hf + 32 * c, raw[c]);
             tmem_ld_wait();
+            if (full_tile) {
 #pragma unroll
-            for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
-            tmem_st16(tmem + lane_base + t_o(g) + 16 * c, o);
+              for (int c = 0; c < 2; ++c)
+#pragma unroll
+                for (int e = 0; e < 32; e += 2)
+                  mx = max3(mx, __uint_as_float(raw[c][e]), __uint_as_float(raw[c][e + 1]));
+            } else {
+#pragma unroll
+              for (int c = 0; c < 2; ++c)
+#pragma unroll
+                for (int e = 0; e < 32; ++e)
+                  if (64 * hf + 32 * c + e < valid) mx = fmaxf(mx, __uint_as_float(raw[c][e]));
+            }
           }
-#else
-          uint32_t o[32];
+          const float m_new = fmaxf(m_ref, mx * scale_log2);
+          bool rescale = false;
+          float corr = 1.f;
+          if (j == 0) {
+            m_ref = m_new;
+          } else if (m_new > m_ref + kRescaleThreshold) {
+            corr = ex2_approx(m_ref - m_new);
+            m_ref = m_new;
+            rescale = true;
+          }
+          if (__any_sync(0xffffffffu, rescale)) {
+            uint32_t o[32];
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            tmem_ld32(tmem + lane_base + t_o(g) + 32 * c, o);
+            for (int c = 0; c < 2; ++c) {
+              tmem_ld32(tmem + lane_base + t_o(g) + 32 * c, o);
+              tmem_ld_wait();
+#pragma unroll
+              for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
+              fa::tmem_st32(tmem + lane_base + t_o(g) + 32 * c, o);
+            }
+            uint32_t l;
+            fa::tmem_ld1(tmem + lane_base + t_l(g), l);
             tmem_ld_wait();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
-            fa::tmem_st32(tmem + lane_base + t_o(g) + 32 * c, o);
+            fa::tmem_st1(tmem + lane_base + t_l(g), __float_as_uint(__uint_as_float(l) * corr));
           }
-#endif
-          uint32_t l;
-          fa::tmem_ld1(tmem + lane_base + t_l(g), l);
-          tmem_ld_wait();
-          fa::tmem_st1(tmem + lane_base + t_l(g), __float_as_uint(__uint_as_float(l) * corr));
         }
-        // The two warpgroups take turns at the exponentials (WG0 of tile j, WG1 of tile j, WG0 of tile
-        // j+1, ...): each gets the whole MUFU pipe while the other's P V and next S run on the tensor core.
-        if (has1 && (g == 1 || j > 0) &&
-            !mbar_wait(&order[g], static_cast<uint32_t>(g == 0 ? j - 1 : j) & 1u, abort_flag, err, kDevTimeoutAttn)) {
+        // The two warpgroups take turns at the exponentials (WG0 of tile t, WG1 of tile t, WG0 of tile
+        // t+1, ... counted across items): each gets the whole MUFU pipe while the other's P V and next S
+        // run on the tensor core.
+        if ((g == 1 || tiles > 0) &&
+            !mbar_wait(&order[g], static_cast<uint32_t>(g == 0 ? tiles - 1 : tiles) & 1u, abort_flag, err,
+                       kDevTimeoutAttn)) {
           ok = false;
           break;
         }
-        // Pass 2: P = 2^(s * scale_log2 - m_ref + 7) as fp16 pairs over S columns [0, 64), in two halves
-        // of 64 keys (two loads, one wait each). P of half hf (columns 32hf..32hf+31) only overlaps S
-        // columns already read (those of half 0).
-        const float2 sc2 = make_float2(scale_log2, scale_log2);
-        const float2 nm2 = make_float2(kPScaleLog2 - m_ref, kPScaleLog2 - m_ref);
-#if FF_ATTN_S_REGS
-        // S is still in registers from pass 1: no second TMEM read.
+        if (active) {
+          // Pass 2: P = 2^(s * scale_log2 - m_ref + 7) as fp16 pairs over S columns [0, 64), in two halves
+          // of 64 keys (two loads, one wait each). P of half hf (columns 32hf..32hf+31) only overlaps S
+          // columns already read (those of half 0).
+          const float2 sc2 = make_float2(scale_log2, scale_log2);
+          const float2 nm2 = make_float2(kPScaleLog2 - m_ref, kPScaleLog2 - m_ref);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t pk[16];
-          if (!full_tile && 32 * c >= valid) {
-            // P past the ragged tile's keys is never read
-          } else if (full_tile) {
+          for (int hf = 0; hf < 2; ++hf) {
+            if (!full_tile && 64 * hf >= valid) break;  // P past the ragged tile's keys is never read
+            uint32_t raw[2][32];
+            tmem_ld32(ts + 64 * hf, raw[0]);
+            tmem_ld32(ts + 64 * hf + 32, raw[1]);
+            tmem_ld_wait();
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const float2 x =
-                  fma2(make_float2(__uint_as_float(raw[c][2 * e]), __uint_as_float(raw[c][2 * e + 1])), sc2, nm2);
-              pk[e] = ((kPolyChunks >> c) & 1u) ? fa::exp2_poly(x) : fa::exp2_mufu(x);
-            }
-          } else {
+            for (int cc = 0; cc < 2; ++cc) {
+              const int c = 2 * hf + cc;
+              if (!full_tile && 32 * c >= valid) break;
+              uint32_t pk[16];
+              if (full_tile) {
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              float2 x = fma2(make_float2(__uint_as_float(raw[c][2 * e]), __uint_as_float(raw[c][2 * e + 1])), sc2, nm2);
-              if (32 * c + 2 * e >= valid) x.x = -INFINITY;
-              if (32 * c + 2 * e + 1 >= valid) x.y = -INFINITY;
-              pk[e] = fa::exp2_mufu(x);  // exact zeros for masked keys
+                for (int e = 0; e < 16; ++e) {
+                  const float2 x = fma2(
+                      make_float2(__uint_as_float(raw[cc][2 * e]), __uint_as_float(raw[cc][2 * e + 1])), sc2, nm2);
+                  pk[e] = ((kPolyChunks >> c) & 1u) ? fa::exp2_poly(x) : fa::exp2_mufu(x);
+                }
+              } else {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                  float2 x = fma2(
+                      make_float2(__uint_as_float(raw[cc][2 * e]), __uint_as_float(raw[cc][2 * e + 1])), sc2, nm2);
+                  if (32 * c + 2 * e >= valid) x.x = -INFINITY;
+                  if (32 * c + 2 * e + 1 >= valid) x.y = -INFINITY;
+                  pk[e] = fa::exp2_mufu(x);  // exact zeros for masked keys
+                }
+              }
+              tmem_st16(ts + 16 * c, pk);
             }
           }
-          if (full_tile || 32 * c < valid) tmem_st16(ts + 16 * c, pk);
         }
-#else
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          if (!full_tile && 64 * hf >= valid) break;  // P past the ragged tile's keys is never read
-          uint32_t raw[2][32];
-          tmem_ld32(ts + 64 * hf, raw[0]);
-          tmem_ld32(ts + 64 * hf + 32, raw[1]);
-          tmem_ld_wait();
-#pragma unroll
-          for (int cc = 0; cc < 2; ++cc) {
-            const int c = 2 * hf + cc;
-            if (!full_tile && 32 * c >= valid) break;
-            uint32_t pk[16];
-            if (full_tile) {
-#pragma unroll
-              for (int e = 0; e < 16; ++e) {
-                const float2 x =
-                    fma2(make_float2(__uint_as_float(raw[cc][2 * e]), __uint_as_float(raw[cc][2 * e + 1])), sc2, nm2);
-                pk[e] = ((kPolyChunks >> c) & 1u) ? fa::exp2_poly(x) : fa::exp2_mufu(x);
-              }
-            } else {
-#pragma unroll
-              for (int e = 0; e < 16; ++e) {
-                float2 x =
-                    fma2(make_float2(__uint_as_float(raw[cc][2 * e]), __uint_as_float(raw[cc][2 * e + 1])), sc2, nm2);
-                if (32 * c + 2 * e >= valid) x.x = -INFINITY;
-                if (32 * c + 2 * e + 1 >= valid) x.y = -INFINITY;
-                pk[e] = fa::exp2_mufu(x);  // exact zeros for masked keys
-              }
-            }
-            tmem_st16(ts + 16 * c, pk);
-          }
-        }
-#endif
         __syncwarp();
-        if (has1 && lane == 0) mbar_arrive(&order[g ^ 1]);
+        if (lane == 0) mbar_arrive(&order[g ^ 1]);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[g]);
       }
-      if (ok && mbar_wait(o_full, 0, abort_flag, err, kDevTimeoutAttn)) {
-        tc_fence_after();
-        uint32_t o2[2][32], l;
-        tmem_ld32(tmem + lane_base + t_o(g), o2[0]);
-        tmem_ld32(tmem + lane_base + t_o(g) + 32, o2[1]);
+      if (!ok) break;
+      // Epilogue: read O and l, release them to the next item's P V, then normalise and store.
+      if (!mbar_wait(&o_full[g], static_cast<uint32_t>(n) & 1u, abort_flag, err, kDevTimeoutAttn)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t packed[32];  // O / l as fp16 pairs, 32 columns at a time through registers
+      if (active) {
+        uint32_t o[32], l;
         fa::tmem_ld1(tmem + lane_base + t_l(g), l);
+        tmem_ld32(tmem + lane_base + t_o(g), o);
         tmem_ld_wait();
-        const uint32_t* o = &o2[0][0];
-        if (row < T_main) {
-          const float inv = 1.f / __uint_as_float(l);
-          uint4* dst = reinterpret_cast<uint4*>(out + (static_cast<size_t>(img) * T + row) * dim + h * HD);
+        const float inv = 1.f / __uint_as_float(l);
 #pragma unroll
-          for (int v4 = 0; v4 < 8; ++v4)
-            dst[v4] = make_uint4(pack_half2(__uint_as_float(o[8 * v4]) * inv, __uint_as_float(o[8 * v4 + 1]) * inv),
-                                 pack_half2(__uint_as_float(o[8 * v4 + 2]) * inv, __uint_as_float(o[8 * v4 + 3]) * inv),
-                                 pack_half2(__uint_as_float(o[8 * v4 + 4]) * inv, __uint_as_float(o[8 * v4 + 5]) * inv),
-                                 pack_half2(__uint_as_float(o[8 * v4 + 6]) * inv, __uint_as_float(o[8 * v4 + 7]) * inv));
-        }
+        for (int e = 0; e < 16; ++e) packed[e] = pack_half2(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
+        tmem_ld32(tmem + lane_base + t_o(g) + 32, o);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          packed[16 + e] = pack_half2(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_empty[g]);
+      if (active && row < T_main) {
+        uint4* dst = reinterpret_cast<uint4*>(out + (static_cast<size_t>(img) * T + row) * dim + h * HD);
+#pragma unroll
+        for (int v4 = 0; v4 < 8; ++v4)
+          dst[v4] = make_uint4(packed[4 * v4], packed[4 * v4 + 1], packed[4 * v4 + 2], packed[4 * v4 + 3]);
       }
     }
   }
@@ -575,6 +649,37 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, T_COLS);
+}
+
+// Per-device side stream for the tail-row kernel, created on first use (outside any stream capture: the
+// engine's first forward of a batch size runs eagerly). The mutex keeps one caller's fork/join pair intact.
+struct SideStream {
+  cudaStream_t stream = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+  std::mutex mu;
+};
+
+SideStream* side_stream(int dev) {
+  static SideStream streams[64];
+  static std::mutex create_mu;
+  if (dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(create_mu);
+  SideStream& ss = streams[dev];
+  if (ss.stream == nullptr) {
+    if (cudaStreamCreateWithFlags(&ss.stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming) != cudaSuccess) {
+      cudaGetLastError();
+      ss.stream = nullptr;
+      return nullptr;
+    }
+  }
+  return &ss;
+}
+
+int attention_tc_launches(int seq_len) {
+  const int rem = seq_len % fa::BQ;
+  return rem != 0 && rem <= fa::kTailRows && seq_len > fa::BQ ? 2 : 1;
 }
 
 int attention_tc(const void* qkv, void* out, int num_seqs, int seq_len, int heads, float scale, cudaStream_t s) {
@@ -594,14 +699,46 @@ int attention_tc(const void* qkv, void* out, int num_seqs, int seq_len, int head
       return check_launch("attention_tc: cudaFuncSetAttribute");
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  // Rows past the last full query tile go to one CUDA-core CTA per (image, head) when they are few.
-  const int rem = seq_len % BQ;
-  const int t_main = rem != 0 && rem <= kTailRows && seq_len > BQ ? seq_len - rem : seq_len;
-  const int tail_ctas = t_main < seq_len ? 1 : 0;
-  const dim3 grid((t_main + 2 * BQ - 1) / (2 * BQ) + tail_ctas, heads, num_seqs);
-  attention_tc_kernel<<<grid, THREADS, SMEM, s>>>(map, static_cast<const __half*>(qkv), static_cast<__half*>(out),
-                                                  seq_len, t_main, heads, scale * 1.4426950408889634f, err);
-  return check_launch("attention_tc_kernel");
+  const float scale_log2 = scale * 1.4426950408889634f;
+  const int t_main = attention_tc_launches(seq_len) == 2 ? seq_len - seq_len % BQ : seq_len;
+  const long long items = static_cast<long long>(num_seqs) * heads * ((t_main + 2 * BQ - 1) / (2 * BQ));
+  FF_REQUIRE(items <= 0x7fffffff, "attention: %lld work items", items);
+  const int grid = static_cast<int>(std::min<long long>(items, sm_count()));
+  // Rows past the last full query tile go to a CUDA-core kernel (one CTA per (head, image)) when they are
+  // few. When the tensor-core grid leaves SMs free (small batches), that kernel runs beside it on a side
+  // stream (fork/join by events, captured into graphs as such) instead of in front of it.
+  SideStream* side = nullptr;
+  if (t_main < seq_len) {
+    cudaStream_t ts = s;
+    if (grid + static_cast<long long>(num_seqs) * heads <= sm_count()) {
+      side = side_stream(dev);
+      FF_REQUIRE(side != nullptr, "attention: side stream creation failed");
+      side->mu.lock();
+      if (cudaEventRecord(side->fork, s) != cudaSuccess || cudaStreamWaitEvent(side->stream, side->fork, 0) != cudaSuccess) {
+        side->mu.unlock();
+        return check_launch("attention: fork");
+      }
+      ts = side->stream;
+    }
+    attention_tail_kernel<<<dim3(heads, num_seqs), THREADS, 0, ts>>>(static_cast<const __half*>(qkv),
+                                                                    static_cast<__half*>(out), seq_len, t_main, heads,
+                                                                    scale_log2);
+    rc = check_launch("attention_tail_kernel");
+    if (side != nullptr && rc == FF_OK && cudaEventRecord(side->join, side->stream) != cudaSuccess)
+      rc = check_launch("attention: join record");
+    if (rc != FF_OK) {
+      if (side != nullptr) side->mu.unlock();
+      return rc;
+    }
+  }
+  attention_tc_kernel<<<grid, THREADS, SMEM, s>>>(map, static_cast<__half*>(out), seq_len, t_main, heads, num_seqs,
+                                                  scale_log2, err);
+  rc = check_launch("attention_tc_kernel");
+  if (side != nullptr) {
+    if (cudaStreamWaitEvent(s, side->join, 0) != cudaSuccess && rc == FF_OK) rc = check_launch("attention: join");
+    side->mu.unlock();
+  }
+  return rc;
 }
 
 }  // namespace ff
