@@ -137,9 +137,15 @@ def measured_peaks() -> dict:
     return {"bf16": 1590.0, "bf16_sustained": 1400.0, "hbm": 6650.0, "source": "fallback"}
 
 
-def profiled_traffic(kernel: str) -> int | None:
-    """DRAM bytes per launch of `kernel` from the committed ncu launch-list summary (profiles/)."""
-    f = ROOT / "profiles" / "launches_eva02l_bs64.md"
+PROFILES = {("eva02-l-448", 64): "launches_eva02l_bs64.md", ("pixai-1008", 16): "launches_pixai1008_bs16.md"}
+
+
+def profiled_traffic(kernel: str, cfg_name: str, B: int) -> int | None:
+    """DRAM bytes per launch of `kernel` from the committed ncu launch-list summary of this workload."""
+    name = PROFILES.get((cfg_name, B))
+    if name is None:
+        return None
+    f = ROOT / "profiles" / name
     if not f.is_file():
         return None
     for line in f.read_text().splitlines():
@@ -357,10 +363,12 @@ def run_ours(args) -> None:
             "peak": peak,
             "unit": "TFLOP/s",
             "frac": achieved / peak,
-            "traffic": profiled_traffic("gemm_tc_kernel int8") if cfg.name == "eva02-l-448" and B == 64 else None,
-            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, averaged over the 96 "
-            "int8 GEMM launches of one bs64 forward (profiles/launches_eva02l_bs64.md); algorithmic bytes per "
-            "launch average 427 MB" if cfg.name == "eva02-l-448" and B == 64 else "not captured for this workload",
+            "traffic": profiled_traffic("gemm_tc_kernel int8", cfg.name, B),
+            "traffic_source": (
+                f"ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, averaged over the int8 GEMM launches "
+                f"of one forward (profiles/{PROFILES[(cfg.name, B)]}); algorithmic A + W + output bytes per launch "
+                f"average {427 if cfg.arch == 'eva02' else 667} MB"
+                if (cfg.name, B) in PROFILES else "not captured for this workload"),
             "peak_source": f"2 x bf16_tflops_sustained of MEASURED_PEAKS.json ({peaks['source']}): dense int8 runs "
             "at twice the dense bf16 rate on B200; int8 ops counted as 2 per multiply-add",
             "frac_of_nominal_4500": achieved / 4500.0,
