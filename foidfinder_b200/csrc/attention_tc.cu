@@ -234,7 +234,7 @@ __device__ __noinline__ void attention_tail_rows(const __half* __restrict__ qkv,
 }  // namespace fa
 
 // Rows past the last full query tile (see attention_tail_rows), one CTA per (head, image).
-__global__ void __launch_bounds__(fa::THREADS)
+__global__ void __launch_bounds__(fa::THREADS, 3)
     attention_tail_kernel(const __half* __restrict__ qkv, __half* __restrict__ out, int T, int T_main, int heads,
                           float scale_log2) {
   fa::attention_tail_rows(qkv, out, T, T_main, heads, scale_log2, blockIdx.y, blockIdx.x);
@@ -705,37 +705,32 @@ int attention_tc(const void* qkv, void* out, int num_seqs, int seq_len, int head
   FF_REQUIRE(items <= 0x7fffffff, "attention: %lld work items", items);
   const int grid = static_cast<int>(std::min<long long>(items, sm_count()));
   // Rows past the last full query tile go to a CUDA-core kernel (one CTA per (head, image)) when they are
-  // few. When the tensor-core grid leaves SMs free (small batches), that kernel runs beside it on a side
-  // stream (fork/join by events, captured into graphs as such) instead of in front of it.
+  // few. It runs beside the tensor-core kernel on a side stream (fork/join by events, captured into graphs
+  // as such), submitted after it: its CTAs (64 registers, 10.5 KB) fit next to a persistent attention CTA
+  // on the same SM, so they fill the issue slots the softmax chain leaves idle.
   SideStream* side = nullptr;
   if (t_main < seq_len) {
-    cudaStream_t ts = s;
-    if (grid + static_cast<long long>(num_seqs) * heads <= sm_count()) {
-      side = side_stream(dev);
-      FF_REQUIRE(side != nullptr, "attention: side stream creation failed");
-      side->mu.lock();
-      if (cudaEventRecord(side->fork, s) != cudaSuccess || cudaStreamWaitEvent(side->stream, side->fork, 0) != cudaSuccess) {
-        side->mu.unlock();
-        return check_launch("attention: fork");
-      }
-      ts = side->stream;
-    }
-    attention_tail_kernel<<<dim3(heads, num_seqs), THREADS, 0, ts>>>(static_cast<const __half*>(qkv),
-                                                                    static_cast<__half*>(out), seq_len, t_main, heads,
-                                                                    scale_log2);
-    rc = check_launch("attention_tail_kernel");
-    if (side != nullptr && rc == FF_OK && cudaEventRecord(side->join, side->stream) != cudaSuccess)
-      rc = check_launch("attention: join record");
-    if (rc != FF_OK) {
-      if (side != nullptr) side->mu.unlock();
-      return rc;
+    side = side_stream(dev);
+    FF_REQUIRE(side != nullptr, "attention: side stream creation failed");
+    side->mu.lock();
+    if (cudaEventRecord(side->fork, s) != cudaSuccess || cudaStreamWaitEvent(side->stream, side->fork, 0) != cudaSuccess) {
+      side->mu.unlock();
+      return check_launch("attention: fork");
     }
   }
   attention_tc_kernel<<<grid, THREADS, SMEM, s>>>(map, static_cast<__half*>(out), seq_len, t_main, heads, num_seqs,
                                                   scale_log2, err);
   rc = check_launch("attention_tc_kernel");
   if (side != nullptr) {
-    if (cudaStreamWaitEvent(s, side->join, 0) != cudaSuccess && rc == FF_OK) rc = check_launch("attention: join");
+    if (rc == FF_OK) {
+      attention_tail_kernel<<<dim3(heads, num_seqs), THREADS, 0, side->stream>>>(
+          static_cast<const __half*>(qkv), static_cast<__half*>(out), seq_len, t_main, heads, scale_log2);
+      rc = check_launch("attention_tail_kernel");
+    }
+    // Join even after a failed launch, so the side stream never leaves work unjoined in a capture.
+    if (cudaEventRecord(side->join, side->stream) != cudaSuccess || cudaStreamWaitEvent(s, side->join, 0) != cudaSuccess) {
+      if (rc == FF_OK) rc = check_launch("attention: join");
+    }
     side->mu.unlock();
   }
   return rc;
