@@ -28,6 +28,7 @@ STATUS = {
 # (foidfinder/backends/cuda/csrc/gemm.cuh:8-12).
 EPI_QKV_ROPE, EPI_RESIDUAL, EPI_SWIGLU, EPI_BIAS, EPI_S32, EPI_STEM, EPI_LOGITS = 0, 1, 3, 4, 5, 6, 7
 EPI_GELU = 2
+TILE_PAIR256 = 512  # ff_gemm_s8 tile_n: 256 x 256 tiles over a cluster of two CTAs (FF_TILE_PAIR256)
 
 # ff_engine_profile kernel classes (FF_PROF_*).
 PROF_CLASSES = ("stem_prep", "stem_gemm", "rotate", "gemm_qkv", "attention", "gemm_proj", "gemm_fc1", "gemm_fc2", "head")

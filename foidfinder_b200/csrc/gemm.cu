@@ -26,6 +26,43 @@ int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& 
   return check_launch("gemm_tc_kernel");
 }
 
+// Pair tiles (256 x BN over a cluster of two CTAs): as many clusters as fit at once, each walking tiles.
+constexpr int kPairStages = 6;
+
+template <int EPI>
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& a,
+                cudaStream_t stream) {
+  using C = GemmCfg<256, kPairStages, true>;
+  auto kernel = gemm_tc_kernel<256, kPairStages, false, EPI, true>;
+  static int max_clusters[64] = {};  // per instantiation and device, 0 = not configured yet
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = dev >= 0 && dev < 64 ? max_clusters[dev] : 0;
+  if (clusters == 0) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+      return check_launch("gemm (pair): cudaFuncSetAttribute");
+    cfg.gridDim = dim3(2 * (sm_count() / 2));
+    if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess || clusters < 1)
+      return check_launch("gemm (pair): cudaOccupancyMaxActiveClusters");
+    if (dev >= 0 && dev < 64) max_clusters[dev] = clusters;
+  }
+  const int tiles = a.tiles_m * (a.N / 256);
+  cfg.gridDim = dim3(2 * (tiles < clusters ? tiles : clusters));
+  if (cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, a) != cudaSuccess) return check_launch("gemm_tc_kernel (pair)");
+  return check_launch("gemm_tc_kernel (pair)");
+}
+
 template <int BN, bool F16IN>
 int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& a,
                  cudaStream_t s) {
@@ -52,6 +89,21 @@ int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CU
 
 }  // namespace
 
+bool pair_supported(int N, int bn, bool f16, int epi) {
+  return !f16 && bn == 256 && N % 256 == 0 &&
+         (epi == EPI_QKV_ROPE || epi == EPI_RESIDUAL || epi == EPI_SWIGLU || epi == EPI_BIAS || epi == EPI_GELU_F16 ||
+          epi == EPI_S32);
+}
+
+// Pair tiles pay off on long K loops (measured at M = 65,600: K = 2816 +5-6%; K = 1024 within +-3%, the
+// epilogue's output traffic being what bounds those) once there are enough 256-row tiles to keep every SM
+// pair busy for a few waves.
+bool choose_pair(int M, int N, int K, int bn, bool f16, int epi) {
+  if (!pair_supported(N, bn, f16, epi) || epi == EPI_S32 || K < 2048) return false;
+  const long long pair_tiles = static_cast<long long>((M + 255) / 256) * (N / 256);
+  return pair_tiles >= 2LL * sm_count();
+}
+
 int choose_tile_n(int M, int N) {
   // Prefer 256-wide tiles; drop to 128 when 256 would leave most SMs idle (small M) or N needs it.
   if (N % 256 != 0) return 128;
@@ -66,15 +118,18 @@ int gemm_prepare(const GemmProblem& p, GemmPlan* plan) {
   FF_REQUIRE(p.M >= 1 && p.N >= 1 && p.K >= 1, "gemm: bad shape M=%d N=%d K=%d", p.M, p.N, p.K);
   FF_REQUIRE((static_cast<int64_t>(p.K) * elt) % 128 == 0, "gemm: K*%d bytes must be a multiple of 128 (K=%d)", elt, p.K);
   FF_REQUIRE(aligned16(p.A) && aligned16(p.W), "gemm: A and W must be 16-byte aligned");
-  int bn = p.tile_n == 0 ? choose_tile_n(p.M, p.N) : p.tile_n;
-  FF_REQUIRE(bn == 128 || bn == 256, "gemm: tile_n must be 0, 128 or 256 (got %d)", p.tile_n);
+  int bn = p.tile_n == 0 ? choose_tile_n(p.M, p.N) : p.tile_n == FF_TILE_PAIR256 ? 256 : p.tile_n;
+  FF_REQUIRE(bn == 128 || bn == 256, "gemm: tile_n must be 0, 128, 256 or FF_TILE_PAIR256 (got %d)", p.tile_n);
+  const bool pair = p.tile_n == FF_TILE_PAIR256 || (p.tile_n == 0 && choose_pair(p.M, p.N, p.K, bn, f16, p.epi));
+  FF_REQUIRE(!pair || pair_supported(p.N, bn, f16, p.epi),
+             "gemm: pair tiles need int8 operands, N %% 256 == 0 and an s32/bias/QKV/SwiGLU/GELU/residual epilogue");
   FF_REQUIRE(p.N % bn == 0, "gemm: N=%d must be a multiple of the tile width %d", p.N, bn);
   const CUtensorMapDataType dt = f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   const uint32_t box_k = 128 / elt;
   int rc = make_tmap_2d(&plan->ta, p.A, dt, elt, static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.M), box_k, 128);
   if (rc != FF_OK) return rc;
   rc = make_tmap_2d(&plan->tb, p.W, dt, elt, static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.N), box_k,
-                    static_cast<uint32_t>(bn));
+                    static_cast<uint32_t>(pair ? bn / 2 : bn));  // a pair CTA loads half of the tile's W rows
   if (rc != FF_OK) return rc;
   // Output map for the TMA-store (and, for the residual, TMA add-reduce) epilogues: fp16 [M, out_cols] with
   // row pitch ldo, boxes of 32 rows x
@@ -98,17 +153,30 @@ int gemm_prepare(const GemmProblem& p, GemmPlan* plan) {
   plan->args.N = p.N;
   plan->args.K = p.K;
   plan->args.num_kb = static_cast<int>((static_cast<int64_t>(p.K) * elt) / 128);
-  plan->args.tiles_m = (p.M + 127) / 128;
+  plan->args.tiles_m = pair ? (p.M + 255) / 256 : (p.M + 127) / 128;
   plan->args.out = p.out;
   plan->args.err = p.err_word != nullptr ? p.err_word : device_error_word();
   FF_REQUIRE(plan->args.err != nullptr, "gemm: no device error word");
   plan->bn = bn;
+  plan->pair = pair;
   plan->f16 = f16;
   plan->epi = p.epi;
   return FF_OK;
 }
 
 int gemm_launch(const GemmPlan& plan, cudaStream_t stream) {
+  if (plan.pair) {
+    switch (plan.epi) {
+      case EPI_QKV_ROPE: return launch_pair<EPI_QKV_ROPE>(plan.ta, plan.tb, plan.tc, plan.args, stream);
+      case EPI_RESIDUAL: return launch_pair<EPI_RESIDUAL>(plan.ta, plan.tb, plan.tc, plan.args, stream);
+      case EPI_SWIGLU: return launch_pair<EPI_SWIGLU>(plan.ta, plan.tb, plan.tc, plan.args, stream);
+      case EPI_BIAS: return launch_pair<EPI_BIAS>(plan.ta, plan.tb, plan.tc, plan.args, stream);
+      case EPI_GELU_F16: return launch_pair<EPI_GELU_F16>(plan.ta, plan.tb, plan.tc, plan.args, stream);
+      case EPI_S32: return launch_pair<EPI_S32>(plan.ta, plan.tb, plan.tc, plan.args, stream);
+    }
+    set_error("gemm: epilogue %d has no pair-tile kernel", plan.epi);
+    return FF_ERR_INVALID_ARGUMENT;
+  }
   if (plan.f16)
     return plan.bn == 256 ? dispatch_epi<256, true>(plan.epi, plan.ta, plan.tb, plan.tc, plan.args, stream)
                           : dispatch_epi<128, true>(plan.epi, plan.ta, plan.tb, plan.tc, plan.args, stream);

@@ -24,11 +24,13 @@ struct GemmPlan {
   CUtensorMap ta, tb, tc;  // tc: fp16 output, for the epilogues that store through TMA
   GemmArgs args;
   int bn;
+  bool pair;  // 256-row tiles over a cluster of two CTAs
   bool f16;
   int epi;
 };
 
 int choose_tile_n(int M, int N);
+bool choose_pair(int M, int N, int K, int bn, bool f16, int epi);
 int gemm_prepare(const GemmProblem& p, GemmPlan* plan);
 int gemm_launch(const GemmPlan& plan, cudaStream_t stream);
 

@@ -16,23 +16,35 @@
 // epilogue of one tile hides under the next tile's mainloop as far as possible.
 // Accumulators are double-buffered in TMEM (2 x BN columns), so the epilogue of tile i overlaps the
 // mainloop of tile i+1. Stages are a ring of STAGES smem buffers guarded by full/empty mbarriers.
+//
+// PAIR: clusters of two CTAs on two SMs share 256-row tiles through tcgen05.mma.cta_group::2 (M = 256):
+// each CTA loads its own 128 rows of A and half of B's BN rows, the even CTA issues the MMAs, and each
+// CTA's TMEM receives its 128 rows of the accumulator. Per SM this halves the B bytes moved through
+// shared memory per multiply-add, which bounds the single-CTA mainloop (TMA writes + MMA operand reads
+// of 48 KB per 128-byte K step against the shared-memory bandwidth). Both CTAs' copies of a stage signal
+// the even CTA's full barrier (cta_group::2 loads, no multicast: each CTA loads its own rows); the MMA
+// commits arrive on both CTAs' empty / accumulator-full barriers at once (commit with a CTA mask); the odd
+// CTA's epilogue warps release the accumulator on the even CTA's tempty barrier (mapa address).
 #pragma once
 #include "ptx.cuh"
 #include "gemm_args.h"
 
 namespace ff {
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool PAIR = false>
 struct GemmCfg {
-  static constexpr int BM = 128;
+  static constexpr int BM = 128;    // rows per CTA (a PAIR tile is 2 x BM)
+  static constexpr int TILE_M = PAIR ? 2 * BM : BM;
   static constexpr int BKB = 128;  // K bytes per stage (one 128-byte swizzle row)
   static constexpr int A_BYTES = BM * BKB;
-  static constexpr int B_BYTES = BN * BKB;
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // W rows this CTA loads per stage
+  static constexpr int B_BYTES = B_ROWS * BKB;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;  // double-buffered accumulator
   static constexpr int EPI_WARPS = 8;       // two per TMEM sub-partition, each owning half the tile's columns
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
-  static constexpr int STAGING = 4096;      // per epilogue warp: 32 rows x 128 B
+  static constexpr int STAGING = 4096;      // per epilogue warp: 32 rows x 128 B (one TMA store in flight;
+                                            // a second buffer measured no faster and costs a stage)
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM = 1024 /*alignment slack*/ + STAGES * STAGE_BYTES + EPI_WARPS * STAGING + BAR_BYTES;
   static_assert(BN == 128 || BN == 256, "BN");
@@ -107,14 +119,15 @@ __device__ __forceinline__ void dequant32(const uint32_t (&r)[32], float rs, con
   }
 }
 
-template <int BN, int STAGES, bool F16IN, int EPI>
-__global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
+template <int BN, int STAGES, bool F16IN, int EPI, bool PAIR = false>
+__global__ void __launch_bounds__(GemmCfg<BN, STAGES, PAIR>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
   // fp16 outputs of these epilogues leave through TMA stores of the swizzled staging buffer (tmC).
   constexpr bool kTmaStore =
       EPI == EPI_BIAS || EPI == EPI_QKV_ROPE || EPI == EPI_SWIGLU || EPI == EPI_RESIDUAL || EPI == EPI_GELU_F16;
-  using C = GemmCfg<BN, STAGES>;
+  static_assert(!PAIR || !F16IN, "pair tiles are built for the int8 GEMMs");
+  using C = GemmCfg<BN, STAGES, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = smem + STAGES * C::STAGE_BYTES;
@@ -128,7 +141,18 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_n = args.N / BN;
-  const int tiles = args.tiles_m * tiles_n;
+  const int tiles = args.tiles_m * tiles_n;  // tiles_m counts TILE_M-row tiles
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int unit = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);  // CTA or pair
+  const int units = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  // Waits on barriers the other CTA of a pair arrives on take cluster-scope acquire.
+  auto wait = [&](uint64_t* bar, uint32_t parity, int code) {
+    if constexpr (PAIR)
+      return mbar_wait_cluster(bar, parity, abort_flag, args.err, code);
+    else
+      return mbar_wait(bar, parity, abort_flag, args.err, code);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -137,7 +161,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], C::EPI_WARPS);  // one arrive per epilogue warp
+      mbar_init(&tempty[a], (PAIR ? 2 : 1) * C::EPI_WARPS);  // one arrive per epilogue warp (of both CTAs)
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -148,11 +172,17 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
     tma_prefetch_map(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc2(tmem_slot, C::TMEM_COLS);
+      tmem_relinquish2();
+    } else {
+      tmem_alloc(tmem_slot, C::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
@@ -166,17 +196,26 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
       for (int s = 0; s < STAGES; ++s) last_phase[s] = -1;
       constexpr int kElemsPerStage = F16IN ? C::BKB / 2 : C::BKB;
       bool ok = true;
-      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      for (int t = unit; t < tiles && ok; t += units) {
         const int tm = t / tiles_n, tn = t % tiles_n;
         for (int kb = 0; kb < args.num_kb; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, args.err, kDevTimeoutSmemEmpty)) {
+          if (!wait(&empty[stage], phase ^ 1u, kDevTimeoutSmemEmpty)) {
             ok = false;
             break;
           }
           uint8_t* sa = smem + stage * C::STAGE_BYTES;
-          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-          tma_load_2d(sa, &tmA, &full[stage], kb * kElemsPerStage, tm * C::BM);
-          tma_load_2d(sa + C::A_BYTES, &tmB, &full[stage], kb * kElemsPerStage, tn * BN);
+          if constexpr (PAIR) {
+            // Both CTAs' copies of this stage complete on the even CTA's full barrier.
+            if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+            const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0u);
+            tma_load_2d_pair(sa, &tmA, fb, kb * kElemsPerStage, tm * C::TILE_M + static_cast<int>(rank) * C::BM);
+            tma_load_2d_pair(sa + C::A_BYTES, &tmB, fb, kb * kElemsPerStage,
+                             tn * BN + static_cast<int>(rank) * C::B_ROWS);
+          } else {
+            mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+            tma_load_2d(sa, &tmA, &full[stage], kb * kElemsPerStage, tm * C::BM);
+            tma_load_2d(sa + C::A_BYTES, &tmB, &full[stage], kb * kElemsPerStage, tn * BN);
+          }
           last_phase[stage] = static_cast<int>(phase);
           if (++stage == STAGES) {
             stage = 0;
@@ -184,8 +223,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
           }
         }
       }
-      if (!ok) {
-        // Let every issued copy land before the CTA exits (bounded).
+      if (!ok && leader) {
+        // Let every issued copy land before the CTA exits (bounded). In a pair the even CTA's full barrier
+        // also counts the odd CTA's copies, and the odd CTA stays resident until the even one is done.
         for (int s = 0; s < STAGES; ++s)
           if (last_phase[s] >= 0) {
             const uint32_t addr = smem_u32(&full[s]);
@@ -196,23 +236,35 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = F16IN ? idesc_f16(128, BN) : idesc_s8(128, BN);
+    // ------------------------------------------------------------ MMA issuer (the even CTA of a pair)
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = F16IN ? idesc_f16(128, BN) : idesc_s8(C::TILE_M, BN);
+      auto commit = [&](uint64_t* bar) {  // local barrier
+        if constexpr (PAIR)
+          tc_commit2(bar);
+        else
+          tc_commit(bar);
+      };
+      auto commit_both = [&](uint64_t* bar) {  // the barrier of both CTAs of a pair
+        if constexpr (PAIR)
+          tc_commit2_both(bar);
+        else
+          tc_commit(bar);
+      };
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, args.err, kDevTimeoutTmemEmpty)) {
+      for (int t = unit; t < tiles && ok; t += units) {
+        if (!wait(&tempty[acc], acc_phase ^ 1u, kDevTimeoutTmemEmpty)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d = tmem + static_cast<uint32_t>(acc * BN);
         for (int kb = 0; kb < args.num_kb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, args.err, kDevTimeoutTmaFull)) {
+          if (!wait(&full[stage], phase, kDevTimeoutTmaFull)) {
             ok = false;
             break;
           }
@@ -225,24 +277,26 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
             const uint64_t step = static_cast<uint64_t>(k * 2);  // (32 bytes) >> 4
             if constexpr (F16IN)
               mma_f16(d, adesc + step, bdesc + step, idesc, (kb | k) != 0);
+            else if constexpr (PAIR)
+              mma_i8_pair(d, adesc + step, bdesc + step, idesc, (kb | k) != 0);
             else
               mma_i8(d, adesc + step, bdesc + step, idesc, (kb | k) != 0);
           }
-          tc_commit(&empty[stage]);  // frees the stage once these MMAs have read it
+          commit_both(&empty[stage]);  // frees the stage (in both CTAs) once these MMAs have read it
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        tc_commit(&tfull[acc]);  // accumulator ready for the epilogue
+        commit_both(&tfull[acc]);  // accumulator ready for the epilogue (of both CTAs)
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
         }
       }
       // Drain: every MMA this thread issued must finish before TMEM is released.
-      tc_commit(drain);
+      commit(drain);
       const uint32_t addr = smem_u32(drain);
       const unsigned long long t0 = globaltimer();
       while (!mbar_try_wait(addr, 0)) {
@@ -258,15 +312,15 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
     const int q = warp & 3;         // TMEM sub-partition (lanes 32q..32q+31) this warp can read
     const int half = ew >> 2;       // which half of the tile's columns this warp owns
     const int row_in_tile = q * 32 + lane;
-    uint8_t* stg = staging + ew * C::STAGING;
+    uint8_t* const stg = staging + ew * C::STAGING;
     constexpr int HALF = BN / 2;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, args.err, kDevTimeoutTmemFull)) break;
+    for (int t = unit; t < tiles; t += units) {
+      if (!wait(&tfull[acc], acc_phase, kDevTimeoutTmemFull)) break;
       tc_fence_after();
       const int tm = t / tiles_n, tn = t % tiles_n;
-      const int m_block = tm * C::BM + q * 32;  // first row of this warp's 32-row block
+      const int m_block = tm * C::TILE_M + static_cast<int>(rank) * C::BM + q * 32;  // this warp's 32-row block
       const int m = m_block + row_in_tile - q * 32;
       const bool row_ok = m < args.M;
       const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
@@ -424,7 +478,12 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (lane == 0) {
+        if (PAIR && !leader)
+          mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0u));  // the even CTA's MMA reuses it
+        else
+          mbar_arrive(&tempty[acc]);
+      }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
@@ -437,8 +496,14 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES>::THREADS, 1)
   __syncwarp();
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the even CTA's MMAs into this CTA's TMEM have drained
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+  if (warp == 1) {
+    if constexpr (PAIR)
+      tmem_dealloc2(tmem, C::TMEM_COLS);
+    else
+      tmem_dealloc(tmem, C::TMEM_COLS);
+  }
 }
 
 }  // namespace ff

@@ -44,7 +44,7 @@ def _time(fn, iters: int, warmup: int = 3) -> float:
     return s.elapsed_time(e) / iters
 
 
-def bench_gemm(batch: int, shapes: list[str], iters: int, epi: str) -> None:
+def bench_gemm(batch: int, shapes: list[str], iters: int, epi: str, tile: int = 0) -> None:
     d = torch.device("cuda")
     g = torch.Generator(device=d).manual_seed(0)
     M = TOKENS * batch
@@ -64,11 +64,12 @@ def bench_gemm(batch: int, shapes: list[str], iters: int, epi: str) -> None:
 
             cos, sin = (t.t().contiguous().to(d) for t in rope_tables(32, 16))  # angle-major
             rope = dict(rope_cos=cos, rope_sin=sin, rope_cols=2 * N // 3, tokens=TOKENS)
-        ms = _time(lambda: ops.gemm_s8(A, W, rs, cs, b, out, e, **rope), iters)
+        ms = _time(lambda: ops.gemm_s8(A, W, rs, cs, b, out, e, tile_n=tile, **rope), iters)
         n_alg = {"1024x5632": 5460, "2816x1024": 1024}.get(name, N)
         k_alg = 2730 if name == "2816x1024" else K
         ops_alg = 2 * M * n_alg * k_alg
         print(json.dumps({"kernel": "gemm_s8", "shape": name, "what": what, "M": M, "N": N, "K": K, "epilogue": epi,
+                          "tile_n": tile,
                           "ms": ms, "tflops": ops_alg / ms / 1e9,
                           "bytes": M * K + N * K + out.numel() * 2, "gbs": (M * K + N * K + out.numel() * 2) / ms / 1e6}))
 
@@ -118,13 +119,14 @@ def main() -> None:
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--shape", action="append", choices=sorted(GEMM_SHAPES))
     ap.add_argument("--epilogue", default="bias", choices=("bias", "swiglu", "residual", "qkv_rope"))
+    ap.add_argument("--tile", type=int, default=0, help="gemm: tile_n (0 auto, 128, 256, 512 = pair tiles)")
     ap.add_argument("--rope", action="store_true")
     ap.add_argument("--seq", type=int, default=TOKENS, help="attention: sequence length")
     ap.add_argument("--tokens", type=int, default=TOKENS, help="rotate: rows per image")
     ap.add_argument("--cols", type=int, action="append", choices=sorted(ROT_CASES), help="rotate: row widths")
     a = ap.parse_args()
     if a.kernel == "gemm":
-        bench_gemm(a.batch, a.shape or list(GEMM_SHAPES), a.iters, a.epilogue)
+        bench_gemm(a.batch, a.shape or list(GEMM_SHAPES), a.iters, a.epilogue, a.tile)
     elif a.kernel == "attention":
         bench_attention(a.batch, a.iters, a.rope, a.seq)
     else:

@@ -11,10 +11,12 @@ import ctypes as C
 import torch
 
 from . import _lib
-from ._lib import EPI_BIAS, EPI_GELU, EPI_LOGITS, EPI_QKV_ROPE, EPI_RESIDUAL, EPI_S32, EPI_STEM, EPI_SWIGLU, check, lib
+from ._lib import (
+    EPI_BIAS, EPI_GELU, EPI_LOGITS, EPI_QKV_ROPE, EPI_RESIDUAL, EPI_S32, EPI_STEM, EPI_SWIGLU, TILE_PAIR256, check, lib,
+)
 
 __all__ = [
-    "EPI_QKV_ROPE", "EPI_RESIDUAL", "EPI_SWIGLU", "EPI_BIAS", "EPI_S32", "EPI_STEM", "EPI_LOGITS", "EPI_GELU",
+    "EPI_QKV_ROPE", "EPI_RESIDUAL", "EPI_SWIGLU", "EPI_BIAS", "EPI_S32", "EPI_STEM", "EPI_LOGITS", "EPI_GELU", "TILE_PAIR256",
     "gemm_s8", "gemm_f16", "rot_q8", "rot_q8_1024", "rot_q8_h128", "attention", "patchify", "fill_cls",
     "layernorm", "topk", "tree_pool", "resize_pad", "patchify_windowed", "layernorm_pos", "pool_query_attention",
 ]

@@ -55,11 +55,15 @@ int ff_device_error(int device, int* code, int clear);
  *   A [M, K] int8 (per-token codes), W [N, K] int8 (per-channel codes), K % 128 == 0, N % 128 == 0.
  *   rope_cos / rope_sin [32, tokens] f32 (angle-major) are read only by FF_EPI_QKV_ROPE: row m uses
  *   position m % tokens, and pair (2i, 2i+1) of every 64-wide head uses angle row (i % 32).
- *   tile_n: 0 = automatic, else 128 or 256 output columns per CTA tile.
+ *   tile_n: 0 = automatic, else 128 or 256 output columns per CTA tile (128 rows), or FF_TILE_PAIR256:
+ *           256 x 256 tiles over a cluster of two CTAs on two SMs (tcgen05 cta_group::2; int8 operands,
+ *           N % 256 == 0). Automatic picks the pair tiles for K >= 2048 when there are at least two
+ *           256 x 256 tiles per SM.
  * Replaces torch.ops.foidfinder.gemm_s8 (foidfinder/backends/cuda/csrc/kernels.cu:187-217, schema
  * kernels.cu:267-271); the reference's `stages` knob becomes `tile_n`, and its q_scale is folded into
  * the q rows of W and bias at conversion time.
  */
+#define FF_TILE_PAIR256 512
 int ff_gemm_s8(const int8_t* A, const int8_t* W, const float* row_scale, const float* col_scale, const float* bias,
                void* out, int M, int N, int K, int epi, const float* rope_cos, const float* rope_sin, int rope_cols,
                int tokens, int tile_n, void* stream);

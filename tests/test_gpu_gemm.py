@@ -29,7 +29,20 @@ S32_CASES = [
 ]
 
 
-@pytest.mark.parametrize(("M", "N", "K", "tile"), S32_CASES)
+PAIR = 512  # ops.TILE_PAIR256: 256 x 256 tiles over a cluster of two CTAs (tcgen05 cta_group::2)
+
+# Pair tiles, smallest first: one pair tile, a ragged last 256-row tile, several tiles per cluster.
+PAIR_S32_CASES = [
+    (256, 256, 128, PAIR),
+    (300, 256, 256, PAIR),
+    (1025, 3072, 1024, PAIR),
+    (2050, 5632, 1024, PAIR),
+    (4100, 2304, 768, PAIR),
+    (65600 // 4, 1024, 2816, PAIR),
+]
+
+
+@pytest.mark.parametrize(("M", "N", "K", "tile"), PAIR_S32_CASES + S32_CASES)
 def test_gemm_s8_int32_bit_exact(cuda_device, no_device_error, M, N, K, tile):
     g = torch.Generator().manual_seed(M * 131 + N * 7 + K)
     A, W = _rand_i8((M, K), g), _rand_i8((N, K), g)
@@ -49,7 +62,7 @@ def _dequant_case(M, N, K, gen):
     return A, W, rs, cs, b
 
 
-@pytest.mark.parametrize("tile", [128, 256])
+@pytest.mark.parametrize("tile", [128, 256, PAIR])
 def test_gemm_s8_bias_epilogue(cuda_device, no_device_error, tile):
     from foidfinder_b200 import ops
 
@@ -63,7 +76,7 @@ def test_gemm_s8_bias_epilogue(cuda_device, no_device_error, tile):
     torch.testing.assert_close(out.float().cpu(), ref.half().float(), atol=1e-3, rtol=2e-3)
 
 
-@pytest.mark.parametrize("tile", [128, 256])
+@pytest.mark.parametrize("tile", [128, 256, PAIR])
 def test_gemm_s8_residual_epilogue(cuda_device, no_device_error, tile):
     """x = fp16(x + fp16(y)): the reference stages y in fp16 and adds with __hadd2
     (foidfinder/backends/cuda/csrc/gemm.cuh:153-169); here a TMA add-reduction does the same add."""
@@ -83,7 +96,7 @@ def test_gemm_s8_residual_epilogue(cuda_device, no_device_error, tile):
     assert (got == ref).float().mean().item() > 0.999
 
 
-@pytest.mark.parametrize("tile", [128, 256])
+@pytest.mark.parametrize("tile", [128, 256, PAIR])
 def test_gemm_s8_swiglu_epilogue(cuda_device, no_device_error, tile):
     from foidfinder_b200 import ops
 
@@ -100,7 +113,8 @@ def test_gemm_s8_swiglu_epilogue(cuda_device, no_device_error, tile):
     torch.testing.assert_close(out.float().cpu(), ref.half().float(), atol=2e-3, rtol=3e-3)
 
 
-def test_gemm_s8_qkv_rope_epilogue(cuda_device, no_device_error):
+@pytest.mark.parametrize("tile", [0, PAIR])
+def test_gemm_s8_qkv_rope_epilogue(cuda_device, no_device_error, tile):
     from foidfinder_b200 import ops
 
     tokens, dim = 1025, 1024
@@ -117,6 +131,7 @@ def test_gemm_s8_qkv_rope_epilogue(cuda_device, no_device_error):
     ops.gemm_s8(
         A.to(d), W.to(d), rs.to(d), cs.to(d), b.to(d), out, ops.EPI_QKV_ROPE,
         rope_cos=cos.t().contiguous().to(d), rope_sin=sin.t().contiguous().to(d), rope_cols=2 * dim, tokens=tokens,
+        tile_n=tile,
     )
     torch.cuda.synchronize()
     torch.testing.assert_close(out.float().cpu(), ref.half().float(), atol=2e-3, rtol=3e-3)

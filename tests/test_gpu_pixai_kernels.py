@@ -19,7 +19,7 @@ def _rand_i8(shape, gen):
     return torch.randint(-127, 128, shape, generator=gen, dtype=torch.int8)
 
 
-@pytest.mark.parametrize(("N", "tile"), [(4736, 128), (4736, 0), (2048, 256)])
+@pytest.mark.parametrize(("N", "tile"), [(4736, 128), (4736, 0), (2048, 256), (4864, 512)])
 def test_gemm_s8_gelu_epilogue(cuda_device, no_device_error, N, tile):
     """fp16 out = gelu_tanh(acc * rs * cs + b) (foidfinder/backends/cuda/csrc/gemm.cuh:137-140, common.cuh:56).
     4736 = 18.5 x 256 columns: only the 128-wide tile fits it."""
