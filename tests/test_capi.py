@@ -136,3 +136,27 @@ def test_struct_layouts_match_ctypes(tmp_path):
         assert int(got[f"{cname} size"]) == C.sizeof(py), cname
         for field, _ in py._fields_:
             assert int(got[f"{cname}.{field}"]) == getattr(py, field).offset, f"{cname}.{field}"
+
+
+def test_pair_tiles_need_int8_and_256_columns():
+    pair = DEFINES["FF_TILE_PAIR256"]
+    rc = _lib.lib().ff_gemm_s8(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 512, 384, 128, _lib.EPI_BIAS, None, None, 0, 1, pair,
+                               None)
+    assert rc == DEFINES["FF_ERR_INVALID_ARGUMENT"]
+    assert "pair tiles" in _err() or "multiple of the tile width" in _err()
+    rc = _lib.lib().ff_gemm_f16(FAKE, FAKE, FAKE, FAKE, 512, 256, 128, _lib.EPI_BIAS, 256, 256, None, 0, 0, pair, None)
+    assert rc == DEFINES["FF_ERR_INVALID_ARGUMENT"]
+    assert "pair tiles need int8" in _err()
+
+
+@pytest.mark.parametrize(("name", "launches"), [("eva02-l-448", 3 + 10 * 24 + 1 + 1 + 1),
+                                                 ("eva02-b-448", 3 + 10 * 12 + 7 + 1 + 1),
+                                                 ("pixai-1008", 3 + 9 * 32 + 4 + 1 + 1)])
+def test_launches_per_forward(name, launches):
+    """Kernel launches of one forward: 9 per block (+1 where the attention has CUDA-core tail rows: 1025
+    tokens), the head's launches, the tag GEMM and the top-k."""
+    from foidfinder_b200.config import CONFIGS
+    from foidfinder_b200.engine import c_config
+
+    cfg = c_config(CONFIGS[name])
+    assert _lib.lib().ff_engine_launches_per_forward(C.byref(cfg)) == launches
