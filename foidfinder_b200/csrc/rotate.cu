@@ -379,6 +379,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 
 namespace {
 
+// Below this many rows of at most 1024 columns the per-row grid wins (a few rows per warp leave the
+// persistent kernel's prologue and TMEM fill unamortised; measured at 8,200 x 1024: 15.3 vs 17.4 us, at
+// 65,600 x 1024: 79 vs 72 us).
+constexpr int kPersistMinRows1024 = 32768;
 #ifndef FF_ROT_PWARPS
 #define FF_ROT_PWARPS 24
 #endif
@@ -410,11 +414,13 @@ int launch_persistent(const __half* x, const float* g, const float* b, float eps
 template <int NCH, int BLOCK>
 int launch_rot(const __half* x, const float* g, const float* b, float eps, int rows, int valid, int8_t* out,
                float* rs, int* err, cudaStream_t s) {
-  // LayerNorm rows take the persistent kernel (gamma/beta in TMEM). Rows without a norm need no per-row
+  // LayerNorm rows take the persistent kernel (gamma/beta in TMEM) unless there are few of them. Rows
+  // without a norm need no per-row
   // constants and run faster on the per-row grid, whose higher occupancy hides the HBM latency (measured:
   // 48 vs 64 us for 65,600 x 1024). The widest rows (4096) do not fit the persistent kernel's staging.
   if constexpr (NCH <= 11) {
-    if (g != nullptr) return launch_persistent<NCH, BLOCK, true>(x, g, b, eps, rows, valid, out, rs, err, s);
+    if (g != nullptr && (NCH > 4 || rows >= kPersistMinRows1024))
+      return launch_persistent<NCH, BLOCK, true>(x, g, b, eps, rows, valid, out, rs, err, s);
   }
   const dim3 grid((rows + kRotWarps - 1) / kRotWarps);
   if (g != nullptr)
