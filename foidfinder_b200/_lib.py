@@ -105,6 +105,7 @@ _SIGNATURES = {
     "ff_last_error": (C.c_char_p, []),
     "ff_version": (i32, []),
     "ff_device_error": (i32, [i32, C.POINTER(i32), i32]),
+    "ff_int8_mma_peak": (i32, [i32, C.POINTER(f32), C.POINTER(C.c_double), vp]),
     "ff_gemm_s8": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp, vp, i32, i32, i32, vp]),
     "ff_gemm_f16": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, i32, i32, i32, vp]),
     "ff_rot_q8": (i32, [vp, vp, vp, f32, i32, i32, i32, i32, vp, vp, vp]),

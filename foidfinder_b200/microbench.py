@@ -5,6 +5,7 @@ stream after warm-up. Also the entry point for ncu captures of single kernels.
                                               [--epilogue bias|swiglu|residual|qkv_rope]
     python -m foidfinder_b200.microbench attention [--batch 64] [--seq 1025] [--rope] [--iters 20]
     python -m foidfinder_b200.microbench rotate [--batch 64] [--tokens 1025] [--cols 1024 ...] [--iters 20]
+    python -m foidfinder_b200.microbench peak      (measured dense int8 tensor-core TOPS)
 
 PixAI-1008 shapes: `attention --batch 144 --seq 576` (16 images x 9 windows), `attention --batch 16 --seq
 5184` (global blocks), `rotate --batch 16 --tokens 5184 --cols 1024 --cols 4864`.
@@ -114,7 +115,7 @@ def bench_rotate(batch: int, iters: int, tokens: int = TOKENS, widths: list[int]
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("kernel", choices=("gemm", "attention", "rotate"))
+    ap.add_argument("kernel", choices=("gemm", "attention", "rotate", "peak"))
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--shape", action="append", choices=sorted(GEMM_SHAPES))
@@ -125,7 +126,10 @@ def main() -> None:
     ap.add_argument("--tokens", type=int, default=TOKENS, help="rotate: rows per image")
     ap.add_argument("--cols", type=int, action="append", choices=sorted(ROT_CASES), help="rotate: row widths")
     a = ap.parse_args()
-    if a.kernel == "gemm":
+    if a.kernel == "peak":
+        for _ in range(3):
+            print(json.dumps({"kernel": "int8_mma_peak", "tops": ops.int8_mma_peak()}))
+    elif a.kernel == "gemm":
         bench_gemm(a.batch, a.shape or list(GEMM_SHAPES), a.iters, a.epilogue, a.tile)
     elif a.kernel == "attention":
         bench_attention(a.batch, a.iters, a.rope, a.seq)

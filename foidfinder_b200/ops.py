@@ -275,3 +275,13 @@ def pool_query_attention(q: torch.Tensor, kv: torch.Tensor, B: int, tokens: int,
     with torch.cuda.device(kv.device):
         check(lib().ff_pool_query_attention(_ptr(q), _ptr(kv), B, tokens, heads, _ptr(out), _stream(kv)),
               "pool_query_attention")
+
+
+def int8_mma_peak(device: int = 0, iters: int = 200_000) -> float:
+    """Measured dense int8 tensor-core throughput of `device` in TOPS (back-to-back tcgen05 MMAs on
+    resident operands, one CTA per SM; about 50 ms)."""
+    ms, ops = C.c_float(), C.c_double()
+    with torch.cuda.device(device):
+        check(lib().ff_int8_mma_peak(iters, C.byref(ms), C.byref(ops), torch.cuda.current_stream(device).cuda_stream),
+              "int8_mma_peak")
+    return ops.value / (ms.value * 1e-3) / 1e12

@@ -41,6 +41,11 @@ int ff_version(void);
  * *code = 0 when no kernel reported a failure. */
 int ff_device_error(int device, int* code, int clear);
 
+/* Measured dense int8 tensor-core peak of the current device (no reference counterpart): one CTA per SM
+ * issues `iters` x 4 back-to-back tcgen05 kind::i8 MMAs (M128 N256 K32) on resident shared-memory operands,
+ * timed with CUDA events on `stream` (synchronises it). ms: elapsed time; ops: 2 x multiply-adds done. */
+int ff_int8_mma_peak(int iters, float* ms, double* ops, void* stream);
+
 /* ---------------------------------------------------------------- GEMM epilogues */
 #define FF_EPI_QKV_ROPE 0 /* fp16 out [M, N]; 2-D RoPE on columns [0, rope_cols) */
 #define FF_EPI_RESIDUAL 1 /* fp16 out [M, N] = fp16(out + fp16(y)) (the residual stream) */
