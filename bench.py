@@ -187,7 +187,8 @@ def workload(cfg, B: int, world: int) -> dict:
                 f"{list(cfg.global_blocks)}), dim {cfg.dim}, GELU {cfg.mlp_hidden}, attention-pool head, "
                 f"{cfg.num_tags} tags, top-{cfg.topk}")
     else:
-        desc = (f"{cfg.name} int8 forward (BASELINE config 3): {cfg.image_size}px, {cfg.tokens} tokens, "
+        which = "BASELINE config 4" if cfg.head == "tree" else "BASELINE config 3"
+        desc = (f"{cfg.name} int8 forward ({which}): {cfg.image_size}px, {cfg.tokens} tokens, "
                 f"{cfg.depth} blocks, dim {cfg.dim}, SwiGLU {cfg.mlp_hidden}, {cfg.num_tags} tags, top-{cfg.topk}")
     return {
         "workload": desc,
