@@ -4,8 +4,9 @@
 // softmax(q k^T) v per head on the packed QKV activations, scale folded into q), with f32 accumulation and
 // masked ragged tails (EVA02 at 448 px has 1025 tokens).
 //
-// Persistent CTAs (one per SM, 320 threads, all 512 TMEM columns) walk work items of up to 256 queries
-// (two 128-row tiles, Q0 and Q1) of one (image, head); consecutive items overlap in the pipeline:
+// Persistent CTAs (one per SM, 320 threads, or 384 with tail rows; all 512 TMEM columns) walk work items of
+// up to 256 queries (two 128-row tiles, Q0 and Q1) of one (image, head); consecutive items overlap in the
+// pipeline:
 //   warp 0     TMA: each item's Q0/Q1 into one of two Q buffers, K/V tiles of 128 keys through a 3-stage
 //              ring. The tensor map is 3-D [images, tokens, 3*dim], so rows past an image's last token
 //              arrive as zeros.
@@ -24,10 +25,11 @@
 //              (build-time option) a degree-3 polynomial whose fp16 bits are assembled with integer ops.
 //              The 2^7 factor keeps every P in fp16 range (<= 2^15) while polynomial results below 2^-14
 //              (saturated there) are at most 2^-21 of the row maximum; it cancels in O / l.
+//   warps 10-11  (sequences with 1..kTailRows rows past the last full query tile, e.g. EVA02's 1025th)
+//              those rows on the CUDA cores; their keys stay in the ragged last key tile of the others.
 // The row sum l is column 64 of the widened P V product: it costs no extra MMA instruction (every
 // tcgen05.mma costs >= ~56 cycles whatever its N) and is rescaled together with O.
 #include <algorithm>
-#include <mutex>
 
 #include "common.h"
 #include "kernels.h"
@@ -45,7 +47,8 @@ constexpr int ONES_LBO = STAGES * TILE;          // V stage s + ONES_LBO: its at
 constexpr int OFF_ONES = OFF_V + ONES_LBO;       // STAGES atoms of 128 rows x 128 B
 constexpr int OFF_BAR = OFF_ONES + STAGES * TILE;
 constexpr int SMEM = 1024 + OFF_BAR + 256;
-constexpr int THREADS = 320;
+constexpr int THREADS = 320;          // load, MMA, 2 x 4 softmax warps
+constexpr int THREADS_TAIL = 384;     // + 2 tail-row warps (sequences with kTailRows or fewer extra rows)
 constexpr uint32_t T_COLS = 512;
 __host__ __device__ constexpr uint32_t t_s(int i) { return 128u * i; }
 __host__ __device__ constexpr uint32_t t_o(int i) { return 256u + 80u * i; }  // O in [0, 64), l at 64
@@ -136,21 +139,32 @@ constexpr unsigned kPolyChunks = FF_ATTN_POLY_CHUNKS;
 }  // namespace fa
 
 // Query rows past the last full 128-row tile, when there are at most kTailRows of them (EVA02: 1025 =
-// 8 x 128 + 1), go to a separate launch with one CTA per (image, head) that computes them on the CUDA
-// cores in f32: a tensor-core item for them would run a whole query tile (and all key tiles) for one row. Each
-// quarter-warp (8 lanes x 8 dims = one 128-byte key/value row, coalesced) walks its share of the keys
-// with its own online softmax (running max m, sum l, o over its 8 dims per lane), four keys in flight;
-// the 40 partial results are then merged through shared memory. Called by every thread of the CTA.
+// 8 x 128 + 1), are computed on the CUDA cores in f32 by kTailWarps extra warps of the persistent kernel,
+// during one of the items of their (image, head), so their keys and values are read while the TMA loads
+// of that (image, head)'s items bring the same rows into L2 (a tensor-core tile for them
+// would run a whole 128-row query tile for one row; a separate launch re-read all keys and values from
+// HBM). Each quarter-warp (8 lanes x 8 dims = one 128-byte key/value row, coalesced) walks its share of
+// the keys with its own online softmax (running max m, sum l, o over its 8 dims per lane), UNR keys in
+// flight; the partial results are then merged through shared memory. Called by every thread of the tail
+// warps (t = 0 .. 32 kTailWarps - 1), which synchronise among themselves on named barrier 1.
 namespace fa {
 constexpr int kTailRows = 4;
+constexpr int kTailWarps = (THREADS_TAIL - THREADS) / 32;
 
-__device__ __noinline__ void attention_tail_rows(const __half* __restrict__ qkv, __half* __restrict__ out, int T,
-                                                 int T_main, int heads, float scale_log2, int img, int h) {
-  constexpr int NQ = THREADS / 8;  // quarter-warps
-  constexpr int UNR = 4;           // keys in flight per quarter-warp
+// Named barrier 1 over the tail warps. The quarter-warps leave their key loops at different points, so the
+// warps reconverge first (bar.sync is the warp-aligned form).
+__device__ __forceinline__ void tail_bar() {
+  __syncwarp();
+  asm volatile("bar.sync 1, %0;" ::"n"(kTailWarps * 32) : "memory");
+}
+
+__device__ __forceinline__ void attention_tail_rows(const __half* __restrict__ qkv, __half* __restrict__ out, int T,
+                                                 int T_main, int heads, float scale_log2, int img, int h, int t) {
+  constexpr int NQ = kTailWarps * 4;  // quarter-warps (8 lanes each)
+  constexpr int UNR = 4;              // keys in flight per quarter-warp
   __shared__ float part_m[NQ], part_l[NQ];
   __shared__ float part_o[NQ][HD];
-  const int dim = heads * HD, t = threadIdx.x, qw = t >> 3, ql = t & 7;
+  const int dim = heads * HD, qw = t >> 3, ql = t & 7;
   const size_t img_row0 = static_cast<size_t>(img) * T;
   const unsigned qmask = 0xFFu << (t & 24);  // this quarter-warp's lanes
   for (int r = T_main; r < T; ++r) {
@@ -208,14 +222,14 @@ __device__ __noinline__ void attention_tail_rows(const __half* __restrict__ qkv,
         }
       }
     }
-    __syncthreads();  // the previous row's merge has read the partials
+    tail_bar();  // the previous row's merge has read the partials
     if (ql == 0) {
       part_m[qw] = m;
       part_l[qw] = l;
     }
 #pragma unroll
     for (int d = 0; d < 8; ++d) part_o[qw][8 * ql + d] = o[d];
-    __syncthreads();
+    tail_bar();
     if (t < HD) {
       float mm = -INFINITY;
 #pragma unroll 8
@@ -233,13 +247,6 @@ __device__ __noinline__ void attention_tail_rows(const __half* __restrict__ qkv,
 }
 }  // namespace fa
 
-// Rows past the last full query tile (see attention_tail_rows), one CTA per (head, image).
-__global__ void __launch_bounds__(fa::THREADS, 3)
-    attention_tail_kernel(const __half* __restrict__ qkv, __half* __restrict__ out, int T, int T_main, int heads,
-                          float scale_log2) {
-  fa::attention_tail_rows(qkv, out, T, T_main, heads, scale_log2, blockIdx.y, blockIdx.x);
-}
-
 // Persistent: min(items, SMs) CTAs, each walking work items (image, head, pair of query tiles) with a grid
 // stride, pair index fastest so the items running at once share their keys/values in L2. The pipeline
 // runs across item boundaries: the producer loads the next item's Q into the other Q buffer and its
@@ -248,9 +255,11 @@ __global__ void __launch_bounds__(fa::THREADS, 3)
 // storing, so the next item's first P V, which overwrites O, waits only for that read. Every barrier
 // phase is counted per CTA (items, tiles), not per item. An item whose second query tile is empty runs
 // that warpgroup's protocol without work (its S and P V are skipped, its barriers still advance).
-__global__ void __launch_bounds__(fa::THREADS, 1)
-    attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, __half* __restrict__ out, int T, int T_main,
-                        int heads, int num_seqs, float scale_log2, int* err) {
+template <bool TAILW>
+__global__ void __launch_bounds__(TAILW ? fa::THREADS_TAIL : fa::THREADS, 1)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __half* __restrict__ qkv,
+                        __half* __restrict__ out, int T, int T_main, int heads, int num_seqs, float scale_log2,
+                        int* err) {
   using namespace fa;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -307,7 +316,7 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
   }
   if (warp >= 2) {  // the constant ones atoms that widen V (fp16 1.0; the TMA never writes them)
     uint4* ones = reinterpret_cast<uint4*>(smem + OFF_ONES);
-    for (int i = threadIdx.x - 64; i < STAGES * TILE / 16; i += THREADS - 64)
+    for (int i = threadIdx.x - 64; i < STAGES * TILE / 16; i += static_cast<int>(blockDim.x) - 64)
       ones[i] = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
     fence_async_smem();
   }
@@ -481,6 +490,18 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
         }
       }
     }
+  } else if (warp >= 10) {
+    // ------------------------------------------------------------ tail query rows (warps 10, 11)
+    if constexpr (TAILW) {
+      for (int it = blockIdx.x; it < items; it += gridDim.x) {
+        // One item of each (image, head) carries its tail rows, chosen so that they spread evenly over
+        // the CTAs (a CTA's items all have the same pair index when the grid is a multiple of n_pairs).
+        if (it % n_pairs != (it / n_pairs) % n_pairs) continue;
+        int img, h, q0;
+        item_of(it, img, h, q0);
+        attention_tail_rows(qkv, out, T, T_main, heads, scale_log2, img, h, threadIdx.x - THREADS);
+      }
+    }
   } else {
     // ------------------------------------------------------------ softmax + epilogue (warps 2..9)
     const int g = (warp - 2) >> 2;  // query tile of this warpgroup
@@ -639,35 +660,11 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
   if (warp == 1) tmem_dealloc(tmem, T_COLS);
 }
 
-// Per-device side stream for the tail-row kernel, created on first use (outside any stream capture: the
-// engine's first forward of a batch size runs eagerly). The mutex keeps one caller's fork/join pair intact.
-struct SideStream {
-  cudaStream_t stream = nullptr;
-  cudaEvent_t fork = nullptr, join = nullptr;
-  std::mutex mu;
-};
-
-SideStream* side_stream(int dev) {
-  static SideStream streams[64];
-  static std::mutex create_mu;
-  if (dev < 0 || dev >= 64) return nullptr;
-  std::lock_guard<std::mutex> lock(create_mu);
-  SideStream& ss = streams[dev];
-  if (ss.stream == nullptr) {
-    if (cudaStreamCreateWithFlags(&ss.stream, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming) != cudaSuccess) {
-      cudaGetLastError();
-      ss.stream = nullptr;
-      return nullptr;
-    }
-  }
-  return &ss;
-}
-
-int attention_tc_launches(int seq_len) {
+// Query rows past the last full 128-row tile that attention_tc computes on the CUDA cores inside its one
+// launch (1..kTailRows of them, e.g. EVA02's 1025th token), or 0 when the last query tile is ragged instead.
+int attention_tc_tail_rows(int seq_len) {
   const int rem = seq_len % fa::BQ;
-  return rem != 0 && rem <= fa::kTailRows && seq_len > fa::BQ ? 2 : 1;
+  return rem != 0 && rem <= fa::kTailRows && seq_len > fa::BQ ? rem : 0;
 }
 
 int attention_tc(const void* qkv, void* out, int num_seqs, int seq_len, int heads, float scale, cudaStream_t s) {
@@ -683,45 +680,27 @@ int attention_tc(const void* qkv, void* out, int num_seqs, int seq_len, int head
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !configured[dev]) {
-    if (cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess)
+    if (cudaFuncSetAttribute(attention_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess ||
+        cudaFuncSetAttribute(attention_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess)
       return check_launch("attention_tc: cudaFuncSetAttribute");
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
   const float scale_log2 = scale * 1.4426950408889634f;
-  const int t_main = attention_tc_launches(seq_len) == 2 ? seq_len - seq_len % BQ : seq_len;
+  const int t_main = seq_len - attention_tc_tail_rows(seq_len);
   const long long items = static_cast<long long>(num_seqs) * heads * ((t_main + 2 * BQ - 1) / (2 * BQ));
   FF_REQUIRE(items <= 0x7fffffff, "attention: %lld work items", items);
   const int grid = static_cast<int>(std::min<long long>(items, sm_count()));
-  // Rows past the last full query tile go to a CUDA-core kernel (one CTA per (head, image)) when they are
-  // few. It runs beside the tensor-core kernel on a side stream (fork/join by events, captured into graphs
-  // as such), submitted after it: its CTAs (64 registers, 10.5 KB) fit next to a persistent attention CTA
-  // on the same SM, so they fill the issue slots the softmax chain leaves idle.
-  SideStream* side = nullptr;
-  if (t_main < seq_len) {
-    side = side_stream(dev);
-    FF_REQUIRE(side != nullptr, "attention: side stream creation failed");
-    side->mu.lock();
-    if (cudaEventRecord(side->fork, s) != cudaSuccess || cudaStreamWaitEvent(side->stream, side->fork, 0) != cudaSuccess) {
-      side->mu.unlock();
-      return check_launch("attention: fork");
-    }
-  }
-  attention_tc_kernel<<<grid, THREADS, SMEM, s>>>(map, static_cast<__half*>(out), seq_len, t_main, heads, num_seqs,
-                                                  scale_log2, err);
-  rc = check_launch("attention_tc_kernel");
-  if (side != nullptr) {
-    if (rc == FF_OK) {
-      attention_tail_kernel<<<dim3(heads, num_seqs), THREADS, 0, side->stream>>>(
-          static_cast<const __half*>(qkv), static_cast<__half*>(out), seq_len, t_main, heads, scale_log2);
-      rc = check_launch("attention_tail_kernel");
-    }
-    // Join even after a failed launch, so the side stream never leaves work unjoined in a capture.
-    if (cudaEventRecord(side->join, side->stream) != cudaSuccess || cudaStreamWaitEvent(s, side->join, 0) != cudaSuccess) {
-      if (rc == FF_OK) rc = check_launch("attention: join");
-    }
-    side->mu.unlock();
-  }
-  return rc;
+  // Tail rows (EVA02's 1025th) run on two extra warps of the same launch; without them the kernel keeps
+  // 320 threads (the extra warps, idle, measured 2.6% slower on 1024-token sequences).
+  if (t_main < seq_len)
+    attention_tc_kernel<true><<<grid, THREADS_TAIL, SMEM, s>>>(map, static_cast<const __half*>(qkv),
+                                                               static_cast<__half*>(out), seq_len, t_main, heads,
+                                                               num_seqs, scale_log2, err);
+  else
+    attention_tc_kernel<false><<<grid, THREADS, SMEM, s>>>(map, static_cast<const __half*>(qkv),
+                                                           static_cast<__half*>(out), seq_len, t_main, heads,
+                                                           num_seqs, scale_log2, err);
+  return check_launch("attention_tc_kernel");
 }
 
 }  // namespace ff

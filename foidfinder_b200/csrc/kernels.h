@@ -11,8 +11,9 @@ int rot_q8(const void* x, const float* g, const float* b, float eps, int rows, i
 int attention(const void* qkv, void* out, int num_seqs, int seq_len, int heads, const float* rope_cos,
               const float* rope_sin, float scale, cudaStream_t s);
 int attention_tc(const void* qkv, void* out, int num_seqs, int seq_len, int heads, float scale, cudaStream_t s);
-// Kernel launches attention_tc makes for one call (2 when a CUDA-core launch takes the ragged tail rows).
-int attention_tc_launches(int seq_len);
+// Query rows (and keys) past the last full 128-row tile that attention_tc computes on the CUDA cores inside
+// its one launch (1..4 of them, e.g. EVA02's 1025th token), or 0 when the last tiles are ragged instead.
+int attention_tc_tail_rows(int seq_len);
 int topk(const float* logits, int B, int n, int k, int32_t* idx, float* val, cudaStream_t s);
 int patchify(const uint8_t* img, int B, int S, int p, const float* mean, const float* stdv, void* out, int k_pad,
              cudaStream_t s, int win = 0);

@@ -149,12 +149,12 @@ def test_pair_tiles_need_int8_and_256_columns():
     assert "pair tiles need int8" in _err()
 
 
-@pytest.mark.parametrize(("name", "launches"), [("eva02-l-448", 3 + 10 * 24 + 1 + 1 + 1),
-                                                 ("eva02-b-448", 3 + 10 * 12 + 7 + 1 + 1),
+@pytest.mark.parametrize(("name", "launches"), [("eva02-l-448", 3 + 9 * 24 + 1 + 1 + 1),
+                                                 ("eva02-b-448", 3 + 9 * 12 + 7 + 1 + 1),
                                                  ("pixai-1008", 3 + 9 * 32 + 4 + 1 + 1)])
 def test_launches_per_forward(name, launches):
-    """Kernel launches of one forward: 9 per block (+1 where the attention has CUDA-core tail rows: 1025
-    tokens), the head's launches, the tag GEMM and the top-k."""
+    """Kernel launches of one forward: 9 per block (EVA02's 1025th query row and key are computed inside the
+    attention launch), the head's launches, the tag GEMM and the top-k."""
     from foidfinder_b200.config import CONFIGS
     from foidfinder_b200.engine import c_config
 

@@ -103,13 +103,21 @@ def _ref_attention(qkv, seqs, T, heads, scale, rope=None):
                                                           (1, 1, 16, False), (2, 577, 16, True), (1, 128, 4, False),
                                                           # tensor-core path: masked ragged query tile (577),
                                                           # CUDA-core tail rows (259: 3 rows; 1540: 4 rows and
-                                                          # more keys than one pass of the tail CTA)
-                                                          (2, 577, 16, False), (2, 259, 8, False), (1, 1540, 4, False)])
+                                                          # more keys than one pass of the tail warps)
+                                                          (2, 577, 16, False), (2, 259, 8, False), (1, 1540, 4, False),
+                                                          # the keys of the ragged last key tile (and the
+                                                          # CUDA-core tail rows) hold the row maximum by far
+                                                          (2, 1025, 16, "dominant"), (1, 1540, 4, "dominant")])
 def test_attention_matches_oracle(cuda_device, no_device_error, seqs, T, heads, rope):
     from foidfinder_b200 import ops
 
     g = torch.Generator().manual_seed(seqs * 1000 + T)
     qkv = torch.randn(seqs * T, 3 * heads * 64, generator=g).half()
+    if rope == "dominant":
+        rope = False
+        x = qkv.view(seqs, T, 3, heads, 64)
+        x[:, :, 0] = x[:, :, 0].abs()  # q >= 0
+        x[:, T - T % 128 :, 1] = 0.6 * (1 + torch.rand(seqs, T % 128, heads, 64, generator=g)).half()  # q k ~ 60
     scale = 1.0 / math.sqrt(64)
     tables = None
     if rope:

@@ -66,8 +66,7 @@ def test_engine_tree_head_matches_int8_oracle(cuda_device, no_device_error, imag
     imgs = _images(B, image, 29)
     ref = E.forward_int8(conv, cfg, imgs)
     eng = Engine(cfg, conv, device=0)
-    tail = 1 if 1 <= cfg.tokens % 128 <= 4 and cfg.tokens > 128 else 0  # CUDA-core attention tail rows
-    assert eng.launches_per_forward == 3 + (9 + tail) * depth + 7 + 1 + 1
+    assert eng.launches_per_forward == 3 + 9 * depth + 7 + 1 + 1
     logits, idx, val = eng.forward(imgs, graph=False)
     torch.cuda.synchronize()
     got = logits.cpu()
