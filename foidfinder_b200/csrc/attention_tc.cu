@@ -247,6 +247,56 @@ __device__ __forceinline__ void attention_tail_rows(const __half* __restrict__ q
 }
 }  // namespace fa
 
+namespace fa {
+// Cold paths of the softmax warps, kept out of line so the full-tile loop stays compact in the
+// instruction cache. Row maximum over the first `valid` (< BKV) keys of a ragged tile (raw S values).
+__device__ __noinline__ float ragged_max(uint32_t ts, int valid) {
+  float mx = -INFINITY;
+  for (int c = 0; c < 4; ++c) {
+    uint32_t raw[32];
+    tmem_ld32(ts + 32 * c, raw);
+    tmem_ld_wait();
+#pragma unroll
+    for (int e = 0; e < 32; ++e)
+      if (32 * c + e < valid) mx = fmaxf(mx, __uint_as_float(raw[e]));
+  }
+  return mx;
+}
+// P of a ragged tile: exact zeros for keys >= valid; chunks of 32 keys past `valid` are not written.
+__device__ __noinline__ void ragged_p(uint32_t ts, int valid, float sc, float nm) {
+  const float2 sc2 = make_float2(sc, sc), nm2 = make_float2(nm, nm);
+  for (int c = 0; c < 4; ++c) {
+    if (32 * c >= valid) break;
+    uint32_t raw[32], pk[16];
+    tmem_ld32(ts + 32 * c, raw);
+    tmem_ld_wait();
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      float2 x = fma2(make_float2(__uint_as_float(raw[2 * e]), __uint_as_float(raw[2 * e + 1])), sc2, nm2);
+      if (32 * c + 2 * e >= valid) x.x = -INFINITY;
+      if (32 * c + 2 * e + 1 >= valid) x.y = -INFINITY;
+      pk[e] = exp2_mufu(x);
+    }
+    tmem_st16(ts + 16 * c, pk);
+  }
+}
+// O and l (80 TMEM columns from to) scaled by corr.
+__device__ __noinline__ void rescale_o(uint32_t to, float corr) {
+  for (int c = 0; c < 2; ++c) {
+    uint32_t o[32];
+    tmem_ld32(to + 32 * c, o);
+    tmem_ld_wait();
+#pragma unroll
+    for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
+    tmem_st32(to + 32 * c, o);
+  }
+  uint32_t l;
+  tmem_ld1(to + 64, l);
+  tmem_ld_wait();
+  tmem_st1(to + 64, __float_as_uint(__uint_as_float(l) * corr));
+}
+}  // namespace fa
+
 // Persistent: min(items, SMs) CTAs, each walking work items (image, head, pair of query tiles) with a grid
 // stride, pair index fastest so the items running at once share their keys/values in L2. The pipeline
 // runs across item boundaries: the producer loads the next item's Q into the other Q buffer and its
@@ -528,25 +578,21 @@ __global__ void __launch_bounds__(TAILW ? fa::THREADS_TAIL : fa::THREADS, 1)
           // Pass 1: row maximum, 64 keys (two loads, one wait) at a time: holding all 128 in registers
           // pushed the kernel to the 168-register cap with spills (measured 5-10% slower).
           float mx = -INFINITY;
+          if (full_tile) {
 #pragma unroll
-          for (int hf = 0; hf < 2; ++hf) {
-            uint32_t raw[2][32];
+            for (int hf = 0; hf < 2; ++hf) {
+              uint32_t raw[2][32];
 #pragma unroll
-            for (int c = 0; c < 2; ++c) tmem_ld32(ts + 64 * hf + 32 * c, raw[c]);
-            tmem_ld_wait();
-            if (full_tile) {
+              for (int c = 0; c < 2; ++c) tmem_ld32(ts + 64 * hf + 32 * c, raw[c]);
+              tmem_ld_wait();
 #pragma unroll
               for (int c = 0; c < 2; ++c)
 #pragma unroll
                 for (int e = 0; e < 32; e += 2)
                   mx = max3(mx, __uint_as_float(raw[c][e]), __uint_as_float(raw[c][e + 1]));
-            } else {
-#pragma unroll
-              for (int c = 0; c < 2; ++c)
-#pragma unroll
-                for (int e = 0; e < 32; ++e)
-                  if (64 * hf + 32 * c + e < valid) mx = fmaxf(mx, __uint_as_float(raw[c][e]));
             }
+          } else {
+            mx = fa::ragged_max(ts, valid);
           }
           const float m_new = fmaxf(m_ref, mx * scale_log2);
           bool rescale = false;
@@ -558,21 +604,7 @@ __global__ void __launch_bounds__(TAILW ? fa::THREADS_TAIL : fa::THREADS, 1)
             m_ref = m_new;
             rescale = true;
           }
-          if (__any_sync(0xffffffffu, rescale)) {
-            uint32_t o[32];
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-              tmem_ld32(tmem + lane_base + t_o(g) + 32 * c, o);
-              tmem_ld_wait();
-#pragma unroll
-              for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
-              fa::tmem_st32(tmem + lane_base + t_o(g) + 32 * c, o);
-            }
-            uint32_t l;
-            fa::tmem_ld1(tmem + lane_base + t_l(g), l);
-            tmem_ld_wait();
-            fa::tmem_st1(tmem + lane_base + t_l(g), __float_as_uint(__uint_as_float(l) * corr));
-          }
+          if (__any_sync(0xffffffffu, rescale)) fa::rescale_o(tmem + lane_base + t_o(g), corr);
         }
         if (active) {
           // Pass 2: P = 2^(s * scale_log2 - m_ref + 7) as fp16 pairs over S columns [0, 64), in two halves
@@ -580,37 +612,28 @@ __global__ void __launch_bounds__(TAILW ? fa::THREADS_TAIL : fa::THREADS, 1)
           // columns already read (those of half 0).
           const float2 sc2 = make_float2(scale_log2, scale_log2);
           const float2 nm2 = make_float2(kPScaleLog2 - m_ref, kPScaleLog2 - m_ref);
+          if (full_tile) {
 #pragma unroll
-          for (int hf = 0; hf < 2; ++hf) {
-            if (!full_tile && 64 * hf >= valid) break;  // P past the ragged tile's keys is never read
-            uint32_t raw[2][32];
-            tmem_ld32(ts + 64 * hf, raw[0]);
-            tmem_ld32(ts + 64 * hf + 32, raw[1]);
-            tmem_ld_wait();
+            for (int hf = 0; hf < 2; ++hf) {
+              uint32_t raw[2][32];
+              tmem_ld32(ts + 64 * hf, raw[0]);
+              tmem_ld32(ts + 64 * hf + 32, raw[1]);
+              tmem_ld_wait();
 #pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-              const int c = 2 * hf + cc;
-              if (!full_tile && 32 * c >= valid) break;
-              uint32_t pk[16];
-              if (full_tile) {
+              for (int cc = 0; cc < 2; ++cc) {
+                const int c = 2 * hf + cc;
+                uint32_t pk[16];
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
                   const float2 x = fma2(
                       make_float2(__uint_as_float(raw[cc][2 * e]), __uint_as_float(raw[cc][2 * e + 1])), sc2, nm2);
                   pk[e] = ((kPolyChunks >> c) & 1u) ? fa::exp2_poly(x) : fa::exp2_mufu(x);
                 }
-              } else {
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                  float2 x = fma2(
-                      make_float2(__uint_as_float(raw[cc][2 * e]), __uint_as_float(raw[cc][2 * e + 1])), sc2, nm2);
-                  if (32 * c + 2 * e >= valid) x.x = -INFINITY;
-                  if (32 * c + 2 * e + 1 >= valid) x.y = -INFINITY;
-                  pk[e] = fa::exp2_mufu(x);  // exact zeros for masked keys
-                }
+                tmem_st16(ts + 16 * c, pk);
               }
-              tmem_st16(ts + 16 * c, pk);
             }
+          } else {
+            fa::ragged_p(ts, valid, scale_log2, kPScaleLog2 - m_ref);
           }
         }
         __syncwarp();
