@@ -130,11 +130,6 @@ __device__ __forceinline__ uint32_t exp2_poly(float2 x) {
 #endif
 constexpr unsigned kPolyChunks = FF_ATTN_POLY_CHUNKS;
 
-// Build-time option: keep the row of S that pass 1 loads in registers for pass 2 instead of reading it
-// from TMEM again.
-#ifndef FF_ATTN_S_REGS
-#define FF_ATTN_S_REGS 0
-#endif
 
 }  // namespace fa
 

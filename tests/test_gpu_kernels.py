@@ -24,6 +24,8 @@ ROT_CASES = [
     (1025, 1024, 1024, 1024, True),
     (1025, 1024, 1024, 1024, False),
     (2050, 2816, 2730, 128, True),
+    (3, 2816, 2816, 128, True),  # an odd row count: the last CTA of the split kernel has a row without data
+    (1, 2816, 2730, 128, True),
     (1025, 2816, 2816, 128, False),
     (777, 768, 768, 256, True),
     (300, 2048, 2048, 128, True),
