@@ -122,9 +122,9 @@ __device__ __forceinline__ uint32_t exp2_poly(float2 x) {
 }
 
 // Which 32-key chunks of a tile take the polynomial path (bit c set: chunk c; the others use MUFU).
-// Tunable at build time. Measured on B200 (EVA02-L, 1025 tokens, batch 64): all-MUFU is fastest once
-// the two warpgroups alternate their exponential phases (371 TFLOP/s vs 348 with one polynomial chunk),
-// because the polynomial's ~15 instructions per pair cost more issue slots than the MUFU time they save.
+// Tunable at build time. Measured on B200 (EVA02-L, 1025 tokens, batch 64): all-MUFU is fastest (0.531 ms
+// per launch vs 0.549 with one polynomial chunk of four, 0.552 with the last chunk), because the
+// polynomial's ~15 instructions per pair cost more issue slots than the MUFU time they save.
 #ifndef FF_ATTN_POLY_CHUNKS
 #define FF_ATTN_POLY_CHUNKS 0x0u
 #endif
