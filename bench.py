@@ -248,7 +248,22 @@ def run_ours(args) -> None:
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+        # The communicator set-up may print a version banner on the process's stdout (seen on the GPU hosts);
+        # stdout is reserved for the one JSON result line, so the C-level stdout points at stderr until the
+        # first collective has created the communicator.
+        import ctypes
+
+        sys.stdout.flush()
+        saved_stdout = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+            dist.barrier()
+        finally:
+            ctypes.CDLL(None).fflush(None)  # C stdio buffers still hold what was printed in the window
+            sys.stdout.flush()
+            os.dup2(saved_stdout, 1)
+            os.close(saved_stdout)
     from foidfinder_b200.config import CONFIGS
     from foidfinder_b200.engine import Engine
 
