@@ -119,6 +119,7 @@ _SIGNATURES = {
     "ff_topk": (i32, [vp, i32, i32, i32, vp, vp, vp]),
     "ff_tree_pool": (i32, [C.POINTER(ModelConfig), C.POINTER(ModelWeights), vp, i32, vp, i64, vp, vp]),
     "ff_resize_pad": (i32, [vp, i32, i32, i32, i32, i32, i32, i32, vp, vp, i64, vp]),
+    "ff_letterbox_aa_f16": (i32, [vp, i32, i32, i32, i32, i32, vp, vp]),
     "ff_patchify_windowed": (i32, [vp, i32, i32, i32, C.POINTER(f32), C.POINTER(f32), vp, i32, i32, vp]),
     "ff_layernorm_pos": (i32, [vp, i64, vp, vp, f32, i32, i32, vp, i32, vp, vp]),
     "ff_pool_query_attention": (i32, [vp, vp, i32, i32, i32, vp, vp]),
@@ -127,6 +128,7 @@ _SIGNATURES = {
     "ff_engine_create": (i32, [C.POINTER(ModelConfig), C.POINTER(ModelWeights), i32, C.POINTER(vp)]),
     "ff_engine_forward": (i32, [vp, vp, i32, vp, vp, vp, vp]),
     "ff_engine_forward_eager": (i32, [vp, vp, i32, vp, vp, vp, vp]),
+    "ff_engine_forward_pixels": (i32, [vp, vp, i32, vp, vp, vp, i32, vp]),
     "ff_engine_workspace_bytes": (i64, [C.POINTER(ModelConfig), i32]),
     "ff_engine_profile": (i32, [vp, vp, i32, i32, C.POINTER(f32), C.POINTER(i32), vp]),
     "ff_engine_launches_per_forward": (i32, [C.POINTER(ModelConfig)]),

@@ -28,7 +28,7 @@ struct ff_engine {
   struct Batch {
     int B = 0;
     void* block = nullptr;  // one allocation for every activation buffer below
-    uint8_t* images = nullptr;
+    uint8_t* images = nullptr;  // the input: uint8 pixels, or (fp16 input) normalised fp16 pixels
     __half* patches = nullptr;
     __half* x = nullptr;
     int8_t* a8 = nullptr;
@@ -43,7 +43,7 @@ struct ff_engine {
     ff::GemmPlan stem, head, pool_kv, pool_proj;
     ff::PoolBuffers pool;
     std::vector<ff::GemmPlan> qkv_p, proj_p, fc1_p, fc2_p;
-    cudaGraphExec_t exec = nullptr;
+    cudaGraphExec_t exec[2] = {nullptr, nullptr};  // graph per input kind: [0] uint8, [1] fp16 pixels
     cudaStream_t capture_stream = nullptr;
   };
   ff_model_config cfg{};
@@ -97,7 +97,7 @@ Layout layout_for(const ff_model_config& c, int B) {
     off = align_up(off + bytes, 1024);
     return at;
   };
-  l.images = take(static_cast<size_t>(B) * c.image_size * c.image_size * 3);
+  l.images = take(static_cast<size_t>(B) * c.image_size * c.image_size * 3 * 2);  // room for fp16 pixels
   l.patches = take(static_cast<size_t>(B) * P * kpad * 2);
   l.x = take(M * c.dim * 2);
   l.a8 = take(M * wide);
@@ -314,11 +314,11 @@ struct Profiler {
   } while (0)
 
 // Every launch of one forward of batch b on stream s.
-int run_forward(ff_engine* e, ff_engine::Batch* b, cudaStream_t s, Profiler* prof = nullptr) {
+int run_forward(ff_engine* e, ff_engine::Batch* b, cudaStream_t s, Profiler* prof = nullptr, bool f16_in = false) {
   const ff_model_config& c = e->cfg;
   const int B = b->B, M = B * e->tokens, D = c.dim, H = c.mlp_hidden_pad;
   FF_LAUNCH(FF_PROF_STEM_PREP, patchify(b->images, B, c.image_size, c.patch, c.mean, c.std, b->patches, e->k_pad, s,
-                                        pixai(c) ? c.window : 0));
+                                        pixai(c) ? c.window : 0, f16_in));
   FF_LAUNCH(FF_PROF_STEM_GEMM, gemm_launch(b->stem, s));
   if (pixai(c))  // ln_pre, in place (engine.py:148)
     FF_LAUNCH(FF_PROF_STEM_PREP, layernorm(b->x, D, e->w.ln_pre_w, e->w.ln_pre_b, c.ln_eps, M, D, b->x, s));
@@ -453,57 +453,77 @@ extern "C" int ff_engine_create(const ff_model_config* cfg, const ff_model_weigh
   return FF_OK;
 }
 
-extern "C" int ff_engine_forward_eager(ff_engine* e, const uint8_t* images, int B, float* logits, int32_t* top_idx,
-                                       float* top_val, void* stream) {
-  FF_TRY(check_inputs(e, images, B, logits, top_idx));
-  std::lock_guard<std::mutex> lock(e->mu);
-  DeviceScope scope(e->device);
-  const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  ff_engine::Batch* b = nullptr;
-  FF_TRY(get_batch(e, B, &b));
-  const size_t in_bytes = static_cast<size_t>(B) * e->cfg.image_size * e->cfg.image_size * 3;
-  if (cudaMemcpyAsync(b->images, images, in_bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
-    return check_launch("engine: image copy");
-  FF_TRY(run_forward(e, b, s));
-  return copy_out(e, b, logits, top_idx, top_val, s);
+namespace ff {
+namespace {
+
+size_t input_bytes(const ff_engine* e, int B, bool f16_in) {
+  return static_cast<size_t>(B) * e->cfg.image_size * e->cfg.image_size * 3 * (f16_in ? 2 : 1);
 }
 
-extern "C" int ff_engine_forward(ff_engine* e, const uint8_t* images, int B, float* logits, int32_t* top_idx,
-                                 float* top_val, void* stream) {
-  FF_TRY(check_inputs(e, images, B, logits, top_idx));
+// One forward of B images (uint8, or normalised fp16 pixels) already on the device: copy into the batch's
+// input buffer, then the captured graph of this batch size and input kind (captured on first use) or the
+// eager launch sequence, then the outputs to the caller's buffers, all on `stream`.
+int forward_impl(ff_engine* e, const void* input, bool f16_in, int B, float* logits, int32_t* top_idx, float* top_val,
+                 bool use_graph, void* stream) {
   std::lock_guard<std::mutex> lock(e->mu);
   DeviceScope scope(e->device);
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   ff_engine::Batch* b = nullptr;
   FF_TRY(get_batch(e, B, &b));
-  if (b->exec == nullptr) {
+  cudaGraphExec_t& exec = b->exec[f16_in ? 1 : 0];
+  if (use_graph && exec == nullptr) {
     // Warm up outside capture (kernel attributes, module loading), then capture on a private stream.
-    if (cudaStreamCreateWithFlags(&b->capture_stream, cudaStreamNonBlocking) != cudaSuccess)
+    if (b->capture_stream == nullptr &&
+        cudaStreamCreateWithFlags(&b->capture_stream, cudaStreamNonBlocking) != cudaSuccess)
       return check_launch("engine: stream create");
-    FF_TRY(run_forward(e, b, b->capture_stream));
+    FF_TRY(run_forward(e, b, b->capture_stream, nullptr, f16_in));
     if (cudaStreamSynchronize(b->capture_stream) != cudaSuccess) return check_launch("engine: warm-up forward");
     cudaGraph_t graph = nullptr;
     if (cudaStreamBeginCapture(b->capture_stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
       return check_launch("engine: begin capture");
-    const int rc = run_forward(e, b, b->capture_stream);
+    const int rc = run_forward(e, b, b->capture_stream, nullptr, f16_in);
     const cudaError_t ce = cudaStreamEndCapture(b->capture_stream, &graph);
     if (rc != FF_OK) {
       if (graph) cudaGraphDestroy(graph);
       return rc;
     }
     if (ce != cudaSuccess) return check_launch("engine: end capture");
-    const cudaError_t ie = cudaGraphInstantiate(&b->exec, graph, 0);
+    const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
     cudaGraphDestroy(graph);
     if (ie != cudaSuccess) {
-      b->exec = nullptr;
+      exec = nullptr;
       return check_launch("engine: graph instantiate");
     }
   }
-  const size_t in_bytes = static_cast<size_t>(B) * e->cfg.image_size * e->cfg.image_size * 3;
-  if (cudaMemcpyAsync(b->images, images, in_bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
-    return check_launch("engine: image copy");
-  if (cudaGraphLaunch(b->exec, s) != cudaSuccess) return check_launch("engine: graph launch");
+  if (cudaMemcpyAsync(b->images, input, input_bytes(e, B, f16_in), cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+    return check_launch("engine: input copy");
+  if (use_graph) {
+    if (cudaGraphLaunch(exec, s) != cudaSuccess) return check_launch("engine: graph launch");
+  } else {
+    FF_TRY(run_forward(e, b, s, nullptr, f16_in));
+  }
   return copy_out(e, b, logits, top_idx, top_val, s);
+}
+
+}  // namespace
+}  // namespace ff
+
+extern "C" int ff_engine_forward_eager(ff_engine* e, const uint8_t* images, int B, float* logits, int32_t* top_idx,
+                                       float* top_val, void* stream) {
+  FF_TRY(check_inputs(e, images, B, logits, top_idx));
+  return forward_impl(e, images, false, B, logits, top_idx, top_val, false, stream);
+}
+
+extern "C" int ff_engine_forward(ff_engine* e, const uint8_t* images, int B, float* logits, int32_t* top_idx,
+                                 float* top_val, void* stream) {
+  FF_TRY(check_inputs(e, images, B, logits, top_idx));
+  return forward_impl(e, images, false, B, logits, top_idx, top_val, true, stream);
+}
+
+extern "C" int ff_engine_forward_pixels(ff_engine* e, const uint16_t* pixels, int B, float* logits, int32_t* top_idx,
+                                        float* top_val, int use_graph, void* stream) {
+  FF_TRY(check_inputs(e, reinterpret_cast<const uint8_t*>(pixels), B, logits, top_idx));
+  return forward_impl(e, pixels, true, B, logits, top_idx, top_val, use_graph != 0, stream);
 }
 
 extern "C" int ff_engine_profile(ff_engine* e, const uint8_t* images, int B, int iters, float* ms, int* launches,
@@ -555,7 +575,8 @@ extern "C" int ff_engine_destroy(ff_engine* e) {
     cudaDeviceSynchronize();
     for (auto& kv : e->batches) {
       ff_engine::Batch* b = kv.second;
-      if (b->exec) cudaGraphExecDestroy(b->exec);
+      for (cudaGraphExec_t x : b->exec)
+        if (x) cudaGraphExecDestroy(x);
       if (b->capture_stream) cudaStreamDestroy(b->capture_stream);
       cudaFree(b->block);
       delete b;

@@ -15,8 +15,9 @@ int attention_tc(const void* qkv, void* out, int num_seqs, int seq_len, int head
 // its one launch (1..4 of them, e.g. EVA02's 1025th token), or 0 when the last tiles are ragged instead.
 int attention_tc_tail_rows(int seq_len);
 int topk(const float* logits, int B, int n, int k, int32_t* idx, float* val, cudaStream_t s);
-int patchify(const uint8_t* img, int B, int S, int p, const float* mean, const float* stdv, void* out, int k_pad,
-             cudaStream_t s, int win = 0);
+// img: uint8 pixels (normalised with mean/std) or, with f16_pixels, already normalised fp16 pixels.
+int patchify(const void* img, int B, int S, int p, const float* mean, const float* stdv, void* out, int k_pad,
+             cudaStream_t s, int win = 0, bool f16_pixels = false);
 int fill_cls(const void* cls, void* x, int B, int tokens, int dim, cudaStream_t s);
 int layernorm(const void* x, int64_t stride, const float* g, const float* b, float eps, int rows, int cols, void* out,
               cudaStream_t s, const void* pos = nullptr, int period = 0);

@@ -6,11 +6,18 @@
 namespace ff {
 
 // ---------------------------------------------------------------- patchify
-// images [B, S, S, 3] uint8 -> patches [B * G * G, k_pad] fp16, column k = (kh * p + kw) * 3 + c
-// (the (kh, kw, c) order of reference.py:103-107 and mlx/haruka.py:78), value (px / 255 - mean) / std.
+// images [B, S, S, 3] -> patches [B * G * G, k_pad] fp16, column k = (kh * p + kw) * 3 + c (the (kh, kw, c)
+// order of reference.py:103-107 and mlx/haruka.py:78). uint8 pixels become (px / 255 - mean) / std; fp16
+// pixels are already normalised (PixAICuda's input, engine.py:163-165) and are copied as they are.
 // Patch rows in row-major grid order, or (win > 0) window order: the grid cut into win x win windows,
 // windows row-major, patches row-major inside each (foidfinder/backends/cuda/reference.py:21-24, 103-107).
-__global__ void patchify_kernel(const uint8_t* __restrict__ img, int B, int S, int p, float m0, float m1, float m2,
+__device__ __forceinline__ float pixel_value(uint8_t u, float mean, float istd) {
+  return __fmul_rn(__fmaf_rn(static_cast<float>(u), 1.f / 255.f, -mean), istd);  // one rounding per step
+}
+__device__ __forceinline__ float pixel_value(__half h, float, float) { return __half2float(h); }
+
+template <typename Px>
+__global__ void patchify_kernel(const Px* __restrict__ img, int B, int S, int p, float m0, float m1, float m2,
                                 float is0, float is1, float is2, __half* __restrict__ out, int k_pad, int win) {
   const int G = S / p, P = G * G, kreal = p * p * 3;
   const int nw = win > 0 ? G / win : 1;
@@ -31,10 +38,10 @@ __global__ void patchify_kernel(const uint8_t* __restrict__ img, int B, int S, i
       const int kh = k / (p * 3), rem = k % (p * 3);
       const int y = py * p + kh;
       const int c = rem % 3;
-      const uint8_t u = img[(static_cast<int64_t>(b) * S + y) * S * 3 + static_cast<int64_t>(px) * p * 3 + rem];
+      const Px u = img[(static_cast<int64_t>(b) * S + y) * S * 3 + static_cast<int64_t>(px) * p * 3 + rem];
       const float mean = c == 0 ? m0 : (c == 1 ? m1 : m2);
       const float istd = c == 0 ? is0 : (c == 1 ? is1 : is2);
-      v = (static_cast<float>(u) * (1.f / 255.f) - mean) * istd;
+      v = pixel_value(u, mean, istd);
     }
     out[t] = __float2half_rn(v);
   }
@@ -210,8 +217,8 @@ int topk(const float* logits, int B, int n, int k, int32_t* idx, float* val, cud
   return check_launch("topk_kernel");
 }
 
-int patchify(const uint8_t* img, int B, int S, int p, const float* mean, const float* stdv, void* out, int k_pad,
-             cudaStream_t s, int win) {
+int patchify(const void* img, int B, int S, int p, const float* mean, const float* stdv, void* out, int k_pad,
+             cudaStream_t s, int win, bool f16_pixels) {
   FF_REQUIRE(img && out && mean && stdv, "ff_patchify: NULL pointer");
   FF_REQUIRE(p >= 1 && S % p == 0 && k_pad >= p * p * 3, "ff_patchify: bad geometry S=%d p=%d k_pad=%d", S, p, k_pad);
   FF_REQUIRE(win >= 0 && (win == 0 || (S / p) % win == 0), "ff_patchify: window %d does not tile the %d-patch grid",
@@ -219,8 +226,13 @@ int patchify(const uint8_t* img, int B, int S, int p, const float* mean, const f
   if (B == 0) return FF_OK;
   const int64_t total = static_cast<int64_t>(B) * (S / p) * (S / p) * k_pad;
   const int grid = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 16));
-  patchify_kernel<<<grid, 256, 0, s>>>(img, B, S, p, mean[0], mean[1], mean[2], 1.f / stdv[0], 1.f / stdv[1],
-                                       1.f / stdv[2], static_cast<__half*>(out), k_pad, win);
+  if (f16_pixels)
+    patchify_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(img), B, S, p, 0.f, 0.f, 0.f, 1.f, 1.f,
+                                                 1.f, static_cast<__half*>(out), k_pad, win);
+  else
+    patchify_kernel<uint8_t><<<grid, 256, 0, s>>>(static_cast<const uint8_t*>(img), B, S, p, mean[0], mean[1],
+                                                  mean[2], 1.f / stdv[0], 1.f / stdv[1], 1.f / stdv[2],
+                                                  static_cast<__half*>(out), k_pad, win);
   return check_launch("patchify_kernel");
 }
 

@@ -11,6 +11,8 @@
 // against) resamples horizontally first unless the source is more than 100 times taller than wide — a
 // rule established by comparing both orders against PIL.Image.resize over a few hundred random shapes.
 // Horizontal-first reads only the source rows the vertical pass needs.
+#include <cuda_fp16.h>
+
 #include <cmath>
 #include <vector>
 
@@ -194,4 +196,102 @@ extern "C" int ff_resize_pad(const uint8_t* src, int h, int w, int new_h, int ne
                                                                       top, left, new_h, new_w, fill, dst);
   }
   return check_launch("resample_kernel");
+}
+
+// ---------------------------------------------------------------- PixAI's float letterbox
+// The reference's PixAI preprocessing (foidfinder/backends/cuda/preprocess.py:16-32): pixels / 255 in f32,
+// F.interpolate(mode="bilinear", align_corners=False, antialias=True) to (new_h, new_w), then x * 2 - 1
+// rounded to fp16, centred on a canvas of -1 (black after the normalisation). No 8-bit rounding anywhere.
+//
+// The antialiased bilinear resize is separable: each output index i along an axis of scale
+// s = in / out takes the source indices [xmin, xmin + n) around center = s * (i + 0.5) with the triangle
+// filter stretched by max(s, 1) (support = max(s, 1)), weights normalised by their sum (torch's
+// _compute_weights_aa, the same rule as Pillow's precompute_coeffs but in float, not fixed point). One
+// thread per output pixel sums over the rows of its vertical taps the horizontal sums of each row (the
+// horizontal pass first, as torch's separable CPU kernel runs its width pass first), in f32.
+namespace ff {
+namespace {
+
+struct AaAxis {
+  float scale, support, invscale;
+};
+
+__host__ __device__ inline AaAxis aa_axis(int in_size, int out_size) {
+  AaAxis a;
+  a.scale = static_cast<float>(in_size) / static_cast<float>(out_size);
+  a.support = a.scale >= 1.f ? a.scale : 1.f;  // interp size 2 for bilinear: support = 2/2 * max(scale, 1)
+  a.invscale = a.scale >= 1.f ? 1.f / a.scale : 1.f;
+  return a;
+}
+
+__device__ inline float tri(float x) {
+  x = fabsf(x);
+  return x < 1.f ? 1.f - x : 0.f;
+}
+
+// Taps of output index i: first source index, count, and the sum of the unnormalised weights.
+__device__ inline void aa_taps(const AaAxis& a, int i, int in_size, int* first, int* count, float* total) {
+  const float center = a.scale * (static_cast<float>(i) + 0.5f);
+  int lo = static_cast<int>(center - a.support + 0.5f);
+  if (lo < 0) lo = 0;
+  int hi = static_cast<int>(center + a.support + 0.5f);
+  if (hi > in_size) hi = in_size;
+  float t = 0.f;
+  for (int j = 0; j < hi - lo; ++j) t += tri((static_cast<float>(j + lo) - center + 0.5f) * a.invscale);
+  *first = lo;
+  *count = hi - lo;
+  *total = t;
+}
+
+__device__ inline float aa_weight(const AaAxis& a, int i, int j, int first, float total) {
+  const float center = a.scale * (static_cast<float>(i) + 0.5f);
+  const float w = tri((static_cast<float>(j + first) - center + 0.5f) * a.invscale);
+  return total != 0.f ? w / total : 0.f;
+}
+
+__global__ void letterbox_aa_f16_kernel(const uint8_t* __restrict__ src, int h, int w, int new_h, int new_w, int size,
+                                        int top, int left, __half* __restrict__ dst) {
+  const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y;
+  if (x >= size || y >= size) return;
+  const int yy = y - top, xx = x - left;
+  float v[3] = {-1.f, -1.f, -1.f};
+  if (yy >= 0 && yy < new_h && xx >= 0 && xx < new_w) {
+    const AaAxis ax = aa_axis(w, new_w), ay = aa_axis(h, new_h);
+    int x0, nx, y0, ny;
+    float tx, ty;
+    aa_taps(ax, xx, w, &x0, &nx, &tx);
+    aa_taps(ay, yy, h, &y0, &ny, &ty);
+    float acc[3] = {0.f, 0.f, 0.f};
+    for (int jy = 0; jy < ny; ++jy) {
+      const uint8_t* row = src + (static_cast<size_t>(y0 + jy) * w + x0) * 3;
+      float hs[3] = {0.f, 0.f, 0.f};
+      for (int jx = 0; jx < nx; ++jx) {
+        const float wx = aa_weight(ax, xx, jx, x0, tx);
+        for (int c = 0; c < 3; ++c) hs[c] += __fdiv_rn(static_cast<float>(row[jx * 3 + c]), 255.f) * wx;
+      }
+      const float wy = aa_weight(ay, yy, jy, y0, ty);
+      for (int c = 0; c < 3; ++c) acc[c] += hs[c] * wy;
+    }
+    for (int c = 0; c < 3; ++c) v[c] = __fsub_rn(acc[c] * 2.f, 1.f);
+  }
+  __half* o = dst + (static_cast<size_t>(y) * size + x) * 3;
+  o[0] = __float2half_rn(v[0]);
+  o[1] = __float2half_rn(v[1]);
+  o[2] = __float2half_rn(v[2]);
+}
+
+}  // namespace
+}  // namespace ff
+
+extern "C" int ff_letterbox_aa_f16(const uint8_t* src, int h, int w, int new_h, int new_w, int size, uint16_t* dst,
+                                   void* stream) {
+  FF_REQUIRE(src && dst, "ff_letterbox_aa_f16: NULL pointer");
+  FF_REQUIRE(h >= 1 && w >= 1 && new_h >= 1 && new_w >= 1 && new_h <= size && new_w <= size,
+             "ff_letterbox_aa_f16: bad geometry %dx%d -> %dx%d on %d", h, w, new_h, new_w, size);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int top = (size - new_h) / 2, left = (size - new_w) / 2;
+  constexpr int TX = 128;
+  letterbox_aa_f16_kernel<<<dim3((size + TX - 1) / TX, size), TX, 0, s>>>(src, h, w, new_h, new_w, size, top, left,
+                                                                         reinterpret_cast<__half*>(dst));
+  return check_launch("letterbox_aa_f16_kernel");
 }

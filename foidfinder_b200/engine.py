@@ -2,8 +2,10 @@
 
 Replaces `PixAICuda` (foidfinder/backends/cuda/engine.py:65-184): `engine(images)` returns fp32 logits
 [B, num_tags], the first call for a batch size allocates that size's activation buffers and captures the
-forward in a CUDA graph (engine.py:163-184), later calls replay it. Weights stay owned by this object
-(torch tensors) and are handed to the library as device pointers.
+forward in a CUDA graph (engine.py:163-184), later calls replay it. The input is what PixAICuda takes —
+normalised pixels [B, S, S, 3] of any float dtype, cast to fp16 as the reference's static input does
+(engine.py:170, :182) — or uint8 images [B, S, S, 3], normalised on the GPU with the config's mean/std.
+Weights stay owned by this object (torch tensors) and are handed to the library as device pointers.
 """
 
 from __future__ import annotations
@@ -143,28 +145,40 @@ class Engine:
         topk: bool = True,
         graph: bool = True,
     ) -> tuple[torch.Tensor, torch.Tensor | None, torch.Tensor | None]:
-        """images [B, S, S, 3] uint8 -> (logits [B, tags] f32, top-k indices [B, k] int32, values [B, k] f32)."""
+        """images [B, S, S, 3] uint8, or normalised float pixels (any float dtype, used as fp16) ->
+        (logits [B, tags] f32, top-k indices [B, k] int32, values [B, k] f32)."""
         cfg = self.cfg
-        if images.dtype != torch.uint8 or images.dim() != 4 or tuple(images.shape[1:]) != (cfg.image_size,) * 2 + (3,):
-            raise ValueError(f"images must be uint8 [B, {cfg.image_size}, {cfg.image_size}, 3]")
-        images = images.to(self.device, non_blocking=True).contiguous()
+        pixels = images.is_floating_point()
+        if (images.dtype != torch.uint8 and not pixels) or images.dim() != 4 or \
+                tuple(images.shape[1:]) != (cfg.image_size,) * 2 + (3,):
+            raise ValueError(f"images must be uint8 or normalised float pixels [B, {cfg.image_size}, "
+                             f"{cfg.image_size}, 3]")
+        if pixels:
+            images = images.to(self.device, torch.float16, non_blocking=True).contiguous()
+        else:
+            images = images.to(self.device, non_blocking=True).contiguous()
         B = images.shape[0]
         if logits is None:
             logits = torch.empty(B, cfg.num_tags, device=self.device, dtype=torch.float32)
         idx = torch.empty(B, cfg.topk, device=self.device, dtype=torch.int32) if topk and cfg.topk else None
         val = torch.empty(B, cfg.topk, device=self.device, dtype=torch.float32) if idx is not None else None
-        fn = _lib.lib().ff_engine_forward if graph else _lib.lib().ff_engine_forward_eager
+        lib = _lib.lib()
+        ip = idx.data_ptr() if idx is not None else None
+        vp = val.data_ptr() if val is not None else None
         with torch.cuda.device(self.device):
             stream = torch.cuda.current_stream(self.device).cuda_stream
-            _lib.check(
-                fn(self._h, images.data_ptr(), B, logits.data_ptr(), idx.data_ptr() if idx is not None else None,
-                   val.data_ptr() if val is not None else None, stream),
-                "ff_engine_forward",
-            )
+            if pixels:
+                rc = lib.ff_engine_forward_pixels(self._h, images.data_ptr(), B, logits.data_ptr(), ip, vp,
+                                                  1 if graph else 0, stream)
+            else:
+                fn = lib.ff_engine_forward if graph else lib.ff_engine_forward_eager
+                rc = fn(self._h, images.data_ptr(), B, logits.data_ptr(), ip, vp, stream)
+            _lib.check(rc, "ff_engine_forward")
         return logits, idx, val
 
     def __call__(self, images: torch.Tensor) -> torch.Tensor:
-        """images [B, S, S, 3] uint8 -> logits [B, num_tags] f32 (PixAICuda.__call__, engine.py:163-184)."""
+        """images [B, S, S, 3] normalised float pixels or uint8 -> logits [B, num_tags] f32 (PixAICuda.__call__,
+        engine.py:163-184)."""
         return self.forward(images, topk=False)[0]
 
     @property

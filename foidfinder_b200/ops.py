@@ -248,6 +248,21 @@ def resize_pad(image: torch.Tensor, new_h: int, new_w: int, size: int, out: torc
         torch.cuda.current_stream(image.device).synchronize()  # the workspace is freed on return
 
 
+def letterbox_aa_f16(image: torch.Tensor, new_h: int, new_w: int, size: int, out: torch.Tensor) -> None:
+    """uint8 [h, w, 3] CUDA image -> out fp16 [size, size, 3] normalised pixels: PixAI's float letterbox
+    (foidfinder/backends/cuda/preprocess.py:16-32): /255, antialiased bilinear resize to (new_h, new_w) in
+    f32, x * 2 - 1, centred on a canvas of -1."""
+    _cuda(image, out)
+    _need(image.dtype == torch.uint8 and image.dim() == 3 and image.shape[2] == 3, "letterbox_aa_f16: uint8 [h, w, 3]")
+    _need(out.dtype == torch.float16 and tuple(out.shape[-3:]) == (size, size, 3) and out.is_contiguous(),
+          "letterbox_aa_f16: out must be contiguous fp16 [size, size, 3]")
+    image = image.contiguous()
+    h, w = image.shape[:2]
+    with torch.cuda.device(image.device):
+        check(lib().ff_letterbox_aa_f16(_ptr(image), h, w, new_h, new_w, size, _ptr(out), _stream(image)),
+              "letterbox_aa_f16")
+
+
 def patchify_windowed(images: torch.Tensor, patch: int, mean, std, window: int, out: torch.Tensor) -> None:
     """uint8 [B, S, S, 3] -> fp16 patch rows [B * (S/patch)^2, k_pad] in window order (window x window tiles)."""
     _cuda(images, out)

@@ -107,18 +107,31 @@ def random_pool(cfg: ModelConfig, n) -> dict[str, torch.Tensor]:
     return out
 
 
-def fwht_rows(w: torch.Tensor, block: int) -> torch.Tensor:
-    """w [N, K] -> w · blockdiag(H_block) with the normalised Sylvester H (engine.py:29-34), computed as a
-    fast Walsh-Hadamard transform of each row in float64."""
-    N, K = w.shape
-    x = w.double().reshape(N, K // block, block)
-    h = 1
-    while h < block:
-        x = x.reshape(N, K // block, block // (2 * h), 2, h)
-        a, b = x[:, :, :, 0, :], x[:, :, :, 1, :]
-        x = torch.stack([a + b, a - b], dim=3)
-        h *= 2
-    return (x.reshape(N, K) / math.sqrt(block)).float()
+def hadamard(n: int, device: str | torch.device = "cpu") -> torch.Tensor:
+    """Normalised Sylvester Hadamard matrix H_n / sqrt(n) as float32 (engine.py:29-34): built in float64 by
+    doubling, divided by sqrt(n) in float64, then rounded once to float32."""
+    h = torch.ones(1, 1, dtype=torch.float64)
+    while h.shape[0] < n:
+        h = torch.cat([torch.cat([h, h], 1), torch.cat([h, -h], 1)], 0)
+    return (h / math.sqrt(n)).to(device=device, dtype=torch.float32)
+
+
+_ROT_CACHE: dict[tuple[int, int, str], torch.Tensor] = {}
+
+
+def rotate_rows(w: torch.Tensor, block: int) -> torch.Tensor:
+    """w [N, K] -> w · blockdiag(H_block) as convert_checkpoint computes it (engine.py:58-60): one float32
+    matmul by the full K x K block-diagonal matrix on w's device. The same torch call on the same device
+    gives the reference's float32 sums bit for bit, so the int8 codes derived from them are the
+    reference's codes, ties included (a shorter per-block product or an FWHT rounds differently)."""
+    K = w.shape[1]
+    key = (K, block, str(w.device))
+    rot = _ROT_CACHE.get(key)
+    if rot is None:
+        rot = torch.block_diag(*[hadamard(block, w.device)] * (K // block))
+        _ROT_CACHE.clear()  # keep one matrix (K = 2816 or 4864 takes 32-95 MB)
+        _ROT_CACHE[key] = rot
+    return w.float() @ rot
 
 
 def quantize_rows_int8(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
@@ -194,7 +207,7 @@ def convert(raw: dict[str, torch.Tensor], cfg: ModelConfig, device: str | torch.
             ),
         }
         for name, (w, b, block) in lin.items():
-            q, s = quantize_rows_int8(fwht_rows(w, block))
+            q, s = quantize_rows_int8(rotate_rows(w, block))
             put(f"{p}{name}.qweight", q)
             put(f"{p}{name}.wscale", s)
             put(f"{p}{name}.bias", b.contiguous())
@@ -272,30 +285,62 @@ def pixai_random_raw(cfg: ModelConfig, seed: int = 0, device: str | torch.device
     return raw
 
 
+# Quantised block linears of the PixAI checkpoint -> which Hadamard block rotates their input (engine.py:45:
+# H1024 for the dim-wide inputs, H128 for the hidden; ModelConfig.rot_block_dim / rot_block_hidden).
+PIXAI_QUANTIZED = {"attn.qkv": "dim", "attn.proj": "dim", "mlp.fc1": "dim", "mlp.fc2": "hidden"}
+PIXAI_INT8_FORMAT = "foidfinder-pixai-int8-v1"  # the reference's `foidfinder convert` output (engine.py:46)
+
+
+def is_pixai_int8(raw: dict) -> bool:
+    """True for the reference's converted checkpoint (PixAICuda.__init__'s test, engine.py:71)."""
+    return "blocks.0.attn.qkv.qweight" in raw
+
+
+def pixai_convert_checkpoint(raw: dict[str, torch.Tensor], cfg: ModelConfig) -> dict[str, torch.Tensor]:
+    """Official fp32 PixAI state dict -> the reference's int8 checkpoint (convert_checkpoint,
+    foidfinder/backends/cuda/engine.py:49-62): every block linear becomes `.qweight` (int8 codes of
+    W · blockdiag(H) computed as one float32 matmul on the tensor's device, per-output-channel scale),
+    `.wscale` (f32) and `.bias` (f32); every other tensor is passed through. Same tensor names, same codes."""
+    out = {k: v for k, v in raw.items() if not any(f".{n}." in k for n in PIXAI_QUANTIZED)}
+    for i in range(cfg.depth):
+        for name, which in PIXAI_QUANTIZED.items():
+            block = cfg.rot_block_dim if which == "dim" else cfg.rot_block_hidden
+            p = f"blocks.{i}.{name}"
+            out[p + ".qweight"], out[p + ".wscale"] = quantize_rows_int8(rotate_rows(raw[p + ".weight"].float(), block))
+            out[p + ".bias"] = raw[p + ".bias"].float().contiguous()
+    return out
+
+
 def convert_pixai(raw: dict[str, torch.Tensor], cfg: ModelConfig,
                   device: str | torch.device | None = None) -> dict[str, torch.Tensor]:
-    """Official PixAI fp32 checkpoint -> the engine format.
+    """Official PixAI fp32 checkpoint, or the reference's int8 checkpoint (`foidfinder convert`, format
+    foidfinder-pixai-int8-v1), -> the engine format. The fp32 form is first quantised exactly as
+    `convert_checkpoint` does (`pixai_convert_checkpoint`), so both sources give identical engine weights.
 
-    Block linears as `convert_checkpoint` (foidfinder/backends/cuda/engine.py:49-62): W' = W · blockdiag(H)
-    (H1024 for qkv, proj, fc1; H128 for fc2), per-output-channel int8, f32 bias; the attention scale
-    1/sqrt(64) of F.scaled_dot_product_attention (reference.py:125) is folded into the q rows and bias (a
-    power of two, so the codes are those of the unscaled rows). The stem and tables follow
-    PixAITorch.__init__ (reference.py:70-98): patch weight in (kh, kw, c) column order, the pretraining
-    position embedding tiled over the grid and put in window order, window and global RoPE tables (the
-    global one at positions scaled by window / grid, window-ordered), stored angle-major [32, n]; the pool's
-    position embedding in window order and its query carrying the 1/8 scale. The hidden is padded with zero
-    fc1 rows / fc2 columns to mlp_hidden_pad (4736 -> 4864) so fc1 runs on 256-wide tiles; the padding
-    stays exactly zero through GELU and the H128 blocks. The patch embedding's bias, if the checkpoint has
-    one, is not used — the reference's stem has none (reference.py:112)."""
+    From the int8 checkpoint: `.qweight` codes are used unchanged. The attention scale 1/sqrt(64) of
+    F.scaled_dot_product_attention (reference.py:125), which the reference applies in its QKV epilogue
+    (engine.py:26), is folded into the q rows' `.wscale` and `.bias`: a power of two, so the product equals
+    the reference's scaled output. The hidden is padded to mlp_hidden_pad (4736 -> 4864) with zero fc1
+    rows (zero codes and bias) and zero fc2 columns (one extra all-zero H128 block), so fc1 runs on
+    256-wide tiles; the padding stays exactly zero through GELU and the H128 rotation.
+    The stem and tables follow PixAITorch.__init__ (reference.py:70-98): patch weight in (kh, kw, c)
+    column order, the pretraining position embedding tiled over the grid and put in window order, window
+    and global RoPE tables (the global one at positions scaled by window / grid, window-ordered), stored
+    angle-major [32, n]; the pool's position embedding in window order and its query carrying the 1/8
+    scale. The patch embedding's bias, if the checkpoint has one, is not used — the reference's stem has
+    none (reference.py:112)."""
+    if not is_pixai_int8(raw):
+        raw = pixai_convert_checkpoint(raw, cfg)
     dev = torch.device(device) if device is not None else raw["pos_embed"].device
     D, G, L, win, H, Hp = cfg.dim, cfg.grid, cfg.patches, cfg.window, cfg.mlp_hidden, cfg.mlp_hidden_pad
-    perm = window_order(G, win).to(raw["pos_embed"].device)
+    src = raw["pos_embed"].device
+    perm = window_order(G, win).to(src)
     out: dict[str, torch.Tensor] = {}
 
     def put(name: str, t: torch.Tensor) -> None:
         out[name] = t.to(dev).contiguous()
 
-    pw = torch.zeros(D, cfg.k_pad, device=perm.device)
+    pw = torch.zeros(D, cfg.k_pad, device=src)
     pw[:, : cfg.k_patch] = raw["patch_embed.proj.weight"].float().permute(0, 2, 3, 1).reshape(D, -1)
     put("patch_w", pw.half())
     pos = raw["pos_embed"].float()[0, 1:]
@@ -318,33 +363,37 @@ def convert_pixai(raw: dict[str, torch.Tensor], cfg: ModelConfig,
     put("pool.kv.bias", raw["head_pool.kv.bias"].float())
     put("pool.proj.weight", raw["head_pool.proj.weight"].half())
     put("pool.proj.bias", raw["head_pool.proj.bias"].float())
-    hw = torch.zeros(cfg.num_tags_pad, D, device=perm.device)
+    hw = torch.zeros(cfg.num_tags_pad, D, device=src)
     hw[: cfg.num_tags] = raw["head.weight"].float()
-    hb = torch.zeros(cfg.num_tags_pad, device=perm.device)
+    hb = torch.zeros(cfg.num_tags_pad, device=src)
     hb[: cfg.num_tags] = raw["head.bias"].float()
     put("head.weight", hw.half())
     put("head.bias", hb)
+    pad_scale = torch.tensor(1e-12 / 127.0)  # what quantize_rows_int8 gives an all-zero row
     for i in range(cfg.depth):
         p = f"blocks.{i}."
         for n in ("norm1", "norm2"):
             put(p + n + ".weight", raw[p + n + ".weight"].float())
             put(p + n + ".bias", raw[p + n + ".bias"].float())
-        qkv_w, qkv_b = raw[p + "attn.qkv.weight"].float().clone(), raw[p + "attn.qkv.bias"].float().clone()
-        qkv_w[:D] *= scale
-        qkv_b[:D] *= scale
-        lin = {
-            "qkv": (qkv_w, qkv_b, cfg.rot_block_dim),
-            "proj": (raw[p + "attn.proj.weight"].float(), raw[p + "attn.proj.bias"].float(), cfg.rot_block_dim),
-            "fc1": (torch.nn.functional.pad(raw[p + "mlp.fc1.weight"].float(), (0, 0, 0, Hp - H)),
-                    torch.nn.functional.pad(raw[p + "mlp.fc1.bias"].float(), (0, Hp - H)), cfg.rot_block_dim),
-            "fc2": (torch.nn.functional.pad(raw[p + "mlp.fc2.weight"].float(), (0, Hp - H)),
-                    raw[p + "mlp.fc2.bias"].float(), cfg.rot_block_hidden),
-        }
-        for name, (w, b, block) in lin.items():
-            q, s = quantize_rows_int8(fwht_rows(w, block))
-            put(f"{p}{name}.qweight", q)
-            put(f"{p}{name}.wscale", s)
-            put(f"{p}{name}.bias", b.contiguous())
+
+        def q(name: str):
+            return (raw[f"{p}{name}.qweight"], raw[f"{p}{name}.wscale"].float().clone(),
+                    raw[f"{p}{name}.bias"].float().clone())
+
+        qw, qs, qb = q("attn.qkv")
+        qs[:D] *= scale
+        qb[:D] *= scale
+        f1w, f1s, f1b = q("mlp.fc1")
+        f1w = torch.nn.functional.pad(f1w, (0, 0, 0, Hp - H))
+        f1s = torch.cat([f1s, pad_scale.to(f1s).expand(Hp - H)])
+        f1b = torch.nn.functional.pad(f1b, (0, Hp - H))
+        f2w, f2s, f2b = q("mlp.fc2")
+        f2w = torch.nn.functional.pad(f2w, (0, Hp - H))
+        for name, (w_, s_, b_) in {"qkv": (qw, qs, qb), "proj": q("attn.proj"), "fc1": (f1w, f1s, f1b),
+                                   "fc2": (f2w, f2s, f2b)}.items():
+            put(f"{p}{name}.qweight", w_.to(torch.int8))
+            put(f"{p}{name}.wscale", s_)
+            put(f"{p}{name}.bias", b_)
     return out
 
 

@@ -116,10 +116,13 @@ int ff_rot_q8_h128(const uint16_t* x, int rows, int cols, int8_t* out, float* ro
  *   FF_EPI_BIAS, FF_EPI_RESIDUAL, FF_EPI_SWIGLU, but the codes and row scales live in a static device
  *   array built into the library (held by every GPU that loads it until the process exits).
  *   Limits: rows <= 8192 and rows * cols <= 8 MiB; larger calls fail with FF_ERR_INVALID_ARGUMENT.
- *   err: device int that records a bounded-wait timeout (NULL: a word inside the static array).
- *   The first call on a device resolves the array's address and clears its error word (synchronising
- *   that device); make that first call before any stream capture. All calls share the array: calls
- *   that overlap on the GPU (e.g. on two streams) race.
+ *   err: required device int (from the caller's pool) where a bounded-wait timeout is recorded as a
+ *   non-zero code; the caller clears it. NULL fails with FF_ERR_INVALID_ARGUMENT.
+ *   The array is part of the library's CUDA module, which the default lazy module loading brings onto a
+ *   device only at the first call there (that call resolves the array's address). Make one call per
+ *   device at start-up, before the host reserves the remaining GPU memory for its pool (or set
+ *   CUDA_MODULE_LOADING=EAGER), and before any stream capture. All calls share the array and it keeps
+ *   the last call's contents: calls that overlap on the GPU (e.g. on two streams) race.
  */
 int ff_linear_w8a8_noalloc(const uint16_t* x, const float* gamma, const float* beta, float eps, int rows, int cols,
                            int valid_cols, int block, const int8_t* W, const float* col_scale, const float* bias,
@@ -284,6 +287,16 @@ int ff_resize_pad(const uint8_t* src, int h, int w, int new_h, int new_w, int si
                   void* workspace, int64_t workspace_bytes, void* stream);
 int64_t ff_resize_pad_workspace_bytes(int h, int w, int new_h, int new_w, int filter);
 
+/*
+ * PixAI's letterbox in float on the GPU: src [h, w, 3] uint8 RGB -> dst [size, size, 3] fp16 normalised
+ * pixels (the engine's float input): pixels / 255, resized to (new_h, new_w) by antialiased bilinear
+ * interpolation in f32 (torch F.interpolate(mode="bilinear", align_corners=False, antialias=True)),
+ * x * 2 - 1 rounded to fp16, centred at ((size - new_h) / 2, (size - new_w) / 2) on a canvas of -1.
+ * Replaces foidfinder/backends/cuda/preprocess.py:16-32 (per image). No workspace.
+ */
+int ff_letterbox_aa_f16(const uint8_t* src, int h, int w, int new_h, int new_w, int size, uint16_t* dst,
+                        void* stream);
+
 typedef struct ff_engine ff_engine;
 
 /* Validates the config, keeps the weight pointers (the caller keeps them alive) and binds to `device`. */
@@ -301,6 +314,16 @@ int ff_engine_forward(ff_engine* e, const uint8_t* images, int B, float* logits,
 /* Same forward without a graph (each kernel launched directly); used for debugging and tests. */
 int ff_engine_forward_eager(ff_engine* e, const uint8_t* images, int B, float* logits, int32_t* topk_idx,
                             float* topk_val, void* stream);
+
+/*
+ * The forward from normalised fp16 pixels [B, S, S, 3] on the device instead of uint8 images: the input
+ * PixAICuda.__call__ takes (engine.py:163-165, "normalized pixels"; the reference casts any float dtype to
+ * fp16 into its static input) and ff_letterbox_aa_f16 writes. The patch rows take the pixels as they are
+ * (no mean/std). use_graph != 0: replay this batch size's graph for fp16 input (captured on first use);
+ * 0: launch the kernels directly.
+ */
+int ff_engine_forward_pixels(ff_engine* e, const uint16_t* pixels, int B, float* logits, int32_t* topk_idx,
+                             float* topk_val, int use_graph, void* stream);
 
 /* Kernel classes of ff_engine_profile. */
 #define FF_PROF_STEM_PREP 0 /* patchify + class-token rows */

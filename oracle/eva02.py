@@ -35,11 +35,13 @@ def rope_tables(grid: int, ref: int, head_dim: int = 64) -> tuple[torch.Tensor, 
 
 
 def patchify(images: torch.Tensor, patch: int, mean, std) -> torch.Tensor:
-    """uint8 [B, S, S, 3] -> normalised f32 patches [B, G*G, p*p*3] in (kh, kw, c) order."""
+    """uint8 [B, S, S, 3] -> normalised f32 patches [B, G*G, p*p*3] in (kh, kw, c) order: u * f32(1/255) - mean
+    rounded once to f32 (exact in f64 first, as a fused multiply-add), then times f32(1/std)."""
     B, S = images.shape[:2]
     G = S // patch
-    x = images.float() * np.float32(1.0 / 255.0)
-    x = (x - torch.tensor(mean, dtype=torch.float32)) * (1.0 / torch.tensor(std, dtype=torch.float32))
+    m = torch.tensor(mean, dtype=torch.float32).double()
+    x = (images.double() * float(np.float32(1.0 / 255.0)) - m).float()
+    x = x * (1.0 / torch.tensor(std, dtype=torch.float32))
     x = x.view(B, G, patch, G, patch, 3).permute(0, 1, 3, 2, 4, 5)
     return x.reshape(B, G * G, patch * patch * 3)
 

@@ -6,6 +6,9 @@
 - `gelu_tanh`    foidfinder/backends/cuda/csrc/common.cuh:55-56 (the fc1 epilogue's tanh GELU)
 - `forward_fp32` reference.py:109-140 (PixAITorch.forward + pool_head, f32, official checkpoint names)
 - `forward_int8` foidfinder/backends/cuda/engine.py:142-161 (PixAICuda._forward: int8 blocks, fp16 storage)
+- `rgb_on_white` foidfinder/image.py:41-48 (transparency composited onto white)
+- `preprocess`   foidfinder/backends/cuda/preprocess.py:16-32 (float letterbox: /255, antialiased bilinear
+                 F.interpolate, x * 2 - 1 to fp16 on a -1 canvas), run with torch on the CPU
 """
 
 from __future__ import annotations
@@ -43,6 +46,39 @@ def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.T
     x0, x1 = xf[..., 0], xf[..., 1]
     return torch.stack([x0 * cos - x1 * sin, x0 * sin + x1 * cos], dim=-1).flatten(-2).to(x.dtype)
 
+
+
+def rgb_on_white(image):
+    """PIL image -> RGB with any transparency composited onto white (foidfinder/image.py:41-48)."""
+    from PIL import Image
+
+    if image.mode == "RGB":
+        return image
+    rgba = image.convert("RGBA")
+    canvas = Image.new("RGBA", rgba.size, (255, 255, 255, 255))
+    canvas.alpha_composite(rgba)
+    return canvas.convert("RGB")
+
+
+@torch.no_grad()
+def preprocess(images: list, size: int = 1008) -> torch.Tensor:
+    """PIL images -> [B, size, size, 3] fp16 normalised pixels, as preprocess.py:16-32 computes them (on the
+    CPU here): pixels / 255 in f32, the longer side scaled to `size` with F.interpolate(mode="bilinear",
+    align_corners=False, antialias=True) when the size changes, x * 2 - 1 rounded to fp16, centred on -1."""
+    import numpy as np
+    import torch.nn.functional as F
+
+    out = torch.full((len(images), size, size, 3), -1.0, dtype=torch.half)
+    for b, image in enumerate(images):
+        x = torch.from_numpy(np.array(rgb_on_white(image))).permute(2, 0, 1)[None].float().div_(255.0)
+        h, w = x.shape[-2:]
+        r = min(size / h, size / w)
+        nh, nw = int(h * r), int(w * r)
+        if (nh, nw) != (h, w):
+            x = F.interpolate(x, size=(nh, nw), mode="bilinear", align_corners=False, antialias=True)
+        top, left = (size - nh) // 2, (size - nw) // 2
+        out[b, top : top + nh, left : left + nw] = (x[0].permute(1, 2, 0) * 2.0 - 1.0).half()
+    return out
 
 
 # ---------------------------------------------------------------- whole model

@@ -87,3 +87,96 @@ def test_gpu_letterbox_matches_host_letterbox(cuda_device):
             host = letterbox(im, 448, resample, pad)
             gpu = letterbox_gpu(im, 448, resample, pad, cuda_device).cpu().numpy()
             np.testing.assert_array_equal(gpu, host)
+
+
+def _reference_sample_images():
+    """The reference's preprocessing fixture shapes (tests/conftest.py:18-27): downscale, upscale and
+    exact-size paths, plus an RGBA image composited onto white (seeded noise, blurred so the resize filter
+    matters)."""
+    from PIL import ImageFilter
+
+    rng = np.random.default_rng(0)
+    blur = ImageFilter.GaussianBlur(3)
+    ims = [Image.fromarray(rng.integers(0, 256, (h, w, 3), dtype=np.uint8)).filter(blur)
+           for w, h in ((1500, 2100), (700, 400), (1008, 1008))]
+    return [*ims, Image.fromarray(rng.integers(0, 256, (600, 900, 4), dtype=np.uint8))]
+
+
+def test_pixai_float_letterbox_matches_reference_preprocess(cuda_device):
+    """ff_letterbox_aa_f16 (via backend.preprocess) against the reference's preprocess.py:16-32 restated on
+    the CPU (oracle.pixai.preprocess: torch F.interpolate with antialias): the reference's own bar,
+    |dpixel| < 2e-3, one fp16 step (tests/test_cuda_engine.py:29-35)."""
+    from foidfinder_b200.backend import preprocess
+    from oracle import pixai as P
+
+    ims = _reference_sample_images()
+    got = preprocess(ims, 1008, cuda_device).float().cpu()
+    want = P.preprocess(ims, 1008).float()
+    for g, w in zip(got, want):
+        d = (g - w).abs()
+        assert d.max().item() < 2e-3, d.max().item()
+        assert (d > 0).float().mean().item() < 0.01  # only rounding ties of the fp16 step differ
+
+
+@pytest.mark.parametrize("arch", ["eva02", "pixai"])
+def test_engine_float_pixels_match_uint8_path(cuda_device, no_device_error, arch):
+    """Engine.__call__ takes the reference's normalised float pixels (PixAICuda.__call__, engine.py:163-165).
+    Pixels equal to what the uint8 path's patchify computes ((u * (1/255) - mean) / std in one fused f32
+    step, then fp16) give bit-identical logits through both graphs; float32 input is cast to fp16 as the
+    reference's static input does."""
+    from foidfinder_b200.config import EVA02_L, PIXAI_1008
+    from foidfinder_b200.engine import Engine
+
+    if arch == "pixai":
+        cfg = PIXAI_1008.with_(name="px-float", image_size=336, depth=2, window=8, global_blocks=(1,))
+    else:
+        cfg = EVA02_L.with_(name="eva-float", image_size=112, depth=2)
+    eng = Engine(cfg, device=0, seed=4)
+    u8 = torch.randint(0, 256, (2, cfg.image_size, cfg.image_size, 3), generator=torch.Generator().manual_seed(8),
+                       dtype=torch.uint8)
+    mean = torch.tensor(cfg.mean, dtype=torch.float32).double()
+    inv_std = (1.0 / torch.tensor(cfg.std, dtype=torch.float32)).double()
+    one_255 = float(np.float32(1.0 / 255.0))
+    px = ((u8.double() * one_255 - mean).float().double() * inv_std).float().half()
+    a = eng(u8)
+    b = eng(px.to(cuda_device))
+    c = eng(px.float())  # float32 on the host: moved and cast to fp16
+    torch.cuda.synchronize()
+    assert torch.equal(a.cpu(), b.cpu()) and torch.equal(b.cpu(), c.cpu())
+    eng.close()
+
+
+def test_pixai_backend_from_model_directories(cuda_device, no_device_error, tmp_path):
+    """CUDABackend(model_dir) on a PixAI directory with the official fp32 checkpoint and on one with the
+    reference's `foidfinder convert` int8 output: identical predictions, equal to the engine run on the
+    reference's preprocessing of the same image (the CPU restatement) up to the fp16 pixel step."""
+    import json
+
+    from safetensors.torch import save_file
+
+    from foidfinder_b200 import weights as W
+    from foidfinder_b200.backend import CUDABackend
+    from foidfinder_b200.config import PIXAI_1008
+    from oracle import pixai as P
+
+    cfg = PIXAI_1008.with_(name="px-dir", image_size=336, depth=2, window=8, global_blocks=(1,), num_tags=1000)
+    raw = W.pixai_random_raw(cfg, seed=9)
+    for name, tensors, meta in (("official", raw, None),
+                                ("converted", W.pixai_convert_checkpoint(raw, cfg), {"format": W.PIXAI_INT8_FORMAT})):
+        d = tmp_path / name
+        d.mkdir()
+        save_file({k: v.contiguous() for k, v in tensors.items()}, str(d / "model.safetensors"), meta)
+        (d / "config.json").write_text(json.dumps({"num_classes": cfg.num_tags}))
+    ims = _reference_sample_images()[1:3]
+    preds = []
+    for name in ("official", "converted"):
+        be = CUDABackend(tmp_path / name, config=cfg, device=0)
+        preds.append([be.predict(im) for im in ims])
+        ref = [torch.sigmoid(be.engine(P.preprocess([im], cfg.image_size).to(cuda_device)))[0].cpu().numpy()
+               for im in ims]
+        for p, r in zip(preds[-1], ref):
+            assert p.shape == (cfg.num_tags,)
+            np.testing.assert_allclose(p, r, rtol=0, atol=5e-3)
+        be.engine.close()
+    for a, b in zip(*preds):
+        np.testing.assert_array_equal(a, b)

@@ -108,7 +108,9 @@ def test_engine_rejects_bad_input(cuda_device):
     with pytest.raises(ValueError):
         eng(torch.zeros(1, 100, 100, 3, dtype=torch.uint8))
     with pytest.raises(ValueError):
-        eng(torch.zeros(1, 112, 112, 3, dtype=torch.float32))
+        eng(torch.zeros(1, 112, 112, 3, dtype=torch.int32))
+    with pytest.raises(ValueError):
+        eng(torch.zeros(1, 112, 112, 4, dtype=torch.float16))
     eng.close()
 
 

@@ -41,8 +41,9 @@ def test_hadamard(gold, n):
     h = Q.hadamard(n).numpy()
     assert np.array_equal(h > 0, sign)
     assert np.float32(np.abs(h).max()) == gold[f"hadamard{n}_abs"]
-    # The FWHT used for the weights is the same matrix.
-    assert np.allclose(W.fwht_rows(torch.eye(n), n).numpy(), h, atol=1e-7)
+    # The weight converter rotates by the same float32 matrix.
+    assert np.array_equal(W.hadamard(n).numpy(), h)
+    assert np.array_equal(W.rotate_rows(torch.eye(n), n).numpy(), h)
 
 
 @pytest.mark.parametrize("quant", [Q.quantize_rows_int8, W.quantize_rows_int8])
@@ -54,16 +55,59 @@ def test_quantize_rows_int8(gold, inp, quant):
 
 @pytest.mark.parametrize("name", list(make_golden.CONV_SHAPES))
 def test_convert_checkpoint(gold, inp, name):
-    """Rotated per-channel int8 weights: the oracle's fp32 rotation and the weight converter's fp64 FWHT
-    each match the reference's codes except where a value lies within rounding of a half-step."""
+    """Rotated per-channel int8 weights are the reference's convert_checkpoint output bit for bit (codes and
+    scales), both in the oracle and in the weight converter: the same float32 matmul by blockdiag(H)."""
     w = torch.from_numpy(inp[f"conv_{name}_w"])
     ref_q, ref_s = gold[f"conv_{name}_qweight"], gold[f"conv_{name}_wscale"]
-    for rotated in (Q.rotate_weight(w, ROT_BLOCK[name]), W.fwht_rows(w, ROT_BLOCK[name])):
+    for rotated in (Q.rotate_weight(w, ROT_BLOCK[name]), W.rotate_rows(w, ROT_BLOCK[name])):
         q, s = W.quantize_rows_int8(rotated)
-        np.testing.assert_allclose(s.numpy(), ref_s, rtol=1e-6)
-        diff = np.abs(q.numpy().astype(np.int32) - ref_q.astype(np.int32))
-        assert diff.max() <= 1
-        assert (diff != 0).mean() < 1e-3
+        assert np.array_equal(q.numpy(), ref_q)
+        assert np.array_equal(s.numpy(), ref_s)
+
+
+def test_pixai_convert_checkpoint_matches_reference(gold, inp):
+    """The one-block checkpoint make_golden.py ran through the reference's convert_checkpoint: the
+    converter's own copy of that step (`pixai_convert_checkpoint`) writes the same tensors under the same
+    names, so a checkpoint written by `foidfinder convert` and one converted here are interchangeable."""
+    raw = {}
+    for name, shape in make_golden.CONV_SHAPES.items():
+        raw[f"blocks.0.{name}.weight"] = torch.from_numpy(inp[f"conv_{name}_w"])
+        raw[f"blocks.0.{name}.bias"] = torch.zeros(shape[0])
+    from foidfinder_b200.config import PIXAI_1008
+
+    conv = W.pixai_convert_checkpoint(raw, PIXAI_1008.with_(depth=1))
+    assert W.is_pixai_int8(conv)
+    for name in make_golden.CONV_SHAPES:
+        assert conv[f"blocks.0.{name}.qweight"].dtype == torch.int8
+        assert np.array_equal(conv[f"blocks.0.{name}.qweight"].numpy(), gold[f"conv_{name}_qweight"])
+        assert np.array_equal(conv[f"blocks.0.{name}.wscale"].numpy(), gold[f"conv_{name}_wscale"])
+        assert f"blocks.0.{name}.weight" not in conv
+
+
+def test_pixai_engine_weights_from_reference_int8(inp):
+    """convert_pixai on the official fp32 names and on the reference's int8 checkpoint of the same weights
+    gives identical engine weights: codes unchanged, the 1/8 attention scale folded into the q rows'
+    scale and bias (exact, a power of two), the hidden padded with zero rows/columns."""
+    from foidfinder_b200.config import PIXAI_1008
+
+    cfg = PIXAI_1008.with_(name="pixai-tiny", image_size=336, depth=2, window=8, global_blocks=(1,), dim=128,
+                           heads=2, mlp_hidden=384, num_tags=300, rot_block_dim=128)
+    raw = W.pixai_random_raw(cfg, seed=5, pre_grid=12)
+    ref_int8 = W.pixai_convert_checkpoint(raw, cfg)
+    a, b = W.convert_pixai(raw, cfg), W.convert_pixai(ref_int8, cfg)
+    assert a.keys() == b.keys()
+    for k in a:
+        assert torch.equal(a[k], b[k]), k
+    D, H, Hp = cfg.dim, cfg.mlp_hidden, cfg.mlp_hidden_pad
+    for i in range(cfg.depth):
+        p = f"blocks.{i}."
+        assert torch.equal(a[p + "qkv.qweight"], ref_int8[p + "attn.qkv.qweight"])
+        assert torch.equal(a[p + "qkv.wscale"][:D], ref_int8[p + "attn.qkv.wscale"][:D] * 0.125)
+        assert torch.equal(a[p + "qkv.wscale"][D:], ref_int8[p + "attn.qkv.wscale"][D:])
+        assert torch.equal(a[p + "fc1.qweight"][:H], ref_int8[p + "mlp.fc1.qweight"])
+        assert not a[p + "fc1.qweight"][H:].any() and not a[p + "fc1.bias"][H:].any()
+        assert torch.equal(a[p + "fc2.qweight"][:, :H], ref_int8[p + "mlp.fc2.qweight"])
+        assert a[p + "fc2.qweight"].shape == (D, Hp) and not a[p + "fc2.qweight"][:, H:].any()
 
 
 def test_pixai_axial_rope(gold, inp):
