@@ -4,12 +4,16 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
 
-One step = one forward of a batch of B seeded 448x448 uint8 images (B per GPU, images sharded by rank,
-no collective on the data path: `scaling` is weak). `value` is images/s of the whole job with inputs
-resident in HBM (CUDA-graph replays timed with CUDA events, max over ranks); `e2e` is the same metric
-through the public `Engine.forward` API with the per-step host->device copy of the images from pinned
-memory and the device->host copy of logits and top-50. The roofline entry covers the dominant kernel
-(the tcgen05 int8 GEMM, all four block GEMMs) from a live per-launch CUDA-event profile.
+One step = one forward of a global batch of B seeded 448x448 uint8 images (default 64),
+split contiguously over the N ranks (rank r takes `multigpu.shard_range(B, N, r)`; no collective on the
+data path; `scaling` is strong: the job's work is fixed as N grows). `value` is images/s of the whole job
+with inputs resident in HBM (CUDA-graph replays timed with CUDA events, max over ranks); `e2e` is the same
+metric through the public `Engine.forward` API with, every step, the host->device copy of each rank's
+images from pinned memory, the device->host copy of its logits, and the gather of every rank's top-50 to
+rank 0 (`multigpu.gather_rows`) and its copy to the host. `weak` repeats the device-timed measurement
+with B images per GPU (the per-GPU batch fixed as N grows). The roofline entry covers the dominant kernel
+(the tcgen05 int8 GEMM, all four block GEMMs) from a live per-launch CUDA-event profile of one rank's
+shard.
 
 `--impl reference` times the reference's CPU path instead: the fp32 PyTorch forward of the same model
 (the oracle restatement of foidfinder/backends/cuda/reference.py:109-131 with the EVA02 block), on all
@@ -52,7 +56,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--batch", type=int, default=None, help="images per GPU per step (default 64; pixai-1008: 16)")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="global images per step, split over the GPUs (default 64; pixai-1008: 16)")
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--config", default="eva02-l-448")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -181,6 +186,7 @@ def cpu_forward_timing(cfg, n_images: int, warmup: int = 1) -> tuple[float, int,
 
 
 def workload(cfg, B: int, world: int) -> dict:
+    """B: the global batch of one step, split over `world` GPUs."""
     if cfg.arch == "pixai":
         desc = (f"{cfg.name} int8 forward (the reference's PixAICuda workload): {cfg.image_size}px, {cfg.tokens} "
                 f"window-ordered tokens, {cfg.depth} blocks ({cfg.window}x{cfg.window} windows, global blocks "
@@ -190,11 +196,14 @@ def workload(cfg, B: int, world: int) -> dict:
         which = "BASELINE config 4" if cfg.head == "tree" else "BASELINE config 3"
         desc = (f"{cfg.name} int8 forward ({which}): {cfg.image_size}px, {cfg.tokens} tokens, "
                 f"{cfg.depth} blocks, dim {cfg.dim}, SwiGLU {cfg.mlp_hidden}, {cfg.num_tags} tags, top-{cfg.topk}")
+    from foidfinder_b200.multigpu import shard_sizes
+
     return {
         "workload": desc,
-        "batch_per_gpu": B,
-        "global_batch": B * world,
-        "parallelism": f"dp{world} (images sharded by rank, no collective)",
+        "global_batch": B,
+        "batch_per_gpu": shard_sizes(B, world),
+        "parallelism": f"dp{world} (one global batch split contiguously by rank; no collective on the data path, "
+                       "top-50 gathered to rank 0 in the e2e step)",
         "l2_policy": "no flush: each step streams > 1 GB of weights and activations, far above the 126 MB L2",
         "weights": "random-init N(0, 0.02), seed 0",
     }
@@ -220,7 +229,7 @@ def run_reference(args) -> None:
         "warmup": args.warmup,
         "ms_per_step": sec * 1e3,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic: seeded uint8 images U[0,255], random-init N(0,0.02) weights",
@@ -266,12 +275,20 @@ def run_ours(args) -> None:
             os.close(saved_stdout)
     from foidfinder_b200.config import CONFIGS
     from foidfinder_b200.engine import Engine
+    from foidfinder_b200.multigpu import gather_rows, shard_range
 
     cfg = CONFIGS[args.config]
-    B, K, W = args.batch or DEFAULT_BATCH[cfg.arch], args.steps, max(args.warmup, 3)
+    BG, K, W = args.batch or DEFAULT_BATCH[cfg.arch], args.steps, max(args.warmup, 3)
+    if BG < world:
+        raise SystemExit(f"global batch {BG} is smaller than the {world} GPUs")
+    lo, hi = shard_range(BG, world, rank)
+    B = hi - lo  # this rank's images of the global batch
     eng = Engine(cfg, device=local, seed=0)
-    g = torch.Generator(device=dev).manual_seed(1000 + rank)
-    imgs = torch.randint(0, 256, (B, cfg.image_size, cfg.image_size, 3), generator=g, dtype=torch.uint8, device=dev)
+    # One seeded global batch, identical on every rank; each rank keeps its contiguous shard.
+    g = torch.Generator(device=dev).manual_seed(1000)
+    batch = torch.randint(0, 256, (BG, cfg.image_size, cfg.image_size, 3), generator=g, dtype=torch.uint8, device=dev)
+    imgs = batch[lo:hi].contiguous()
+    del batch
     logits = torch.empty(B, cfg.num_tags, device=dev)
 
     def barrier():
@@ -286,45 +303,59 @@ def run_ours(args) -> None:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         return float(t.item())
 
-    for _ in range(W):
-        eng.forward(imgs, logits=logits)
-    barrier()
     stream = torch.cuda.current_stream(dev)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+
+    def timed_replays(x: torch.Tensor, out: torch.Tensor) -> float:
+        for _ in range(W):
+            eng.forward(x, logits=out)
         barrier()
         start.record(stream)
         for _ in range(K):
-            eng.forward(imgs, logits=logits)
+            eng.forward(x, logits=out)
         end.record(stream)
         barrier()
-        dev_ms = max_over_ranks(start.elapsed_time(end))
+        return max_over_ranks(start.elapsed_time(end))
 
-        # end to end through the public API, host buffers: H2D images, forward, D2H logits + top-k
+    with ClockSampler(local) as clocks:
+        dev_ms = timed_replays(imgs, logits)
+
+        # end to end through the public API, host buffers: H2D of this rank's images, forward, D2H of its
+        # logits, gather of every rank's top-50 to rank 0 and its D2H there
         host_in = imgs.cpu().pin_memory()
         host_logits = torch.empty(B, cfg.num_tags, pin_memory=True)
-        host_idx = torch.empty(B, cfg.topk, dtype=torch.int32, pin_memory=True)
-        host_val = torch.empty(B, cfg.topk, pin_memory=True)
+        host_idx = torch.empty(BG, cfg.topk, dtype=torch.int32, pin_memory=True)
+        host_val = torch.empty(BG, cfg.topk, pin_memory=True)
         dev_in = torch.empty_like(imgs)
-        for _ in range(W):
+
+        def e2e_step():
             dev_in.copy_(host_in, non_blocking=True)
             lg, ix, vl = eng.forward(dev_in, logits=logits)
             host_logits.copy_(lg, non_blocking=True)
-            host_idx.copy_(ix, non_blocking=True)
-            host_val.copy_(vl, non_blocking=True)
+            if world > 1:
+                ix, vl = gather_rows(ix, BG), gather_rows(vl, BG)
+            if rank == 0:
+                host_idx.copy_(ix, non_blocking=True)
+                host_val.copy_(vl, non_blocking=True)
+
+        for _ in range(W):
+            e2e_step()
         barrier()
         start.record(stream)
         for _ in range(K):
-            dev_in.copy_(host_in, non_blocking=True)
-            lg, ix, vl = eng.forward(dev_in, logits=logits)
-            host_logits.copy_(lg, non_blocking=True)
-            host_idx.copy_(ix, non_blocking=True)
-            host_val.copy_(vl, non_blocking=True)
+            e2e_step()
         end.record(stream)
         barrier()
         e2e_ms = max_over_ranks(start.elapsed_time(end))
-    h2d = host_in.numel()
-    d2h = host_logits.numel() * 4 + host_idx.numel() * 4 + host_val.numel() * 4
+
+        # weak scaling for context: the full batch on every GPU
+        if world > 1:
+            weak_imgs = imgs.repeat((BG + B - 1) // B, 1, 1, 1)[:BG].contiguous()
+            weak_logits = torch.empty(BG, cfg.num_tags, device=dev)
+            weak_ms = timed_replays(weak_imgs, weak_logits)
+            del weak_imgs, weak_logits
+    h2d = BG * cfg.image_size * cfg.image_size * 3  # every rank's shard, summed over the job
+    d2h = BG * cfg.num_tags * 4 + 2 * BG * cfg.topk * 4  # every rank's logits + the gathered top-50 on rank 0
 
     # batch-1 latency: p50 over individually timed graph replays
     one = imgs[:1].contiguous()
@@ -356,9 +387,9 @@ def run_ours(args) -> None:
     peak = 2.0 * peaks["bf16_sustained"]
     attn_tflops = cfg.attention_flops_per_image() * B / (prof["attention"][0] * 1e-3) / 1e12
 
-    total = world * B * K
+    total = BG * K
     line = {
-        "metric": metric_for(cfg, B),
+        "metric": metric_for(cfg, BG),
         "value": total / (dev_ms * 1e-3),
         "unit": UNIT,
         "n_gpus": world,
@@ -366,11 +397,11 @@ def run_ours(args) -> None:
         "warmup": W,
         "ms_per_step": dev_ms / K,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "int8",
         "data": "synthetic: seeded uint8 images U[0,255], random-init N(0,0.02) weights",
-        "config": workload(cfg, B, world),
+        "config": workload(cfg, BG, world),
         "e2e": {"value": total / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "latency_bs1_p50_ms": lat_p50,
         "gpu_launches": eng.launches_per_forward * K,
@@ -399,9 +430,13 @@ def run_ours(args) -> None:
             "ms_per_forward": gemm_ms,
         },
         "breakdown_ms_per_forward": {k: round(v[0], 4) for k, v in prof.items()},
+        "breakdown_batch": B,
         "attention_tflops": attn_tflops,
         "clocks": clocks.summary(),
     }
+    if world > 1:
+        line["weak"] = {"value": world * BG * K / (weak_ms * 1e-3), "unit": UNIT, "batch_per_gpu": BG,
+                        "ms_per_step": weak_ms / K, "scaling": "weak"}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sec, cores, sample = cpu_forward_timing(cfg, n_images=1 if cfg.arch == "pixai" else 3)
         line["cpu_baseline"] = {"value": 1.0 / sec, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}

@@ -7,7 +7,7 @@ The sources are compiled where they lie (nothing is copied), with the reference'
 (-O3 -std=c++20 --expt-relaxed-constexpr) plus sm_100 code generation, through
 torch.utils.cpp_extension (ninja) into oracle/_ref/ only.
 
-    python -m oracle.build_ref [/path/to/reference]
+    python -m oracle.build_ref /path/to/reference       (or FOIDFINDER_REFERENCE=/path/to/reference)
 """
 
 from __future__ import annotations
@@ -20,9 +20,18 @@ OUT = Path(__file__).resolve().parent / "_ref"
 NAME = "pixai_kernels"
 
 
-def build(ref_root: str | os.PathLike = "/root/reference", verbose: bool = False) -> Path | None:
-    """Returns the built library, or None when the reference tree is absent (e.g. on a GPU box)."""
-    csrc = Path(ref_root) / "foidfinder" / "backends" / "cuda" / "csrc"
+def reference_root(ref_root: str | os.PathLike | None = None) -> Path | None:
+    """The reference checkout: the argument, else $FOIDFINDER_REFERENCE, else None."""
+    root = ref_root if ref_root is not None else os.environ.get("FOIDFINDER_REFERENCE")
+    return Path(root) if root else None
+
+
+def build(ref_root: str | os.PathLike | None = None, verbose: bool = False) -> Path | None:
+    """Returns the built library, or None when no reference tree is given or found (e.g. on a GPU box)."""
+    root = reference_root(ref_root)
+    if root is None:
+        return None
+    csrc = root / "foidfinder" / "backends" / "cuda" / "csrc"
     if not (csrc / "kernels.cu").is_file():
         return None
     os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0")
@@ -42,4 +51,4 @@ def build(ref_root: str | os.PathLike = "/root/reference", verbose: bool = False
 
 
 if __name__ == "__main__":
-    print(build(sys.argv[1] if len(sys.argv) > 1 else "/root/reference", verbose=True))
+    print(build(sys.argv[1] if len(sys.argv) > 1 else None, verbose=True))

@@ -39,9 +39,9 @@ def patchify(images: torch.Tensor, patch: int, mean, std) -> torch.Tensor:
     rounded once to f32 (exact in f64 first, as a fused multiply-add), then times f32(1/std)."""
     B, S = images.shape[:2]
     G = S // patch
-    m = torch.tensor(mean, dtype=torch.float32).double()
+    m = torch.tensor(mean, dtype=torch.float32, device=images.device).double()
     x = (images.double() * float(np.float32(1.0 / 255.0)) - m).float()
-    x = x * (1.0 / torch.tensor(std, dtype=torch.float32))
+    x = x * (1.0 / torch.tensor(std, dtype=torch.float32, device=images.device))
     x = x.view(B, G, patch, G, patch, 3).permute(0, 1, 3, 2, 4, 5)
     return x.reshape(B, G * G, patch * patch * 3)
 
@@ -60,9 +60,11 @@ def _rope_qk(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, T: int, di
 
 
 def forward_fp32(raw: dict[str, torch.Tensor], cfg, images: torch.Tensor) -> torch.Tensor:
-    """fp32 EVA02 forward on the folded (unquantised) weights -> logits [B, num_tags]."""
+    """fp32 EVA02 forward on the folded (unquantised) weights -> logits [B, num_tags], on
+    the images' device."""
     B, T, D, H = images.shape[0], cfg.tokens, cfg.dim, cfg.heads
     eps = cfg.ln_eps
+    raw = {k: v.to(images.device) for k, v in raw.items()}
     x = patchify(images, cfg.patch, cfg.mean, cfg.std) @ raw["patch_w"].float().t() + raw["patch_b"].float()
     x = x + raw["pos_embed"][1:].float()
     cls = (raw["cls_token"].float() + raw["pos_embed"][0].float()).expand(B, 1, D)
@@ -138,7 +140,8 @@ def _lin(a8: torch.Tensor, rs: torch.Tensor, conv: dict, name: str) -> torch.Ten
 def forward_int8(
     conv: dict[str, torch.Tensor], cfg, images: torch.Tensor, trace: list | None = None, rot=None
 ) -> torch.Tensor:
-    """The GPU engine's arithmetic on the CPU, from the converted checkpoint -> logits [B, num_tags].
+    """The GPU engine's arithmetic, from the converted checkpoint -> logits [B, num_tags], on the images'
+    device (the CPU, or a GPU to check full-size models quickly).
 
     fp16 rounding points match the kernels: patches, x after the stem / each residual add, qkv, the
     attention output, the SwiGLU output h and the final-normed class tokens. If `trace` is a list it
@@ -146,13 +149,13 @@ def forward_int8(
     output, the normed class tokens and the logits (for teacher-forced kernel comparisons). `rot`
     replaces the activation quantiser (default `quant.rot_q8`)."""
     rot_q8 = rot or Q.rot_q8
-    conv = {k: v.cpu() for k, v in conv.items()}
+    conv = {k: v.to(images.device) for k, v in conv.items()}
     B, T, D, H, Hp = images.shape[0], cfg.tokens, cfg.dim, cfg.heads, cfg.mlp_hidden_pad
     eps = cfg.ln_eps
     patches = patchify(images, cfg.patch, cfg.mean, cfg.std).half().float()
     pw = conv["patch_w"].float()[:, : cfg.k_patch]
     stem = patches @ pw.t() + conv["pos_bias"].float()
-    x = torch.empty(B, T, D, dtype=torch.float16)
+    x = torch.empty(B, T, D, dtype=torch.float16, device=images.device)
     x[:, 1:] = stem.half()
     x[:, 0] = conv["cls_row"]
     x = x.reshape(B * T, D)

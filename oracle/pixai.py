@@ -6,6 +6,10 @@
 - `gelu_tanh`    foidfinder/backends/cuda/csrc/common.cuh:55-56 (the fc1 epilogue's tanh GELU)
 - `forward_fp32` reference.py:109-140 (PixAITorch.forward + pool_head, f32, official checkpoint names)
 - `forward_int8` foidfinder/backends/cuda/engine.py:142-161 (PixAICuda._forward: int8 blocks, fp16 storage)
+- `reference_engine_forward` engine.py:142-161 itself: the reference's launch sequence through the
+                 reference's own compiled kernels (torch.ops.foidfinder), with its fp16 torch stem and pool
+                 head (reference.py:103-107, :133-140) — the reference engine as a second, GPU checker
+The forwards run on the device of their inputs (the CPU, or a GPU to check full-size models quickly).
 - `rgb_on_white` foidfinder/image.py:41-48 (transparency composited onto white)
 - `preprocess`   foidfinder/backends/cuda/preprocess.py:16-32 (float letterbox: /255, antialiased bilinear
                  F.interpolate, x * 2 - 1 to fp16 on a -1 canvas), run with torch on the CPU
@@ -110,16 +114,16 @@ def forward_fp32(raw: dict[str, torch.Tensor], cfg, images: torch.Tensor) -> tor
     from . import quant as Q
 
     B, G, D, nh, L, win = images.shape[0], cfg.grid, cfg.dim, cfg.heads, cfg.patches, cfg.window
-    nw, eps = G // win, cfg.ln_eps
-    g = lambda k: raw[k].float()  # noqa: E731
-    perm = window_perm(G, win)
+    nw, eps, dev = G // win, cfg.ln_eps, images.device
+    g = lambda k: raw[k].to(dev).float()  # noqa: E731
+    perm = window_perm(G, win).to(dev)
     pw = g("patch_embed.proj.weight").permute(0, 2, 3, 1).reshape(D, -1)
     pos = g("pos_embed")[0, 1:]
     pre = int(round(pos.shape[0] ** 0.5))
     pos = pos.reshape(pre, pre, D).repeat(G // pre, G // pre, 1).reshape(L, D)[perm]
     x = (patch_rows(images, cfg) @ pw.t() + pos).reshape(B * L, D)
     x = Q.layer_norm(x, g("ln_pre.weight"), g("ln_pre.bias"), eps)
-    cw, sw, cg, sg = _window_tables(cfg)
+    cw, sw, cg, sg = (t.to(dev) for t in _window_tables(cfg))
     for i in range(cfg.depth):
         p = f"blocks.{i}."
         h = Q.layer_norm(x, g(p + "norm1.weight"), g(p + "norm1.bias"), eps)
@@ -140,9 +144,9 @@ def pool_head_fp32(x: torch.Tensor, raw: dict[str, torch.Tensor], cfg) -> torch.
 
     B, L, D = x.shape
     nh = cfg.heads
-    g = lambda k: raw[k].float()  # noqa: E731
+    g = lambda k: raw[k].to(x.device).float()  # noqa: E731
     h = Q.layer_norm(x, g("head_pool.norm.weight"), g("head_pool.norm.bias"), cfg.ln_eps)
-    h = h + g("head_pool.pos_embed")[window_perm(cfg.grid, cfg.window)]
+    h = h + g("head_pool.pos_embed")[window_perm(cfg.grid, cfg.window).to(x.device)]
     k, v = (h @ g("head_pool.kv.weight").t() + g("head_pool.kv.bias")).view(B, L, 2, nh, D // nh).permute(2, 0, 3, 1, 4)
     q = g("head_pool.q").reshape(1, nh, 1, D // nh).expand(B, nh, 1, D // nh)
     o = _sdpa(q, k, v, (D // nh) ** -0.5).reshape(B, D)
@@ -150,7 +154,8 @@ def pool_head_fp32(x: torch.Tensor, raw: dict[str, torch.Tensor], cfg) -> torch.
     return o @ g("head.weight").t() + g("head.bias")
 
 
-def forward_int8(conv: dict[str, torch.Tensor], cfg, images: torch.Tensor, trace: list | None = None) -> torch.Tensor:
+def forward_int8(conv: dict[str, torch.Tensor], cfg, images: torch.Tensor, trace: list | None = None,
+                 rot=None) -> torch.Tensor:
     """The GPU engine's PixAI arithmetic on the CPU, from the converted checkpoint -> logits [B, num_tags].
 
     PixAICuda._forward (foidfinder/backends/cuda/engine.py:142-161) step by step: fp16 stem (+ window-ordered
@@ -158,11 +163,13 @@ def forward_int8(conv: dict[str, torch.Tensor], cfg, images: torch.Tensor, trace
     the global one in the global blocks) -> attention per window / per image -> H1024+q8 -> proj + residual
     -> LN2+H1024+q8 -> fc1 + tanh GELU (csrc/common.cuh:56) -> H128+q8 -> fc2 + residual, and the pool head
     of reference.py:132-140 with fp16 storage between its steps. If `trace` is a list it receives one dict
-    per block (every stage's inputs and outputs) and a final dict (stem, pool stages, logits)."""
+    per block (every stage's inputs and outputs) and a final dict (stem, pool stages, logits). `rot`
+    replaces the activation quantiser (default `quant.rot_q8`)."""
     from . import eva02 as E
     from . import quant as Q
 
-    conv = {k: v.cpu() for k, v in conv.items()}
+    rot_q8 = rot or Q.rot_q8
+    conv = {k: v.to(images.device) for k, v in conv.items()}
     B, L, D, nh, win = images.shape[0], cfg.patches, cfg.dim, cfg.heads, cfg.window
     M, eps = B * L, cfg.ln_eps
     patches = patch_rows(images, cfg).half()
@@ -182,15 +189,15 @@ def forward_int8(conv: dict[str, torch.Tensor], cfg, images: torch.Tensor, trace
         p = f"blocks.{i}."
         x_in = x
         cos, sin, n = tables[cfg.is_global(i)]
-        a8, rs = Q.rot_q8(x, conv[p + "norm1.weight"], conv[p + "norm1.bias"], block=cfg.rot_block_dim, eps=eps)
-        qkv = Q.apply_rope_pairs(lin(a8, rs, p + "qkv"), cos, sin, torch.arange(M) % n, 2 * D).half()
+        a8, rs = rot_q8(x, conv[p + "norm1.weight"], conv[p + "norm1.bias"], block=cfg.rot_block_dim, eps=eps)
+        qkv = Q.apply_rope_pairs(lin(a8, rs, p + "qkv"), cos, sin, torch.arange(M, device=x.device) % n, 2 * D).half()
         o = E._attention(qkv, M // n, n, nh).half()
-        a8o, rso = Q.rot_q8(o, None, None, block=cfg.rot_block_dim)
+        a8o, rso = rot_q8(o, None, None, block=cfg.rot_block_dim)
         x = E._residual(x, lin(a8o, rso, p + "proj"))
         x_attn = x
-        a8m, rsm = Q.rot_q8(x, conv[p + "norm2.weight"], conv[p + "norm2.bias"], block=cfg.rot_block_dim, eps=eps)
+        a8m, rsm = rot_q8(x, conv[p + "norm2.weight"], conv[p + "norm2.bias"], block=cfg.rot_block_dim, eps=eps)
         h = gelu_tanh(lin(a8m, rsm, p + "fc1")).half()
-        a8h, rsh = Q.rot_q8(h, None, None, block=cfg.rot_block_hidden)
+        a8h, rsh = rot_q8(h, None, None, block=cfg.rot_block_hidden)
         x = E._residual(x, lin(a8h, rsh, p + "fc2"))
         if trace is not None:
             trace.append(dict(x_in=x_in, a8=a8, rs=rs, qkv=qkv, o=o, a8o=a8o, rso=rso, x_attn=x_attn, a8m=a8m, rsm=rsm,
@@ -208,3 +215,78 @@ def forward_int8(conv: dict[str, torch.Tensor], cfg, images: torch.Tensor, trace
         trace.append(dict(patches=patches.reshape(M, -1), x_stem=x_stem, x_pre=x_pre, x_final=x, xn=xn, kv=kv,
                           att=att, z=z, logits=logits))
     return logits
+
+
+Q_SCALE_REF = 0.125 * 1.4426950408889634  # engine.py:26: 1/sqrt(64) * log2(e), applied by the QKV epilogue
+
+
+@torch.no_grad()
+def reference_engine_forward(k, ck: dict[str, torch.Tensor], cfg, pixels: torch.Tensor, stages: int = 3) -> torch.Tensor:
+    """PixAICuda._forward (foidfinder/backends/cuda/engine.py:142-161) on the reference's int8 checkpoint `ck`
+    (convert_checkpoint's output, official names) through the reference's own kernels `k` (its
+    torch.ops.foidfinder namespace: gemm_s8, rot_q8_1024, rot_q8_h128, attention), from normalised fp16
+    pixels [B, S, S, 3] on a GPU -> logits [B, num_tags] f32. The stem and the pool head are the reference's
+    fp16 torch code (PixAITorch with dtype fp16: patchify + matmul + position, F.layer_norm ln_pre,
+    reference.py:103-107, :114-116, pool_head :133-140); buffers as _buffers (engine.py:96-106); `stages`
+    is the GEMM pipeline depth _autotune would pick (it changes speed, not results)."""
+    import torch.nn.functional as F
+
+    dev = pixels.device
+    B, G, P, C, nh, win = pixels.shape[0], cfg.grid, cfg.patch, cfg.dim, cfg.heads, cfg.window
+    L, nw, HID, eps = cfg.patches, G // win, cfg.mlp_hidden, cfg.ln_eps
+    T = B * L
+
+    def h16(t):
+        return t.to(dev, torch.float16).contiguous()
+
+    def f32(t):
+        return t.to(dev, torch.float32).contiguous()
+
+    perm = window_perm(G, win).to(dev)
+    patch_w = h16(ck["patch_embed.proj.weight"].permute(0, 2, 3, 1).reshape(C, -1))
+    pos = ck["pos_embed"][0, 1:]
+    pre = int(round(pos.shape[0] ** 0.5))
+    pos = h16(pos.reshape(pre, pre, C).repeat(G // pre, G // pre, 1).reshape(L, C).to(dev)[perm])
+    cw, sw = (f32(t) for t in axial_rope(win, 1.0))
+    cg, sg = axial_rope(G, win / G)
+    cg, sg = f32(cg.to(dev)[perm]), f32(sg.to(dev)[perm])
+    x = torch.empty(T, C, device=dev, dtype=torch.half)
+    a8 = torch.empty(T, C, device=dev, dtype=torch.int8)
+    rs = torch.empty(T, device=dev)
+    qkv = torch.empty(T, 3 * C, device=dev, dtype=torch.half)
+    o16 = torch.empty(T, C, device=dev, dtype=torch.half)
+    hh = torch.empty(T, HID, device=dev, dtype=torch.half)
+    h8 = torch.empty(T, HID, device=dev, dtype=torch.int8)
+    patches = pixels.to(torch.float16).view(B, nw, win, P, nw, win, P, 3).permute(0, 1, 4, 2, 5, 3, 6, 7)
+    torch.matmul(patches.reshape(T, P * P * 3), patch_w.t(), out=x)
+    x.view(B, L, C).add_(pos)
+    x.copy_(F.layer_norm(x, (C,), h16(ck["ln_pre.weight"]), h16(ck["ln_pre.bias"]), eps))
+
+    def lin(p):
+        return ck[p + ".qweight"].to(dev), f32(ck[p + ".wscale"]), f32(ck[p + ".bias"])
+
+    for i in range(cfg.depth):
+        b = f"blocks.{i}."
+        seq, (cos, sin) = (L, (cg, sg)) if cfg.is_global(i) else (win * win, (cw, sw))
+        k.rot_q8_1024(x, f32(ck[b + "norm1.weight"]), f32(ck[b + "norm1.bias"]), a8, rs)
+        w, s, bb = lin(b + "attn.qkv")
+        k.gemm_s8(a8, w, rs, s, bb, qkv, 0, stages, cos, sin, Q_SCALE_REF)
+        k.attention(qkv, o16, seq)
+        k.rot_q8_1024(o16, None, None, a8, rs)
+        w, s, bb = lin(b + "attn.proj")
+        k.gemm_s8(a8, w, rs, s, bb, x, 1, stages, None, None, Q_SCALE_REF)
+        k.rot_q8_1024(x, f32(ck[b + "norm2.weight"]), f32(ck[b + "norm2.bias"]), a8, rs)
+        w, s, bb = lin(b + "mlp.fc1")
+        k.gemm_s8(a8, w, rs, s, bb, hh, 2, stages, None, None, Q_SCALE_REF)
+        k.rot_q8_h128(hh, h8, rs)
+        w, s, bb = lin(b + "mlp.fc2")
+        k.gemm_s8(h8, w, rs, s, bb, x, 1, stages, None, None, Q_SCALE_REF)
+    xv = x.view(B, L, C)
+    h = F.layer_norm(xv, (C,), h16(ck["head_pool.norm.weight"]), h16(ck["head_pool.norm.bias"]), eps)
+    h = h + h16(ck["head_pool.pos_embed"].to(dev)[perm])
+    kk, vv = F.linear(h, h16(ck["head_pool.kv.weight"]), h16(ck["head_pool.kv.bias"])).view(
+        B, L, 2, nh, C // nh).permute(2, 0, 3, 1, 4)
+    q = h16(ck["head_pool.q"]).view(1, nh, 1, C // nh).expand(B, nh, 1, C // nh)
+    o = F.scaled_dot_product_attention(q, kk, vv).reshape(B, C)
+    o = F.linear(o, h16(ck["head_pool.proj.weight"]), h16(ck["head_pool.proj.bias"]))
+    return F.linear(o, h16(ck["head.weight"]), h16(ck["head.bias"])).float()

@@ -75,7 +75,7 @@ def rot_q8(
     if gamma is not None:
         v[:, :valid] = layer_norm(v[:, :valid], gamma[:valid], beta[:valid], eps)
     v[:, valid:] = 0.0
-    r = (v.double().view(T, cols // block, block) @ hadamard(block, torch.float64)).view(T, cols).float()
+    r = (v.double().view(T, cols // block, block) @ hadamard(block, torch.float64).to(v.device)).view(T, cols).float()
     amax = r.abs().amax(1)
     scale = amax.clamp_min(1e-12) / 127.0
     inv = (1.0 / scale).float()
@@ -93,7 +93,7 @@ def rot_q8_f32_fwht(x, gamma, beta, *, block, eps=1e-6, valid_cols=None):
     if gamma is not None:
         v[:, :valid] = layer_norm(v[:, :valid], gamma[:valid], beta[:valid], eps)
     v[:, valid:] = 0.0
-    r = (v.view(T, cols // block, block) @ hadamard(block, torch.float32)).view(T, cols)
+    r = (v.view(T, cols // block, block) @ hadamard(block, torch.float32).to(v.device)).view(T, cols)
     scale = r.abs().amax(1).clamp_min(1e-12) / 127.0
     q = torch.round(r * (1.0 / scale)[:, None]).clamp(-127, 127).to(torch.int8)
     return q, scale.float()
@@ -102,7 +102,7 @@ def rot_q8_f32_fwht(x, gamma, beta, *, block, eps=1e-6, valid_cols=None):
 def gemm_s8_acc(A: torch.Tensor, W: torch.Tensor) -> torch.Tensor:
     """Exact int32 accumulators of int8 A [M, K] x int8 W [N, K]^T (gemm.cuh:43-117)."""
     if A.shape[0] >= 17 and A.shape[1] % 8 == 0 and W.shape[0] % 8 == 0:
-        return torch._int_mm(A.contiguous(), W.t().contiguous())
+        return torch._int_mm(A.contiguous(), W.t().contiguous())  # exact on the CPU and on CUDA devices
     return (A.long() @ W.long().t()).to(torch.int32)
 
 
@@ -122,8 +122,9 @@ def apply_rope_pairs(y: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, pos:
     convention). cos/sin: [positions, 32]."""
     out = y.clone()
     part = y[:, :cols].reshape(y.shape[0], cols // 64, 32, 2)
-    c = cos[pos][:, None, :]
-    s = sin[pos][:, None, :]
+    pos = pos.to(y.device)
+    c = cos.to(y.device)[pos][:, None, :]
+    s = sin.to(y.device)[pos][:, None, :]
     x0, x1 = part[..., 0], part[..., 1]
     rot = torch.stack([x0 * c - x1 * s, x0 * s + x1 * c], dim=-1)
     out[:, :cols] = rot.reshape(y.shape[0], cols)

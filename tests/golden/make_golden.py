@@ -249,4 +249,9 @@ def pixai_pool_input() -> np.ndarray:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    import os
+
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FOIDFINDER_REFERENCE")
+    if not root:
+        sys.exit("usage: make_golden.py /path/to/foidfinder-reference (or set FOIDFINDER_REFERENCE)")
+    main(root)

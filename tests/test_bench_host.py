@@ -21,7 +21,10 @@ def test_metric_names():
 
 def test_workload_descriptions():
     w = bench.workload(CONFIGS["eva02-l-448"], 64, 2)
-    assert w["global_batch"] == 128 and "1025 tokens" in w["workload"] and w["parallelism"].startswith("dp2")
+    assert w["global_batch"] == 64 and w["batch_per_gpu"] == [32, 32]
+    assert "1025 tokens" in w["workload"] and w["parallelism"].startswith("dp2")
+    assert bench.workload(CONFIGS["eva02-l-448"], 64, 8)["batch_per_gpu"] == [8] * 8
+    assert bench.workload(CONFIGS["eva02-l-448"], 10, 4)["batch_per_gpu"] == [2, 3, 2, 3]
     w = bench.workload(CONFIGS["pixai-1008"], 16, 1)
     assert "5184 window-ordered tokens" in w["workload"] and "global blocks [7, 15, 23, 31]" in w["workload"]
 

@@ -114,29 +114,47 @@ def test_engine_rejects_bad_input(cuda_device):
     eng.close()
 
 
-def test_engine_full_size_b1_matches_oracle(cuda_device, no_device_error):
-    """BASELINE config 0 shape (EVA02-L/448, 24 blocks, 30,877 tags) at batch 1, free-running against
-    the oracle, with the tolerance calibrated by the oracle's own rounding sensitivity at this depth
-    (measured here: mean 0.043, max 0.25, 9 of 50 top tags swapped)."""
+def test_engine_full_size_matches_oracle(cuda_device, no_device_error):
+    """BASELINE config 0/3 shape (EVA02-L/448, 24 blocks, 30,877 tags), 16 seeded images, free-running
+    against the int8 oracle and the fp32 model (both run on the GPU as checkers). The bound is the oracle's
+    own rounding sensitivity at this depth (its Hadamard transform in f32 instead of f64) scaled by the
+    ratio the reference engine shows on its own model (tests/test_gpu_reference_engine.py: the reference's
+    kernels drift from the int8 oracle by REF_RATIO times the oracle's self-divergence at PixAI-1008)."""
     from oracle import quant as Q
 
     from foidfinder_b200.config import EVA02_L
     from foidfinder_b200.engine import Engine
     from foidfinder_b200.weights import convert, random_raw
 
-    cfg = EVA02_L
-    conv = convert(random_raw(cfg, seed=0, device="cuda"), cfg, "cpu")
-    imgs = _images(1, 448, 0)
-    ref = E.forward_int8(conv, cfg, imgs)
-    ref2 = E.forward_int8(conv, cfg, imgs, rot=Q.rot_q8_f32_fwht)
-    sd = (ref - ref2).abs()
+    REF_RATIO = 1.5
+    cfg, B, d = EVA02_L, 16, cuda_device
+    raw = random_raw(cfg, seed=0, device=d)
+    conv = convert(raw, cfg)
+    imgs = _images(B, 448, 0).to(d)
+    with torch.no_grad():
+        ref = E.forward_int8(conv, cfg, imgs)
+        ref2 = E.forward_int8(conv, cfg, imgs, rot=Q.rot_q8_f32_fwht)
+        fp32 = E.forward_fp32(raw, cfg, imgs)
     eng = Engine(cfg, conv, device=0)
     logits, idx, _ = eng.forward(imgs)
     torch.cuda.synchronize()
-    got = logits.cpu()
-    _free_running_bounds(got, ref, (sd.mean().item(), sd.max().item()))
-    self_overlap = len(set(torch.topk(ref[0], 50).indices.tolist()) & set(torch.topk(ref2[0], 50).indices.tolist()))
-    overlap = len(set(torch.topk(ref[0], 50).indices.tolist()) & set(idx[0].cpu().tolist()))
-    print(f"top-50 overlap with the oracle {overlap}/50 (oracle vs itself {self_overlap}/50)")
-    assert overlap >= min(self_overlap, 50) - 10
     eng.close()
+
+    def stats(a, b):
+        e = (a.float() - b.float()).abs()
+        ov = [len(set(x.topk(50).indices.tolist()) & set(y.topk(50).indices.tolist())) for x, y in zip(a, b)]
+        return e.mean().item(), e.max().item(), sum(ov) / len(ov), sum(o == 50 for o in ov)
+
+    rows = {"engine vs int8 oracle": stats(logits, ref), "oracle self (f32 FWHT)": stats(ref2, ref),
+            "engine vs fp32 model": stats(logits, fp32), "int8 oracle vs fp32 model": stats(ref, fp32)}
+    print(f"\nEVA02-L/448 free-running, {B} images:")
+    for k, (mean, mx, ov, ident) in rows.items():
+        print(f"  {k:28s} |dlogit| mean {mean:.4f} max {mx:.4f}  top-50 overlap {ov:.1f}/50, identical {ident}/{B}")
+    mean_s, max_s, ov_s, _ = rows["oracle self (f32 FWHT)"]
+    mean_e, max_e, ov_e, _ = rows["engine vs int8 oracle"]
+    assert mean_e <= REF_RATIO * mean_s + 2e-3 and max_e <= REF_RATIO * max_s + 2e-2
+    assert ov_e >= ov_s - REF_RATIO * (50 - ov_s) - 1
+    # against the fp32 model the engine is as close as the int8 oracle itself
+    assert rows["engine vs fp32 model"][0] <= 1.1 * rows["int8 oracle vs fp32 model"][0] + 2e-3
+    for b in range(B):  # the device top-k is the top-50 of the engine's own logits
+        assert set(idx[b].cpu().tolist()) == set(logits[b].cpu().topk(50).indices.tolist())

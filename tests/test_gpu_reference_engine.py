@@ -1,0 +1,98 @@
+"""Free-running parity of the whole forward against the reference's own engine.
+
+The reference's int8 engine (PixAICuda._forward, foidfinder/backends/cuda/engine.py:142-161) runs here
+through its own kernels, compiled from its sources by oracle/build_ref.py (`oracle.pixai.
+reference_engine_forward`), on the same seeded PixAI Tagger v1.0 weights (its `convert_checkpoint` codes,
+which this engine loads unchanged) and the same fp16 pixels. Both engines are compared with the fp32 model
+(oracle.pixai.forward_fp32, PixAITorch's arithmetic) and with the int8 oracle (oracle.pixai.forward_int8).
+
+With random N(0, 0.02) weights the int8 pipeline is chaotic at rounding ties: any change of rounding
+order (the oracle's own Hadamard transform in f32 instead of f64 is measured here as the yardstick) moves
+logits by a few 1e-2 and swaps tags near the rank-50 cut. No implementation — the reference's included —
+reproduces another's top-50 exactly under these weights, so the bar is relative: this engine must drift
+from the fp32 model and from the int8 oracle no more than the reference engine does on the same input.
+The checkers run on the GPU (the oracle's torch code on CUDA tensors, exact int32 GEMMs) to keep the
+full-size model (32 blocks, 5184 tokens) to seconds.
+"""
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+LIB = Path(__file__).resolve().parents[1] / "oracle" / "_ref" / "pixai_kernels.so"
+
+
+@pytest.fixture(scope="module")
+def ref(cuda_device):
+    if not LIB.is_file():
+        pytest.skip("reference kernels not built (python -m oracle.build_ref)")
+    torch.ops.load_library(str(LIB))
+    return torch.ops.foidfinder
+
+
+def _stats(a: torch.Tensor, b: torch.Tensor, k: int = 50) -> dict:
+    d = (a.float() - b.float()).abs()
+    pa, pb = torch.sigmoid(a.float()), torch.sigmoid(b.float())
+    overlap = [len(set(x.topk(k).indices.tolist()) & set(y.topk(k).indices.tolist())) for x, y in zip(a, b)]
+    return {"mean": d.mean().item(), "max": d.max().item(), "p_max": (pa - pb).abs().max().item(),
+            "p_mean": (pa - pb).abs().mean().item(), "top50": float(np.mean(overlap)), "top50_min": min(overlap),
+            "identical": sum(o == k for o in overlap)}
+
+
+def _show(name: str, s: dict) -> None:
+    print(f"  {name:34s} |dlogit| mean {s['mean']:.4f} max {s['max']:.4f}   |dp| mean {s['p_mean']:.2e} "
+          f"max {s['p_max']:.3f}   top-50 overlap {s['top50']:.1f} (min {s['top50_min']}, identical {s['identical']})")
+
+
+def _pixels(u8: torch.Tensor, cfg) -> torch.Tensor:
+    """The fp16 pixels this engine's uint8 path computes, ((u * f32(1/255) - mean) fused, * 1/std)."""
+    mean = torch.tensor(cfg.mean, dtype=torch.float32).double()
+    inv = (1.0 / torch.tensor(cfg.std, dtype=torch.float32)).double()
+    return ((u8.double() * float(np.float32(1.0 / 255.0)) - mean).float().double() * inv).float().half()
+
+
+def test_pixai_full_model_drift_vs_reference_engine(ref, cuda_device, no_device_error):
+    from foidfinder_b200.config import PIXAI_1008
+    from foidfinder_b200.engine import Engine
+    from foidfinder_b200.weights import convert_pixai, pixai_convert_checkpoint, pixai_random_raw
+    from oracle import pixai as P
+    from oracle import quant as Q
+
+    d, cfg, B = cuda_device, PIXAI_1008, 4
+    raw = pixai_random_raw(cfg, seed=0, device=d)
+    ck = pixai_convert_checkpoint(raw, cfg)  # the reference's converter runs on the GPU too (cli.py:149)
+    conv = convert_pixai(ck, cfg)
+    u8 = torch.randint(0, 256, (B, 1008, 1008, 3), generator=torch.Generator().manual_seed(31), dtype=torch.uint8)
+    px = _pixels(u8, cfg).to(d)
+    ref_logits = P.reference_engine_forward(ref, ck, cfg, px)
+    eng = Engine(cfg, conv, device=0)
+    ours = eng(px)
+    torch.cuda.synchronize()
+    eng.close()
+    with torch.no_grad():
+        fp32 = P.forward_fp32(raw, cfg, u8.to(d))
+        i8 = P.forward_int8(conv, cfg, u8.to(d))
+        i8b = P.forward_int8(conv, cfg, u8.to(d), rot=Q.rot_q8_f32_fwht)
+    torch.cuda.synchronize()
+    assert torch.isfinite(ours).all() and torch.isfinite(ref_logits).all()
+    s = {
+        "ours_fp32": _stats(ours, fp32), "ref_fp32": _stats(ref_logits, fp32),
+        "ours_int8": _stats(ours, i8), "ref_int8": _stats(ref_logits, i8),
+        "ours_ref": _stats(ours, ref_logits), "oracle_self": _stats(i8b, i8), "int8_fp32": _stats(i8, fp32),
+    }
+    print(f"\nPixAI-1008 free-running, {B} seeded images, 32 blocks:")
+    for name, label in (("ours_fp32", "this engine vs fp32 model"), ("ref_fp32", "reference engine vs fp32 model"),
+                        ("int8_fp32", "int8 oracle vs fp32 model"), ("ours_int8", "this engine vs int8 oracle"),
+                        ("ref_int8", "reference engine vs int8 oracle"), ("oracle_self", "int8 oracle, f32 FWHT vs f64"),
+                        ("ours_ref", "this engine vs reference engine")):
+        _show(label, s[name])
+    # no worse than the reference engine, against both oracles (statistical: 10% on the mean, 25% on the max)
+    for tgt in ("fp32", "int8"):
+        o, r = s[f"ours_{tgt}"], s[f"ref_{tgt}"]
+        assert o["mean"] <= 1.1 * r["mean"] + 2e-3, (tgt, o, r)
+        assert o["max"] <= 1.25 * r["max"] + 2e-2, (tgt, o, r)
+        assert o["top50"] >= r["top50"] - 1.0, (tgt, o, r)
