@@ -161,8 +161,12 @@ def test_pixai_backend_from_model_directories(cuda_device, no_device_error, tmp_
 
     cfg = PIXAI_1008.with_(name="px-dir", image_size=336, depth=2, window=8, global_blocks=(1,), num_tags=1000)
     raw = W.pixai_random_raw(cfg, seed=9)
+    # `foidfinder convert` converts on the GPU when there is one (cli.py:149), as the backend does with an
+    # fp32 directory: the same float32 matmul on the same device, hence the same codes
+    converted = {k: v.cpu() for k, v in W.pixai_convert_checkpoint({k: v.to(cuda_device) for k, v in raw.items()},
+                                                                  cfg).items()}
     for name, tensors, meta in (("official", raw, None),
-                                ("converted", W.pixai_convert_checkpoint(raw, cfg), {"format": W.PIXAI_INT8_FORMAT})):
+                                ("converted", converted, {"format": W.PIXAI_INT8_FORMAT})):
         d = tmp_path / name
         d.mkdir()
         save_file({k: v.contiguous() for k, v in tensors.items()}, str(d / "model.safetensors"), meta)
