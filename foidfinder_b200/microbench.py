@@ -3,7 +3,7 @@ stream after warm-up. Also the entry point for ncu captures of single kernels.
 
     python -m foidfinder_b200.microbench gemm [--batch 64] [--shape 1024x3072] [--iters 20]
                                               [--epilogue bias|swiglu|residual|qkv_rope]
-    python -m foidfinder_b200.microbench attention [--batch 64] [--seq 1025] [--rope] [--iters 20]
+    python -m foidfinder_b200.microbench attention [--batch 64] [--seq 1025] [--iters 20]
     python -m foidfinder_b200.microbench rotate [--batch 64] [--tokens 1025] [--cols 1024 ...] [--iters 20]
     python -m foidfinder_b200.microbench peak      (measured dense int8 tensor-core TOPS)
 
@@ -75,17 +75,14 @@ def bench_gemm(batch: int, shapes: list[str], iters: int, epi: str, tile: int = 
                           "bytes": M * K + N * K + out.numel() * 2, "gbs": (M * K + N * K + out.numel() * 2) / ms / 1e6}))
 
 
-def bench_attention(batch: int, iters: int, rope: bool, seq: int = TOKENS, heads: int = 16) -> None:
-    from .weights import rope_tables
-
+def bench_attention(batch: int, iters: int, seq: int = TOKENS, heads: int = 16) -> None:
     d = torch.device("cuda")
     g = torch.Generator(device=d).manual_seed(0)
     qkv = torch.randn(batch * seq, 3 * heads * 64, generator=g, device=d).half()
     out = torch.empty(batch * seq, heads * 64, device=d, dtype=torch.float16)
-    tables = tuple(t.to(d) for t in rope_tables(32, 16)) if rope and seq == TOKENS else None  # EVA02 tables only
-    ms = _time(lambda: ops.attention(qkv, out, seq, heads, rope=tables, scale=0.125), iters)
+    ms = _time(lambda: ops.attention(qkv, out, seq, heads, scale=0.125), iters)
     flops = 4 * batch * heads * seq * seq * 64
-    print(json.dumps({"kernel": "attention", "batch": batch, "tokens": seq, "heads": heads, "rope": tables is not None,
+    print(json.dumps({"kernel": "attention", "batch": batch, "tokens": seq, "heads": heads,
                       "ms": ms, "tflops": flops / ms / 1e9}))
 
 
@@ -121,7 +118,6 @@ def main() -> None:
     ap.add_argument("--shape", action="append", choices=sorted(GEMM_SHAPES))
     ap.add_argument("--epilogue", default="bias", choices=("bias", "swiglu", "residual", "qkv_rope"))
     ap.add_argument("--tile", type=int, default=0, help="gemm: tile_n (0 auto, 128, 256, 512 = pair tiles)")
-    ap.add_argument("--rope", action="store_true")
     ap.add_argument("--seq", type=int, default=TOKENS, help="attention: sequence length")
     ap.add_argument("--tokens", type=int, default=TOKENS, help="rotate: rows per image")
     ap.add_argument("--cols", type=int, action="append", choices=sorted(ROT_CASES), help="rotate: row widths")
@@ -132,7 +128,7 @@ def main() -> None:
     elif a.kernel == "gemm":
         bench_gemm(a.batch, a.shape or list(GEMM_SHAPES), a.iters, a.epilogue, a.tile)
     elif a.kernel == "attention":
-        bench_attention(a.batch, a.iters, a.rope, a.seq)
+        bench_attention(a.batch, a.iters, a.seq)
     else:
         bench_rotate(a.batch, a.iters, a.tokens, a.cols)
     torch.cuda.synchronize()

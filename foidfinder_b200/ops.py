@@ -150,7 +150,8 @@ def attention(
     rope: tuple[torch.Tensor, torch.Tensor] | None = None,
     scale: float = 1.0,
 ) -> None:
-    """qkv [S * seq_len, 3 * heads * 64] fp16 -> out [S * seq_len, heads * 64] fp16 (non-causal)."""
+    """qkv [S * seq_len, 3 * heads * 64] fp16 -> out [S * seq_len, heads * 64] fp16 (non-causal). `rope` must be
+    None: q and k arrive rotated, as in the reference (its QKV GEMM epilogue rotates them; here EPI_QKV_ROPE)."""
     _cuda(qkv, out)
     _need(qkv.dtype == torch.float16 and out.dtype == torch.float16, "attention: fp16 tensors expected")
     heads = heads or qkv.shape[1] // 192

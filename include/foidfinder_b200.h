@@ -133,8 +133,9 @@ int ff_linear_w8a8_noalloc(const uint16_t* x, const float* gamma, const float* b
  * Non-causal multi-head attention, head dim 64, fp16 in/out, f32 softmax and accumulation.
  *   qkv [num_seqs * seq_len, 3 * heads * 64] fp16 (q | k | v column sections, head h at columns h*64),
  *   out [num_seqs * seq_len, heads * 64] fp16. Any seq_len >= 1 (ragged tail tiles are masked).
- *   rope_cos / rope_sin: NULL when q and k are already rotated (the QKV epilogue does it), else
- *   [seq_len, 32] f32 tables applied to q and k on load. scale multiplies q·k (1 when folded into q).
+ *   rope_cos / rope_sin: must be NULL; q and k arrive rotated, as in the reference, whose QKV GEMM
+ *   epilogue applies the RoPE (here FF_EPI_QKV_ROPE). scale multiplies q·k (1 when folded into q).
+ *   Runs on the tcgen05 tensor cores (f16 MMAs, f32 accumulation in TMEM).
  * Replaces torch.ops.foidfinder.attention (foidfinder/backends/cuda/csrc/kernels.cu:255-265).
  */
 int ff_attention(const uint16_t* qkv, uint16_t* out, int num_seqs, int seq_len, int heads, const float* rope_cos,

@@ -94,7 +94,8 @@ def test_rot_q8_zero_rows_is_a_no_op():
 
 
 @pytest.mark.parametrize("seqs,seq_len,heads,rope,msg", [(1, 0, 16, None, "bad shape"), (1, 1025, 65, None, "bad shape"),
-                                                     (1, 1025, 16, (FAKE, None), "both RoPE tables")])
+                                                     (1, 1025, 16, (FAKE, None), "RoPE tables must be NULL"),
+                                                     (1, 1025, 16, (FAKE, FAKE), "RoPE tables must be NULL")])
 def test_attention_host_checks(seqs, seq_len, heads, rope, msg):
     cos, sin = rope or (None, None)
     rc = _lib.lib().ff_attention(FAKE, FAKE, seqs, seq_len, heads, cos, sin, 1.0, None)

@@ -127,11 +127,30 @@ def test_attention_matches_oracle(cuda_device, no_device_error, seqs, T, heads, 
         cos, sin = E.rope_tables(grid, 16)
         tables = (cos[:T], sin[:T])
     ref = _ref_attention(qkv, seqs, T, heads, scale, tables)
+    if rope:  # q and k arrive rotated, as the QKV GEMM epilogue leaves them
+        x = qkv.float().view(seqs, T, 3, heads, 32, 2)
+        cos, sin = (t[:, None, :] for t in tables)
+        for s in (0, 1):
+            x0, x1 = x[:, :, s, ..., 0].clone(), x[:, :, s, ..., 1].clone()
+            x[:, :, s, ..., 0], x[:, :, s, ..., 1] = x0 * cos - x1 * sin, x0 * sin + x1 * cos
+        qkv = x.reshape(seqs * T, -1).half()
     d = cuda_device
     out = torch.full((seqs * T, heads * 64), float("nan"), dtype=torch.float16, device=d)
-    ops.attention(qkv.to(d), out, T, heads, rope=(tables[0].to(d), tables[1].to(d)) if rope else None, scale=scale)
+    ops.attention(qkv.to(d), out, T, heads, scale=scale)
     torch.cuda.synchronize()
     torch.testing.assert_close(out.float().cpu(), ref, atol=4e-3, rtol=1e-2)
+
+
+def test_attention_rejects_rope_tables(cuda_device):
+    """RoPE belongs to the QKV GEMM epilogue (as in the reference); the attention op refuses tables."""
+    from foidfinder_b200 import ops
+
+    d = cuda_device
+    qkv = torch.zeros(128, 3 * 64, dtype=torch.float16, device=d)
+    out = torch.zeros(128, 64, dtype=torch.float16, device=d)
+    cos = torch.ones(128, 32, device=d)
+    with pytest.raises(RuntimeError, match="RoPE tables must be NULL"):
+        ops.attention(qkv, out, 128, 1, rope=(cos, cos))
 
 
 def test_layernorm_patchify_fill_cls(cuda_device, no_device_error):
