@@ -372,6 +372,8 @@ __global__ void __launch_bounds__(TAILW ? fa::THREADS_TAIL : fa::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -714,11 +716,11 @@ int attention_tc(const void* qkv, void* out, int num_seqs, int seq_len, int head
   // Tail rows (EVA02's 1025th) run on two extra warps of the same launch; without them the kernel keeps
   // 320 threads (the extra warps, idle, measured 2.6% slower on 1024-token sequences).
   if (t_main < seq_len)
-    attention_tc_kernel<true><<<grid, THREADS_TAIL, SMEM, s>>>(map, static_cast<const __half*>(qkv),
+    launch(attention_tc_kernel<true>, dim3(grid), dim3(THREADS_TAIL), SMEM, s, map, static_cast<const __half*>(qkv),
                                                                static_cast<__half*>(out), seq_len, t_main, heads,
                                                                num_seqs, scale_log2, err);
   else
-    attention_tc_kernel<false><<<grid, THREADS, SMEM, s>>>(map, static_cast<const __half*>(qkv),
+    launch(attention_tc_kernel<false>, dim3(grid), dim3(THREADS), SMEM, s, map, static_cast<const __half*>(qkv),
                                                            static_cast<__half*>(out), seq_len, t_main, heads,
                                                            num_seqs, scale_log2, err);
   return check_launch("attention_tc_kernel");

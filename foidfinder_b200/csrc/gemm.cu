@@ -22,7 +22,7 @@ int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& 
   }
   const int tiles = a.tiles_m * (a.N / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kernel<<<grid, C::THREADS, C::SMEM, stream>>>(ta, tb, tc, a);
+  launch(kernel, dim3(grid), dim3(C::THREADS), C::SMEM, stream, ta, tb, tc, a);
   return check_launch("gemm_tc_kernel");
 }
 
@@ -38,11 +38,13 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   int dev = 0;
   cudaGetDevice(&dev);
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // as ff::launch (common.h)
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.blockDim = dim3(C::THREADS);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = stream;
@@ -59,6 +61,7 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   }
   const int tiles = a.tiles_m * (a.N / 256);
   cfg.gridDim = dim3(2 * (tiles < clusters ? tiles : clusters));
+  cfg.numAttrs = 2;
   if (cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, a) != cudaSuccess) return check_launch("gemm_tc_kernel (pair)");
   return check_launch("gemm_tc_kernel (pair)");
 }

@@ -19,6 +19,8 @@ __device__ __forceinline__ float pixel_value(__half h, float, float) { return __
 template <typename Px>
 __global__ void patchify_kernel(const Px* __restrict__ img, int B, int S, int p, float m0, float m1, float m2,
                                 float is0, float is1, float is2, __half* __restrict__ out, int k_pad, int win) {
+  pdl_wait();
+  pdl_trigger();
   const int G = S / p, P = G * G, kreal = p * p * 3;
   const int nw = win > 0 ? G / win : 1;
   const int64_t total = static_cast<int64_t>(B) * P * k_pad;
@@ -48,6 +50,8 @@ __global__ void patchify_kernel(const Px* __restrict__ img, int B, int S, int p,
 }
 
 __global__ void fill_cls_kernel(const __half* __restrict__ cls, __half* __restrict__ x, int B, int tokens, int dim) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x;
   for (int c = threadIdx.x; c < dim; c += blockDim.x) x[static_cast<size_t>(b) * tokens * dim + c] = cls[c];
 }
@@ -58,6 +62,8 @@ __global__ void fill_cls_kernel(const __half* __restrict__ cls, __half* __restri
 __global__ void layernorm_kernel(const __half* __restrict__ x, int64_t stride, const float* __restrict__ g,
                                  const float* __restrict__ b, float eps, int rows, int cols, __half* __restrict__ out,
                                  const __half* __restrict__ pos, int period) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -97,6 +103,8 @@ __device__ __forceinline__ uint32_t order_key(float f) {
 template <bool STAGED>
 __global__ void __launch_bounds__(kTopkThreads) topk_kernel(const float* __restrict__ logits, int n, int k,
                                                             int32_t* __restrict__ idx_out, float* __restrict__ val_out) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ uint32_t keys_smem[];  // [n] when STAGED
   __shared__ uint32_t hist[256];
   __shared__ uint32_t s_prefix, s_remaining;
@@ -202,7 +210,7 @@ int topk(const float* logits, int B, int n, int k, int32_t* idx, float* val, cud
   const size_t smem = static_cast<size_t>(n) * sizeof(uint32_t);
   if (B == 0) return FF_OK;
   if (smem > 200 * 1024) {
-    topk_kernel<false><<<B, kTopkThreads, 0, s>>>(logits, n, k, idx, val);
+    launch(topk_kernel<false>, dim3(B), dim3(kTopkThreads), 0, s, logits, n, k, idx, val);
     return check_launch("topk_kernel");
   }
   static bool configured[64] = {};
@@ -213,7 +221,7 @@ int topk(const float* logits, int B, int n, int k, int32_t* idx, float* val, cud
       return check_launch("ff_topk: cudaFuncSetAttribute");
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  topk_kernel<true><<<B, kTopkThreads, smem, s>>>(logits, n, k, idx, val);
+  launch(topk_kernel<true>, dim3(B), dim3(kTopkThreads), smem, s, logits, n, k, idx, val);
   return check_launch("topk_kernel");
 }
 
@@ -227,10 +235,10 @@ int patchify(const void* img, int B, int S, int p, const float* mean, const floa
   const int64_t total = static_cast<int64_t>(B) * (S / p) * (S / p) * k_pad;
   const int grid = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 16));
   if (f16_pixels)
-    patchify_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(img), B, S, p, 0.f, 0.f, 0.f, 1.f, 1.f,
+    launch(patchify_kernel<__half>, dim3(grid), dim3(256), 0, s, static_cast<const __half*>(img), B, S, p, 0.f, 0.f, 0.f, 1.f, 1.f,
                                                  1.f, static_cast<__half*>(out), k_pad, win);
   else
-    patchify_kernel<uint8_t><<<grid, 256, 0, s>>>(static_cast<const uint8_t*>(img), B, S, p, mean[0], mean[1],
+    launch(patchify_kernel<uint8_t>, dim3(grid), dim3(256), 0, s, static_cast<const uint8_t*>(img), B, S, p, mean[0], mean[1],
                                                   mean[2], 1.f / stdv[0], 1.f / stdv[1], 1.f / stdv[2],
                                                   static_cast<__half*>(out), k_pad, win);
   return check_launch("patchify_kernel");
@@ -239,7 +247,7 @@ int patchify(const void* img, int B, int S, int p, const float* mean, const floa
 int fill_cls(const void* cls, void* x, int B, int tokens, int dim, cudaStream_t s) {
   FF_REQUIRE(cls && x && tokens >= 1 && dim >= 1, "ff_fill_cls: bad arguments");
   if (B == 0) return FF_OK;
-  fill_cls_kernel<<<B, 256, 0, s>>>(static_cast<const __half*>(cls), static_cast<__half*>(x), B, tokens, dim);
+  launch(fill_cls_kernel, dim3(B), dim3(256), 0, s, static_cast<const __half*>(cls), static_cast<__half*>(x), B, tokens, dim);
   return check_launch("fill_cls_kernel");
 }
 
@@ -248,7 +256,7 @@ int layernorm(const void* x, int64_t stride, const float* g, const float* b, flo
   FF_REQUIRE(x && g && b && out && cols >= 1 && stride >= cols, "ff_layernorm: bad arguments");
   FF_REQUIRE(pos == nullptr || period >= 1, "ff_layernorm: position rows need a period");
   if (rows == 0) return FF_OK;
-  layernorm_kernel<<<(rows + 7) / 8, 256, 0, s>>>(static_cast<const __half*>(x), stride, g, b, eps, rows, cols,
+  launch(layernorm_kernel, dim3((rows + 7) / 8), dim3(256), 0, s, static_cast<const __half*>(x), stride, g, b, eps, rows, cols,
                                                   static_cast<__half*>(out), static_cast<const __half*>(pos), period);
   return check_launch("layernorm_kernel");
 }

@@ -33,6 +33,8 @@ __global__ void __launch_bounds__(kChunk) slot_attend_kernel(const float* __rest
                                                              const float* __restrict__ bias,
                                                              const __half* __restrict__ kv, int tokens, int dim,
                                                              float* __restrict__ z, float* __restrict__ mass_part) {
+  pdl_wait();
+  pdl_trigger();
   static_assert(HD % 8 == 0 && M <= kMaxQ, "head dim must be a multiple of 8");
   constexpr int D4 = HD / 4;
   // v_s [kChunk][HD] | attn_s [M][kChunk] | q_s [M][HD] | red_s [kChunk / 32][M], all f32
@@ -178,6 +180,8 @@ __global__ void __launch_bounds__(256) pool_trunk_kernel(const float* __restrict
                                                          const float* __restrict__ child_w,
                                                          const float* __restrict__ child_b, float eps,
                                                          float* __restrict__ z_coarse, float* __restrict__ q_leaf) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ float sm[];
   float* row = sm;         // [dim]
   float* zc = sm + dim;    // [dim]
@@ -219,6 +223,8 @@ __global__ void __launch_bounds__(256) pool_leaf_kernel(const float* __restrict_
                                                         const float* __restrict__ leaf_w,
                                                         const float* __restrict__ leaf_b, __half* __restrict__ out,
                                                         int ld_out) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ float sm[];
   float* row = sm;        // [dim]
   float* red = sm + dim;  // [32]
@@ -269,7 +275,7 @@ int slot_launch(const float* q, int64_t q_stride, const float* bias, const __hal
       return check_launch("slot_attend_kernel: cudaFuncSetAttribute");
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  slot_attend_kernel<HD, M><<<dim3(heads, B), kChunk, smem, s>>>(q, q_stride, bias, kv, tokens, dim, z, mass);
+  launch(slot_attend_kernel<HD, M>, dim3(dim3(heads, B)), dim3(kChunk), smem, s, q, q_stride, bias, kv, tokens, dim, z, mass);
   return check_launch("slot_attend_kernel");
 }
 
@@ -280,6 +286,8 @@ int slot_launch(const float* q, int64_t q_stride, const float* bias, const __hal
 constexpr int kPqThreads = 320;
 __global__ void __launch_bounds__(kPqThreads) pool_query_kernel(const float* __restrict__ q, const __half* __restrict__ kv,
                                                                int tokens, int dim, __half* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int HD = 64, NQ = kPqThreads / 8, UNR = 4;
   __shared__ float part_m[NQ], part_l[NQ];
   __shared__ float part_o[NQ][HD];
@@ -382,7 +390,7 @@ int pool_query_attention(const float* q, const void* kv, int B, int tokens, int 
   FF_REQUIRE(q && kv && out && heads >= 1 && tokens >= 1, "pool query: bad arguments");
   FF_REQUIRE(aligned16(kv), "pool query: key/value must be 16-byte aligned");
   if (B == 0) return FF_OK;
-  pool_query_kernel<<<dim3(heads, B), kPqThreads, 0, s>>>(q, static_cast<const __half*>(kv), tokens, heads * 64,
+  launch(pool_query_kernel, dim3(dim3(heads, B)), dim3(kPqThreads), 0, s, q, static_cast<const __half*>(kv), tokens, heads * 64,
                                                           static_cast<__half*>(out));
   return check_launch("pool_query_kernel");
 }
@@ -392,7 +400,7 @@ int pool_trunk(const float* z, int B, int coarse, int leaves, int dim, const flo
                float* q_leaf, cudaStream_t s) {
   FF_REQUIRE(coarse >= 1 && leaves % coarse == 0 && dim >= 1, "pool: %d leaves over %d coarse queries", leaves, coarse);
   if (B == 0) return FF_OK;
-  pool_trunk_kernel<<<B, 256, (2 * dim + 32) * sizeof(float), s>>>(z, coarse, leaves, dim, trunk_w, trunk_b, q_child,
+  launch(pool_trunk_kernel, dim3(B), dim3(256), (2 * dim + 32) * sizeof(float), s, z, coarse, leaves, dim, trunk_w, trunk_b, q_child,
                                                                     child_w, child_b, eps, z_coarse, q_leaf);
   return check_launch("pool_trunk_kernel");
 }
@@ -403,8 +411,7 @@ int pool_leaf(const float* z_coarse, const float* z_child, const float* mass_par
   FF_REQUIRE(leaf_dim >= 1 && leaf_dim <= 256 && 256 % leaf_dim == 0, "pool: leaf dim %d must divide 256", leaf_dim);
   FF_REQUIRE(ld_out >= leaves * leaf_dim, "pool: head input stride %d", ld_out);
   if (B == 0) return FF_OK;
-  pool_leaf_kernel<<<dim3(leaves, B), 256, (dim + 32 + 256) * sizeof(float), s>>>(
-      z_coarse, z_child, mass_part, coarse, leaves, heads, dim, leaf_dim, leaf_nw, leaf_nb, eps, leaf_w, leaf_b,
+  launch(pool_leaf_kernel, dim3(dim3(leaves, B)), dim3(256), (dim + 32 + 256) * sizeof(float), s, z_coarse, z_child, mass_part, coarse, leaves, heads, dim, leaf_dim, leaf_nw, leaf_nb, eps, leaf_w, leaf_b,
       static_cast<__half*>(out), ld_out);
   return check_launch("pool_leaf_kernel");
 }

@@ -17,6 +17,7 @@
 #include <vector>
 
 #include "common.h"
+#include "ptx.cuh"
 
 namespace ff {
 namespace {
@@ -86,6 +87,8 @@ template <int AXIS>
 __global__ void resample_kernel(const uint8_t* __restrict__ src, int src_w, int row0, const int32_t* __restrict__ kk,
                                 const int32_t* __restrict__ bounds, int ksize, int out_w, int out_h, int top, int left,
                                 int h, int w, int fill, uint8_t* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y;
   if (x >= out_w || y >= out_h) return;
   const int yy = y - top, xx = x - left;
@@ -185,14 +188,14 @@ extern "C" int ff_resize_pad(const uint8_t* src, int h, int w, int new_h, int ne
   const int top = (size - new_h) / 2, left = (size - new_w) / 2;
   constexpr int TX = 128;
   if (p.vertical_first) {
-    resample_kernel<1><<<dim3((w + TX - 1) / TX, new_h), TX, 0, s>>>(src, w, 0, kv, bv, p.cv.ksize, w, new_h, 0, 0,
+    launch(resample_kernel<1>, dim3(dim3((w + TX - 1) / TX, new_h)), dim3(TX), 0, s, src, w, 0, kv, bv, p.cv.ksize, w, new_h, 0, 0,
                                                                     new_h, w, fill, tmp);
-    resample_kernel<0><<<dim3((size + TX - 1) / TX, size), TX, 0, s>>>(tmp, w, 0, kh, bh, p.ch.ksize, size, size, top,
+    launch(resample_kernel<0>, dim3(dim3((size + TX - 1) / TX, size)), dim3(TX), 0, s, tmp, w, 0, kh, bh, p.ch.ksize, size, size, top,
                                                                       left, new_h, new_w, fill, dst);
   } else {
-    resample_kernel<0><<<dim3((new_w + TX - 1) / TX, p.rows), TX, 0, s>>>(src, w, p.row0, kh, bh, p.ch.ksize, new_w,
+    launch(resample_kernel<0>, dim3(dim3((new_w + TX - 1) / TX, p.rows)), dim3(TX), 0, s, src, w, p.row0, kh, bh, p.ch.ksize, new_w,
                                                                          p.rows, 0, 0, p.rows, new_w, fill, tmp);
-    resample_kernel<1><<<dim3((size + TX - 1) / TX, size), TX, 0, s>>>(tmp, new_w, 0, kv, bv, p.cv.ksize, size, size,
+    launch(resample_kernel<1>, dim3(dim3((size + TX - 1) / TX, size)), dim3(TX), 0, s, tmp, new_w, 0, kv, bv, p.cv.ksize, size, size,
                                                                       top, left, new_h, new_w, fill, dst);
   }
   return check_launch("resample_kernel");
@@ -251,6 +254,8 @@ __device__ inline float aa_weight(const AaAxis& a, int i, int j, int first, floa
 
 __global__ void letterbox_aa_f16_kernel(const uint8_t* __restrict__ src, int h, int w, int new_h, int new_w, int size,
                                         int top, int left, __half* __restrict__ dst) {
+  pdl_wait();
+  pdl_trigger();
   const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y;
   if (x >= size || y >= size) return;
   const int yy = y - top, xx = x - left;
@@ -291,7 +296,7 @@ extern "C" int ff_letterbox_aa_f16(const uint8_t* src, int h, int w, int new_h, 
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int top = (size - new_h) / 2, left = (size - new_w) / 2;
   constexpr int TX = 128;
-  letterbox_aa_f16_kernel<<<dim3((size + TX - 1) / TX, size), TX, 0, s>>>(src, h, w, new_h, new_w, size, top, left,
+  launch(letterbox_aa_f16_kernel, dim3(dim3((size + TX - 1) / TX, size)), dim3(TX), 0, s, src, h, w, new_h, new_w, size, top, left,
                                                                          reinterpret_cast<__half*>(dst));
   return check_launch("letterbox_aa_f16_kernel");
 }

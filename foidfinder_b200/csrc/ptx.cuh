@@ -36,6 +36,16 @@ __device__ __forceinline__ unsigned long long globaltimer() {
   return t;
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Every kernel of this library is launched with programmatic stream serialization (ff::launch), so it may
+// begin while the previous kernel in the stream is still finishing. pdl_wait() blocks until the grids it
+// depends on have completed and their writes are visible (a no-op for a launch without that dependency):
+// every kernel calls it before it touches global memory, so only its prologue (barrier set-up, TMEM
+// allocation, descriptor prefetch) overlaps the previous kernel's tail. pdl_trigger() lets the next launch
+// in the stream start its own prologue on the SMs this grid leaves free.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");

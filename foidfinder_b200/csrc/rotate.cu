@@ -244,6 +244,8 @@ __global__ void __launch_bounds__(kRotWarps * 32)
   __shared__ __align__(16) float smem[kRotWarps][S::SW];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int row = blockIdx.x * kRotWarps + wid;
+  pdl_wait();
+  pdl_trigger();
   if (row >= rows) return;
   rot_row<NCH, BLOCK, NORM, false>(x + static_cast<size_t>(row) * S::COLS, eps, row, valid_cols, out, row_scale,
                                    smem[wid], lane,
@@ -303,6 +305,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();
+  pdl_trigger();
   uint32_t tmem = 0;
   if constexpr (NORM) {
     tmem = tmem_slot + (static_cast<uint32_t>(32 * (wid & 3)) << 16);
@@ -407,7 +411,7 @@ int launch_persistent(const __half* x, const float* g, const float* b, float eps
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
   const int ctas = std::min(sm_count(), (rows + WARPS - 1) / WARPS);
-  kernel<<<ctas, WARPS * 32, smem, s>>>(x, g, b, eps, rows, valid, out, rs, err);
+  launch(kernel, dim3(ctas), dim3(WARPS * 32), smem, s, x, g, b, eps, rows, valid, out, rs, err);
   return check_launch("rot_q8_persistent_kernel");
 }
 
@@ -424,9 +428,9 @@ int launch_rot(const __half* x, const float* g, const float* b, float eps, int r
   }
   const dim3 grid((rows + kRotWarps - 1) / kRotWarps);
   if (g != nullptr)
-    rot_q8_kernel<NCH, BLOCK, true><<<grid, kRotWarps * 32, 0, s>>>(x, g, b, eps, rows, valid, out, rs);
+    launch(rot_q8_kernel<NCH, BLOCK, true>, dim3(grid), dim3(kRotWarps * 32), 0, s, x, g, b, eps, rows, valid, out, rs);
   else
-    rot_q8_kernel<NCH, BLOCK, false><<<grid, kRotWarps * 32, 0, s>>>(x, g, b, eps, rows, valid, out, rs);
+    launch(rot_q8_kernel<NCH, BLOCK, false>, dim3(grid), dim3(kRotWarps * 32), 0, s, x, g, b, eps, rows, valid, out, rs);
   return check_launch("rot_q8_kernel");
 }
 
@@ -498,6 +502,8 @@ __global__ void __launch_bounds__((WPR >= 8 ? 1 : 8 / WPR) * WPR * 32)
   __shared__ __align__(16) float tbuf[ROWS * WPR][SW];
   __shared__ float part[ROWS][WPR];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  pdl_wait();
+  pdl_trigger();
   const int rloc = wid / WPR, wpart = wid % WPR;
   const int row = blockIdx.x * ROWS + rloc;
   const bool live = row < rows;  // dead warps still reach the barrier below
@@ -634,7 +640,7 @@ constexpr int kSplitMaxWarps = 8;       // warps per row: rows up to 8 x kSplitC
 template <int WPR>
 int launch_split(const __half* x, int rows, int cols, int8_t* out, float* rs, cudaStream_t s) {
   constexpr int ROWS = WPR >= 8 ? 1 : 8 / WPR;
-  rot_q8_h128_split_kernel<kSplitCpw, WPR><<<(rows + ROWS - 1) / ROWS, ROWS * WPR * 32, 0, s>>>(x, rows, cols, out, rs);
+  launch(rot_q8_h128_split_kernel<kSplitCpw, WPR>, dim3((rows + ROWS - 1) / ROWS), dim3(ROWS * WPR * 32), 0, s, x, rows, cols, out, rs);
   return check_launch("rot_q8_h128_split_kernel");
 }
 
