@@ -61,33 +61,37 @@ def _rope_qk(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, T: int, di
 
 def forward_fp32(raw: dict[str, torch.Tensor], cfg, images: torch.Tensor) -> torch.Tensor:
     """fp32 EVA02 forward on the folded (unquantised) weights -> logits [B, num_tags], on
-    the images' device."""
+    the images' device. Written with the fused torch ops the reference's PyTorch forward uses
+    (F.layer_norm, F.linear, F.scaled_dot_product_attention; reference.py:114-131), so that timing it on the
+    CPU measures what the reference's own CPU path costs."""
+    import torch.nn.functional as F
+
     B, T, D, H = images.shape[0], cfg.tokens, cfg.dim, cfg.heads
     eps = cfg.ln_eps
-    raw = {k: v.to(images.device) for k, v in raw.items()}
-    x = patchify(images, cfg.patch, cfg.mean, cfg.std) @ raw["patch_w"].float().t() + raw["patch_b"].float()
-    x = x + raw["pos_embed"][1:].float()
-    cls = (raw["cls_token"].float() + raw["pos_embed"][0].float()).expand(B, 1, D)
+    raw = {k: v.to(images.device).float() for k, v in raw.items()}
+    x = F.linear(patchify(images, cfg.patch, cfg.mean, cfg.std), raw["patch_w"], raw["patch_b"])
+    x = x + raw["pos_embed"][1:]
+    cls = (raw["cls_token"] + raw["pos_embed"][0]).expand(B, 1, D)
     x = torch.cat([cls, x], dim=1).reshape(B * T, D)
     cos, sin = rope_tables(cfg.grid, cfg.rope_ref_grid, cfg.head_dim)
     for i in range(cfg.depth):
         p = f"blocks.{i}."
-        h = Q.layer_norm(x, raw[p + "norm1.weight"], raw[p + "norm1.bias"], eps)
-        qkv = h @ raw[p + "qkv.weight"].float().t() + raw[p + "qkv.bias"].float()
-        qkv = _rope_qk(qkv, cos, sin, T, D)
-        o = _attention(qkv, B, T, H)
-        x = x + o @ raw[p + "proj.weight"].float().t() + raw[p + "proj.bias"].float()
-        h = Q.layer_norm(x, raw[p + "norm2.weight"], raw[p + "norm2.bias"], eps)
-        gu = h @ raw[p + "fc1.weight"].float().t() + raw[p + "fc1.bias"].float()
-        hid = Q.silu_mul(gu[:, : cfg.mlp_hidden], gu[:, cfg.mlp_hidden :])
-        hid = Q.layer_norm(hid, raw[p + "mlp_norm.weight"], raw[p + "mlp_norm.bias"], eps)
-        x = x + hid @ raw[p + "fc2.weight"].float().t() + raw[p + "fc2.bias"].float()
+        h = F.layer_norm(x, (D,), raw[p + "norm1.weight"], raw[p + "norm1.bias"], eps)
+        qkv = _rope_qk(F.linear(h, raw[p + "qkv.weight"], raw[p + "qkv.bias"]), cos, sin, T, D)
+        q, k, v = qkv.view(B, T, 3, H, D // H).permute(2, 0, 3, 1, 4)
+        o = F.scaled_dot_product_attention(q, k, v, scale=1.0).transpose(1, 2).reshape(B * T, D)
+        x = x + F.linear(o, raw[p + "proj.weight"], raw[p + "proj.bias"])
+        h = F.layer_norm(x, (D,), raw[p + "norm2.weight"], raw[p + "norm2.bias"], eps)
+        gu = F.linear(h, raw[p + "fc1.weight"], raw[p + "fc1.bias"])
+        hid = F.silu(gu[:, : cfg.mlp_hidden]) * gu[:, cfg.mlp_hidden :]
+        hid = F.layer_norm(hid, (cfg.mlp_hidden,), raw[p + "mlp_norm.weight"], raw[p + "mlp_norm.bias"], eps)
+        x = x + F.linear(hid, raw[p + "fc2.weight"], raw[p + "fc2.bias"])
     if cfg.head == "tree":
-        xf = Q.layer_norm(x, raw["norm.weight"], raw["norm.bias"], eps).view(B, T, D)
+        xf = F.layer_norm(x, (D,), raw["norm.weight"], raw["norm.bias"], eps).view(B, T, D)
         feat = tree_pool(xf, raw, cfg, half=False)
     else:
-        feat = Q.layer_norm(x.view(B, T, D)[:, 0], raw["norm.weight"], raw["norm.bias"], eps)
-    return feat @ raw["head.weight"].float().t() + raw["head.bias"].float()
+        feat = F.layer_norm(x.view(B, T, D)[:, 0], (D,), raw["norm.weight"], raw["norm.bias"], eps)
+    return F.linear(feat, raw["head.weight"], raw["head.bias"])
 
 
 def tree_pool(x: torch.Tensor, w: dict, cfg, half: bool, eps: float | None = None) -> torch.Tensor:

@@ -110,8 +110,9 @@ def _sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float) -> to
 
 def forward_fp32(raw: dict[str, torch.Tensor], cfg, images: torch.Tensor) -> torch.Tensor:
     """PixAITorch.forward (reference.py:109-130) and pool_head (:132-140) in f32 on the official checkpoint
-    layout, from uint8 images -> logits [B, num_tags]. Erf GELU (F.gelu's default, reference.py:129)."""
-    from . import quant as Q
+    layout, from uint8 images -> logits [B, num_tags], with the same torch calls (F.layer_norm, F.linear,
+    F.scaled_dot_product_attention, erf F.gelu), so that its CPU time is the reference's."""
+    import torch.nn.functional as F
 
     B, G, D, nh, L, win = images.shape[0], cfg.grid, cfg.dim, cfg.heads, cfg.patches, cfg.window
     nw, eps, dev = G // win, cfg.ln_eps, images.device
@@ -122,36 +123,36 @@ def forward_fp32(raw: dict[str, torch.Tensor], cfg, images: torch.Tensor) -> tor
     pre = int(round(pos.shape[0] ** 0.5))
     pos = pos.reshape(pre, pre, D).repeat(G // pre, G // pre, 1).reshape(L, D)[perm]
     x = (patch_rows(images, cfg) @ pw.t() + pos).reshape(B * L, D)
-    x = Q.layer_norm(x, g("ln_pre.weight"), g("ln_pre.bias"), eps)
+    x = F.layer_norm(x, (D,), g("ln_pre.weight"), g("ln_pre.bias"), eps)
     cw, sw, cg, sg = (t.to(dev) for t in _window_tables(cfg))
     for i in range(cfg.depth):
         p = f"blocks.{i}."
-        h = Q.layer_norm(x, g(p + "norm1.weight"), g(p + "norm1.bias"), eps)
-        qkv = h @ g(p + "attn.qkv.weight").t() + g(p + "attn.qkv.bias")
+        h = F.layer_norm(x, (D,), g(p + "norm1.weight"), g(p + "norm1.bias"), eps)
+        qkv = F.linear(h, g(p + "attn.qkv.weight"), g(p + "attn.qkv.bias"))
         nb, n, cos, sin = (B, L, cg, sg) if cfg.is_global(i) else (B * nw * nw, win * win, cw, sw)
         q, k, v = qkv.view(nb, n, 3, nh, D // nh).permute(2, 0, 3, 1, 4)
-        o = _sdpa(apply_rope(q, cos, sin), apply_rope(k, cos, sin), v, (D // nh) ** -0.5)
-        x = x + o.transpose(1, 2).reshape(B * L, D) @ g(p + "attn.proj.weight").t() + g(p + "attn.proj.bias")
-        h = Q.layer_norm(x, g(p + "norm2.weight"), g(p + "norm2.bias"), eps)
-        h = torch.nn.functional.gelu(h @ g(p + "mlp.fc1.weight").t() + g(p + "mlp.fc1.bias"))
-        x = x + h @ g(p + "mlp.fc2.weight").t() + g(p + "mlp.fc2.bias")
+        o = F.scaled_dot_product_attention(apply_rope(q, cos, sin), apply_rope(k, cos, sin), v)
+        x = x + F.linear(o.transpose(1, 2).reshape(B * L, D), g(p + "attn.proj.weight"), g(p + "attn.proj.bias"))
+        h = F.layer_norm(x, (D,), g(p + "norm2.weight"), g(p + "norm2.bias"), eps)
+        h = F.gelu(F.linear(h, g(p + "mlp.fc1.weight"), g(p + "mlp.fc1.bias")))
+        x = x + F.linear(h, g(p + "mlp.fc2.weight"), g(p + "mlp.fc2.bias"))
     return pool_head_fp32(x.view(B, L, D), raw, cfg)
 
 
 def pool_head_fp32(x: torch.Tensor, raw: dict[str, torch.Tensor], cfg) -> torch.Tensor:
     """PixAITorch.pool_head (reference.py:132-140) in f32: x [B, L, D] window-ordered -> logits."""
-    from . import quant as Q
+    import torch.nn.functional as F
 
     B, L, D = x.shape
     nh = cfg.heads
     g = lambda k: raw[k].to(x.device).float()  # noqa: E731
-    h = Q.layer_norm(x, g("head_pool.norm.weight"), g("head_pool.norm.bias"), cfg.ln_eps)
+    h = F.layer_norm(x, (D,), g("head_pool.norm.weight"), g("head_pool.norm.bias"), cfg.ln_eps)
     h = h + g("head_pool.pos_embed")[window_perm(cfg.grid, cfg.window).to(x.device)]
-    k, v = (h @ g("head_pool.kv.weight").t() + g("head_pool.kv.bias")).view(B, L, 2, nh, D // nh).permute(2, 0, 3, 1, 4)
+    k, v = F.linear(h, g("head_pool.kv.weight"), g("head_pool.kv.bias")).view(B, L, 2, nh, D // nh).permute(2, 0, 3, 1, 4)
     q = g("head_pool.q").reshape(1, nh, 1, D // nh).expand(B, nh, 1, D // nh)
-    o = _sdpa(q, k, v, (D // nh) ** -0.5).reshape(B, D)
-    o = o @ g("head_pool.proj.weight").t() + g("head_pool.proj.bias")
-    return o @ g("head.weight").t() + g("head.bias")
+    o = F.scaled_dot_product_attention(q, k, v).reshape(B, D)
+    o = F.linear(o, g("head_pool.proj.weight"), g("head_pool.proj.bias"))
+    return F.linear(o, g("head.weight"), g("head.bias"))
 
 
 def forward_int8(conv: dict[str, torch.Tensor], cfg, images: torch.Tensor, trace: list | None = None,
