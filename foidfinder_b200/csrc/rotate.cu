@@ -146,25 +146,30 @@ __device__ __forceinline__ void rot_row(const __half* __restrict__ xr, float eps
             v[i + h][k] = sub2(a, b);
           }
 
-    // Transpose through shared memory: column c of the group sits at c + 8 * (c / QB). Lanes with bit 2
-    // set move their two 16-byte halves in the opposite order, so each quarter-warp phase of a 16-byte
-    // access covers all 32 banks once.
-    const bool swap_halves = lane & 4;
+    // Transpose through shared memory. Writer lane l stores its 8 columns of a chunk as two 16-byte halves
+    // at c + 8 (c / QB) (c = chunk offset + 8 l), the halves swapped in place (low half at +4) when bit 2 of
+    // l is set: each quarter-warp phase of a 16-byte store then covers all 32 banks once. The swap is in
+    // the addresses only (no per-lane data selects); a reader of element t of writer l = t finds column
+    // e at offset e when bit 2 of t is clear and at e ^ 4 when it is set.
+    const int half_sw = (lane & 4) ? 4 : 0;
 #pragma unroll
     for (int i = c0; i < c0 + UNIT; ++i) {
       const int c = (i - c0) * 256 + lane * 8;
       float* d = sw + c + 8 * (c / QB);
-      const float4 lo = make_float4(v[i][0].x, v[i][0].y, v[i][1].x, v[i][1].y);
-      const float4 hi = make_float4(v[i][2].x, v[i][2].y, v[i][3].x, v[i][3].y);
-      *reinterpret_cast<float4*>(d + (swap_halves ? 4 : 0)) = swap_halves ? hi : lo;
-      *reinterpret_cast<float4*>(d + (swap_halves ? 0 : 4)) = swap_halves ? lo : hi;
+      *reinterpret_cast<float4*>(d + half_sw) = make_float4(v[i][0].x, v[i][0].y, v[i][1].x, v[i][1].y);
+      *reinterpret_cast<float4*>(d + 4 - half_sw) = make_float4(v[i][2].x, v[i][2].y, v[i][3].x, v[i][3].y);
     }
     __syncwarp();
     const int e = lane & 7, q = lane >> 3;
-    float* tp = sw + e + q * (QB + 8);  // transposed element t at tp[8 t]
+    // transposed element t at tp[8 t], tp = tp_a when bit 2 of t is clear, tp_b when it is set
+    float* const tp_a = sw + e + q * (QB + 8);
+    float* const tp_b = sw + (e ^ 4) + q * (QB + 8);
     float2 tv[G / 2];
 #pragma unroll
-    for (int j = 0; j < G / 2; ++j) tv[j] = make_float2(tp[16 * j], tp[16 * j + 8]);
+    for (int j = 0; j < G / 2; ++j) {
+      const float* tp = ((j >> 1) & 1) ? tp_b : tp_a;  // elements 2j, 2j + 1 share bit 2 (compile-time choice)
+      tv[j] = make_float2(tp[16 * j], tp[16 * j + 8]);
+    }
 #pragma unroll
     for (int j = 0; j < G / 2; ++j) tv[j] = make_float2(tv[j].x + tv[j].y, tv[j].x - tv[j].y);
 #pragma unroll
@@ -178,6 +183,7 @@ __device__ __forceinline__ void rot_row(const __half* __restrict__ xr, float eps
         }
 #pragma unroll
     for (int j = 0; j < G / 2; ++j) {
+      float* tp = ((j >> 1) & 1) ? tp_b : tp_a;
       tp[16 * j] = tv[j].x;
       tp[16 * j + 8] = tv[j].y;
     }
@@ -186,10 +192,8 @@ __device__ __forceinline__ void rot_row(const __half* __restrict__ xr, float eps
     for (int i = c0; i < c0 + UNIT; ++i) {
       const int c = (i - c0) * 256 + lane * 8;
       const float* d = sw + c + 8 * (c / QB);
-      const float4 first = *reinterpret_cast<const float4*>(d + (swap_halves ? 4 : 0));
-      const float4 second = *reinterpret_cast<const float4*>(d + (swap_halves ? 0 : 4));
-      const float4 a = swap_halves ? second : first;
-      const float4 b = swap_halves ? first : second;
+      const float4 a = *reinterpret_cast<const float4*>(d + half_sw);
+      const float4 b = *reinterpret_cast<const float4*>(d + 4 - half_sw);
       v[i][0] = make_float2(a.x, a.y);
       v[i][1] = make_float2(a.z, a.w);
       v[i][2] = make_float2(b.x, b.y);
