@@ -76,6 +76,20 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
   return g * rcp_newton(1.f + e) * u;
 }
 
+// silu_mul on two lanes at once: the same operations in the same order, packed f32x2 where both lanes
+// take the same one (exactly rounded per lane), so the results equal silu_mul's bit for bit.
+__device__ __forceinline__ float2 silu_mul2(float2 g, float2 u) {
+  const float2 t = mul2(g, make_float2(-1.4426950408889634f, -1.4426950408889634f));
+  const float2 e = make_float2(ex2_approx(fminf(t.x, 64.f)), ex2_approx(fminf(t.y, 64.f)));
+  const float2 d = add2(make_float2(1.f, 1.f), e);
+  const float2 nd = make_float2(-d.x, -d.y), two = make_float2(2.f, 2.f);
+  float2 y = make_float2(__int_as_float(0x7EF311C7 - __float_as_int(d.x)), __int_as_float(0x7EF311C7 - __float_as_int(d.y)));
+  y = mul2(y, fma2(nd, y, two));
+  y = mul2(y, fma2(nd, y, two));
+  y = mul2(y, fma2(nd, y, two));
+  return mul2(mul2(g, y), u);
+}
+
 // Coalesced store of a warp's 32-row x 128-byte block: each lane wrote its own row into `stg` (16-byte
 // chunks XOR-swizzled by row % 8, so both phases are bank-conflict free); here every 8 lanes copy one
 // full row, 4 rows (4 whole cache lines) per warp instruction.
@@ -105,6 +119,21 @@ __device__ __forceinline__ uint4 staged_chunk64(const uint8_t* stg, int r, int c
 // costs six. With the current epilogues the XU pipe has room, and I2F measured faster on every GEMM
 // shape (SwiGLU epilogue +12%).
 __device__ __forceinline__ float acc_to_float(uint32_t raw) { return __int2float_rn(static_cast<int>(raw)); }
+
+// dequant32 in packed f32x2 form: (acc * rs) * cs + b per lane, the same two roundings as the scalar form.
+__device__ __forceinline__ void dequant32_x2(const uint32_t (&r)[32], float rs, const float* cs, const float* bias,
+                                             float2 (&y)[16]) {
+  const float2 rs2 = make_float2(rs, rs);
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {
+    const float4 c4 = *reinterpret_cast<const float4*>(cs + j);
+    const float4 b4 = *reinterpret_cast<const float4*>(bias + j);
+    y[j / 2] = fma2(mul2(make_float2(acc_to_float(r[j]), acc_to_float(r[j + 1])), rs2), make_float2(c4.x, c4.y),
+                    make_float2(b4.x, b4.y));
+    y[j / 2 + 1] = fma2(mul2(make_float2(acc_to_float(r[j + 2]), acc_to_float(r[j + 3])), rs2),
+                        make_float2(c4.z, c4.w), make_float2(b4.z, b4.w));
+  }
+}
 
 __device__ __forceinline__ void dequant32(const uint32_t (&r)[32], float rs, const float* cs, const float* bias,
                                           float (&y)[32]) {
@@ -344,12 +373,14 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, PAIR>::THREADS, 1)
           tmem_ld32(tbase + cg, rg);
           tmem_ld32(tbase + cu, ru);
           tmem_ld_wait();
-          float g[32], u[32];
-          dequant32(rg, rs, args.col_scale + n_tile + cg, args.bias + n_tile + cg, g);
-          dequant32(ru, rs, args.col_scale + n_tile + cu, args.bias + n_tile + cu, u);
+          float2 g[16], u[16];
+          dequant32_x2(rg, rs, args.col_scale + n_tile + cg, args.bias + n_tile + cg, g);
+          dequant32_x2(ru, rs, args.col_scale + n_tile + cu, args.bias + n_tile + cu, u);
 #pragma unroll
-          for (int j = 0; j < 32; j += 2)
-            packed[sub * 16 + j / 2] = pack_half2(silu_mul(g[j], u[j]), silu_mul(g[j + 1], u[j + 1]));
+          for (int j = 0; j < 16; ++j) {
+            const float2 h = silu_mul2(g[j], u[j]);
+            packed[sub * 16 + j] = pack_half2(h.x, h.y);
+          }
         }
         const int col0 = (n_tile >> 1) + (BN == 256 ? half * 64 : half * 32);
         // The staging buffer is free once this warp's previous TMA store has read it.
