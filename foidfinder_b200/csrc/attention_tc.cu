@@ -579,6 +579,10 @@ __global__ void __launch_bounds__(TAILW ? fa::THREADS_TAIL : fa::THREADS, 1)
           // pushed the kernel to the 168-register cap with spills (measured 5-10% slower).
           float mx = -INFINITY;
           if (full_tile) {
+            // Four independent running maxima (max is exact, so the order does not change the result): a
+            // single chain of 64 dependent max instructions per tile left the two softmax warps of each
+            // scheduler waiting on its latency.
+            float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
               uint32_t raw[2][32];
@@ -589,8 +593,9 @@ __global__ void __launch_bounds__(TAILW ? fa::THREADS_TAIL : fa::THREADS, 1)
               for (int c = 0; c < 2; ++c)
 #pragma unroll
                 for (int e = 0; e < 32; e += 2)
-                  mx = max3(mx, __uint_as_float(raw[c][e]), __uint_as_float(raw[c][e + 1]));
+                  mq[(e >> 1) & 3] = max3(mq[(e >> 1) & 3], __uint_as_float(raw[c][e]), __uint_as_float(raw[c][e + 1]));
             }
+            mx = max3(mq[0], mq[1], fmaxf(mq[2], mq[3]));
           } else {
             mx = fa::ragged_max(ts, valid);
           }

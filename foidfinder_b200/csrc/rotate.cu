@@ -206,18 +206,23 @@ __device__ __forceinline__ void rot_row(const __half* __restrict__ xr, float eps
                           : BLOCK == 256 ? 0.0625f
                           : BLOCK == 512 ? 0.04419417382415922f
                                          : 0.03125f;  // 1 / sqrt(BLOCK)
+  // For power-of-two blocks (1/sqrt(BLOCK) = 2^-k) the normalisation is folded into the row maximum and
+  // the quantisation multiplier: scaling by a power of two is exact, so scale and codes are bit-identical
+  // to normalising first.
+  constexpr bool kPow2Norm = BLOCK == 256 || BLOCK == 1024;
   const float2 n2 = make_float2(kNorm, kNorm);
   float amax = 0.f;
 #pragma unroll
   for (int i = 0; i < NCH; ++i)
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      v[i][k] = mul2(v[i][k], n2);
+      if constexpr (!kPow2Norm) v[i][k] = mul2(v[i][k], n2);
       amax = max3(amax, fabsf(v[i][k].x), fabsf(v[i][k].y));
     }
   amax = warp_max(amax);
+  if constexpr (kPow2Norm) amax *= kNorm;
   const float scale = fmaxf(amax, 1e-12f) / 127.f;
-  const float inv = 1.f / scale;
+  const float inv = kPow2Norm ? (1.f / scale) * kNorm : 1.f / scale;
   const float2 inv2 = make_float2(inv, inv), magic2 = make_float2(12582912.f, 12582912.f);
   int8_t* orow = out + static_cast<size_t>(row) * COLS;
 #pragma unroll

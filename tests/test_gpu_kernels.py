@@ -109,17 +109,34 @@ def _ref_attention(qkv, seqs, T, heads, scale, rope=None):
                                                           (2, 577, 16, False), (2, 259, 8, False), (1, 1540, 4, False),
                                                           # the keys of the ragged last key tile (and the
                                                           # CUDA-core tail rows) hold the row maximum by far
-                                                          (2, 1025, 16, "dominant"), (1, 1540, 4, "dominant")])
+                                                          (2, 1025, 16, "dominant"), (1, 1540, 4, "dominant"),
+                                                          # the running maximum grows past the rescale
+                                                          # threshold in the second half of the first key
+                                                          # tile (its first half's P is recomputed), in the
+                                                          # second half of a later tile (O rescaled and the
+                                                          # first half recomputed), in the first half of a
+                                                          # later tile, and steadily over all tiles
+                                                          (2, 1025, 16, ("dominant", 64, 128)),
+                                                          (1, 1025, 16, ("dominant", 320, 384)),
+                                                          (1, 1025, 16, ("dominant", 512, 560)),
+                                                          (2, 1025, 8, "ramp")])
 def test_attention_matches_oracle(cuda_device, no_device_error, seqs, T, heads, rope):
     from foidfinder_b200 import ops
 
     g = torch.Generator().manual_seed(seqs * 1000 + T)
     qkv = torch.randn(seqs * T, 3 * heads * 64, generator=g).half()
-    if rope == "dominant":
+    if rope == "dominant" or isinstance(rope, tuple):
+        k0, k1 = (T - T % 128, T) if rope == "dominant" else rope[1:]
         rope = False
         x = qkv.view(seqs, T, 3, heads, 64)
         x[:, :, 0] = x[:, :, 0].abs()  # q >= 0
-        x[:, T - T % 128 :, 1] = 0.6 * (1 + torch.rand(seqs, T % 128, heads, 64, generator=g)).half()  # q k ~ 60
+        x[:, k0:k1, 1] = 0.6 * (1 + torch.rand(seqs, k1 - k0, heads, 64, generator=g)).half()  # q k ~ 60
+    elif rope == "ramp":
+        rope = False
+        x = qkv.view(seqs, T, 3, heads, 64)
+        x[:, :, 0] = x[:, :, 0].abs()
+        ramp = torch.linspace(0.0, 1.2, T).view(1, T, 1, 1)  # q k grows from ~0 to ~70 over the keys
+        x[:, :, 1] = (ramp * (1 + torch.rand(seqs, T, heads, 64, generator=g))).half()
     scale = 1.0 / math.sqrt(64)
     tables = None
     if rope:
