@@ -16,7 +16,9 @@
 //                                 64-wide atom of ones, MN-major, N = 80)     -> [256 + 80 i, +80)
 //              issue order per key tile j: PV_0(j), S_0(j+1), PV_1(j), S_1(j+1). An S MMA overwrites the
 //              columns its tile's P was read from; tcgen05.mma operations of one thread execute in issue
-//              order, so the preceding P V has consumed P by then.
+//              order, so the preceding P V has consumed P by then. Each P V starts in two halves: keys
+//              0..63 as soon as the softmax has written their P (p_half), keys 64..127 after the rest
+//              (p_full), so the first half of the product overlaps the second half of the softmax.
 //   warps 2-5  softmax of Q0, warps 6-9 softmax of Q1: one query row per thread (TMEM lane = row),
 //              row max, lazy rescale of O and l in TMEM when the max grows by more than 2^8, then
 //              P = 2^(s log2e scale - m + 7) as fp16 pairs written back over S. The two warpgroups run
@@ -318,7 +320,8 @@ __global__ void __launch_bounds__(TAILW ? fa::THREADS_TAIL : fa::THREADS, 1)
   uint64_t* kv_empty = kv_full + STAGES;   // [STAGES]
   uint64_t* s_full = kv_empty + STAGES;    // [2] per query tile
   uint64_t* p_full = s_full + 2;           // [2]
-  uint64_t* o_full = p_full + 2;           // [2]
+  uint64_t* p_half = p_full + 2;           // [2] P of keys 0..63 written
+  uint64_t* o_full = p_half + 2;           // [2]
   uint64_t* o_empty = o_full + 2;          // [2]
   uint64_t* drain = o_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -346,6 +349,7 @@ __global__ void __launch_bounds__(TAILW ? fa::THREADS_TAIL : fa::THREADS, 1)
       mbar_init(&q_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);
+      mbar_init(&p_half[i], 4);
       mbar_init(&o_full[i], 1);
       mbar_init(&o_empty[i], 4);
     }
@@ -440,11 +444,11 @@ __global__ void __launch_bounds__(TAILW ? fa::THREADS_TAIL : fa::THREADS, 1)
         for (int k = 0; k < 4; ++k) mma_f16(tmem + t_s(i), qd + 2 * k, kd + 2 * k, id, k > 0);
         tc_commit(&s_full[i]);
       };
-      auto issue_pv = [&](int i, int j, int c, bool tail) {
+      auto issue_pv = [&](int i, int j, int c, bool tail, int k0) {  // K steps k0 .. k0 + 3
         const uint32_t sv = smem_u32(smem + OFF_V + (c % STAGES) * TILE);
         const int steps = tail ? kv_tail_n / 16 : 8;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {  // 16 keys per step: P columns 8k.., V rows 16k..
+        for (int k = k0; k < k0 + 4; ++k) {  // 16 keys per step: P columns 8k.., V rows 16k..
           if (k < steps) {
             const uint32_t acc = (j > 0 || k > 0) ? 1u : 0u;
             mma_f16_ts(tmem + t_o(i), tmem + t_s(i) + 8 * k, fa::sdesc_mn_sw128(sv + k * 2048), id_o, acc);
@@ -495,13 +499,19 @@ __global__ void __launch_bounds__(TAILW ? fa::THREADS_TAIL : fa::THREADS, 1)
           const uint32_t par = static_cast<uint32_t>(tiles) & 1u;
           const uint32_t opar = static_cast<uint32_t>(n - 1) & 1u;
           if (last) tc_commit(&q_empty[qb]);  // every S of this item is issued: Q frees when they complete
-          if (!mbar_wait(&p_full[0], par, abort_flag, err, kDevTimeoutAttn) ||
+          if (!mbar_wait(&p_half[0], par, abort_flag, err, kDevTimeoutAttn) ||
               (j == 0 && n > 0 && !mbar_wait(&o_empty[0], opar, abort_flag, err, kDevTimeoutAttn))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          issue_pv(0, j, kv_count, last);
+          issue_pv(0, j, kv_count, last, 0);
+          if (!mbar_wait(&p_full[0], par, abort_flag, err, kDevTimeoutAttn)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(0, j, kv_count, last, 4);
           if (last) tc_commit(&o_full[0]);
           if (next) {
             if (!kv_wait(kv_count + 1) ||
@@ -513,13 +523,19 @@ __global__ void __launch_bounds__(TAILW ? fa::THREADS_TAIL : fa::THREADS, 1)
             tc_fence_after();
             issue_s(0, nqb, kv_count + 1, ntail);
           }
-          if (!mbar_wait(&p_full[1], par, abort_flag, err, kDevTimeoutAttn) ||
+          if (!mbar_wait(&p_half[1], par, abort_flag, err, kDevTimeoutAttn) ||
               (has1 && j == 0 && n > 0 && !mbar_wait(&o_empty[1], opar, abort_flag, err, kDevTimeoutAttn))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          if (has1) issue_pv(1, j, kv_count, last);
+          if (has1) issue_pv(1, j, kv_count, last, 0);
+          if (!mbar_wait(&p_full[1], par, abort_flag, err, kDevTimeoutAttn)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (has1) issue_pv(1, j, kv_count, last, 4);
           if (last) tc_commit(&o_full[1]);
           tc_commit(&kv_empty[kv_count % STAGES]);
           if (next) {
@@ -611,6 +627,15 @@ __global__ void __launch_bounds__(TAILW ? fa::THREADS_TAIL : fa::THREADS, 1)
           }
           if (__any_sync(0xffffffffu, rescale)) fa::rescale_o(tmem + lane_base + t_o(g), corr);
         }
+        // P of keys 0..63 is in TMEM: the first half of this tile's P V may start.
+        auto signal_half = [&]() {
+          __syncwarp();
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&p_half[g]);
+        };
+        bool half_sent = false;
         if (active) {
           // Pass 2: P = 2^(s * scale_log2 - m_ref + 7) as fp16 pairs over S columns [0, 64), in two halves
           // of 64 keys (two loads, one wait each). P of half hf (columns 32hf..32hf+31) only overlaps S
@@ -636,11 +661,16 @@ __global__ void __launch_bounds__(TAILW ? fa::THREADS_TAIL : fa::THREADS, 1)
                 }
                 tmem_st16(ts + 16 * c, pk);
               }
+              if (hf == 0) {
+                signal_half();
+                half_sent = true;
+              }
             }
           } else {
             fa::ragged_p(ts, valid, scale_log2, kPScaleLog2 - m_ref);
           }
         }
+        if (!half_sent) signal_half();
         __syncwarp();
         tmem_st_wait();
         tc_fence_before();
