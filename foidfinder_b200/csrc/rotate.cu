@@ -83,23 +83,28 @@ __device__ __forceinline__ void rot_row(const __half* __restrict__ xr, float eps
 
   float rstd = 0.f;
   if constexpr (NORM) {
-    float2 s2 = make_float2(0.f, 0.f);
+    // Four partial sums per statistic (one per register pair k): with only a few warps per scheduler, one
+    // chain of 4 NCH dependent adds per row left the warps waiting on its latency.
+    float2 s2[4], q2[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) s2[k] = q2[k] = make_float2(0.f, 0.f);
 #pragma unroll
     for (int i = 0; i < NCH; ++i)
 #pragma unroll
-      for (int k = 0; k < 4; ++k) s2 = add2(s2, v[i][k]);
+      for (int k = 0; k < 4; ++k) s2[k] = add2(s2[k], v[i][k]);
+    const float2 st = add2(add2(s2[0], s2[1]), add2(s2[2], s2[3]));
     const float inv_n = 1.f / static_cast<float>(valid_cols);
-    const float mean = warp_sum(s2.x + s2.y) * inv_n;
+    const float mean = warp_sum(st.x + st.y) * inv_n;
     const float2 m2 = make_float2(mean, mean);
-    float2 q2 = make_float2(0.f, 0.f);
 #pragma unroll
     for (int i = 0; i < NCH; ++i)
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         v[i][k] = sub2(v[i][k], m2);
-        q2 = fma2(v[i][k], v[i][k], q2);
+        q2[k] = fma2(v[i][k], v[i][k], q2[k]);
       }
-    const float q = warp_sum(q2.x + q2.y) - static_cast<float>(COLS - valid_cols) * mean * mean;
+    const float2 qt = add2(add2(q2[0], q2[1]), add2(q2[2], q2[3]));
+    const float q = warp_sum(qt.x + qt.y) - static_cast<float>(COLS - valid_cols) * mean * mean;
     rstd = rsqrtf(fmaxf(q, 0.f) * inv_n + eps);
   }
 
@@ -211,15 +216,15 @@ __device__ __forceinline__ void rot_row(const __half* __restrict__ xr, float eps
   // to normalising first.
   constexpr bool kPow2Norm = BLOCK == 256 || BLOCK == 1024;
   const float2 n2 = make_float2(kNorm, kNorm);
-  float amax = 0.f;
+  float am[4] = {0.f, 0.f, 0.f, 0.f};  // independent running maxima (max is exact in any order)
 #pragma unroll
   for (int i = 0; i < NCH; ++i)
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       if constexpr (!kPow2Norm) v[i][k] = mul2(v[i][k], n2);
-      amax = max3(amax, fabsf(v[i][k].x), fabsf(v[i][k].y));
+      am[k] = max3(am[k], fabsf(v[i][k].x), fabsf(v[i][k].y));
     }
-  amax = warp_max(amax);
+  float amax = warp_max(max3(am[0], am[1], fmaxf(am[2], am[3])));
   if constexpr (kPow2Norm) amax *= kNorm;
   const float scale = fmaxf(amax, 1e-12f) / 127.f;
   const float inv = kPow2Norm ? (1.f / scale) * kNorm : 1.f / scale;
