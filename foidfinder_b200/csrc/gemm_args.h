@@ -27,7 +27,7 @@ struct GemmArgs {
   void* out;
   int ldo;              // output row stride (elements)
   int n_valid;          // EPI_LOGITS: columns written
-  const float* rope_cos;   // EPI_QKV_ROPE: [tokens, 32]
+  const float* rope_cos;   // EPI_QKV_ROPE: angle-major [32, tokens]
   const float* rope_sin;
   int rope_cols;        // EPI_QKV_ROPE: columns [0, rope_cols) are rotated (q and k)
   int tokens;           // tokens per image (RoPE position = m % tokens; stem row remap)

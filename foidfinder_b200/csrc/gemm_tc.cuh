@@ -99,6 +99,13 @@ __device__ __forceinline__ void stage_row128(uint8_t* stg, int lane, const uint3
     *reinterpret_cast<uint4*>(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) =
         make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
 }
+// Half of a 128-byte row (16-byte chunks 4h .. 4h + 3), same swizzle as stage_row128.
+__device__ __forceinline__ void stage_half_row128(uint8_t* stg, int lane, int h, const uint32_t (&w)[16]) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    *reinterpret_cast<uint4*>(stg + lane * 128 + (((4 * h + c) ^ (lane & 7)) << 4)) =
+        make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+}
 __device__ __forceinline__ uint4 staged_chunk128(const uint8_t* stg, int r, int c) {
   return *reinterpret_cast<const uint4*>(stg + r * 128 + ((c ^ (r & 7)) << 4));
 }
@@ -348,12 +355,27 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, PAIR>::THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = unit; t < tiles; t += units) {
-      if (!wait(&tfull[acc], acc_phase, kDevTimeoutTmemFull)) break;
-      tc_fence_after();
       const int tm = t / tiles_n, tn = t % tiles_n;
       const int m_block = tm * C::TILE_M + static_cast<int>(rank) * C::BM + q * 32;  // this warp's 32-row block
       const int m = m_block + row_in_tile - q * 32;
       const bool row_ok = m < args.M;
+      // RoPE: this row's 32 angles, loaded once per tile (every 64-column head of the tile rotates by the
+      // same angles) and before the accumulator wait, so their L2 latency overlaps the mainloop. The
+      // tables are angle-major [32, tokens]: the warp's 32 consecutive rows read 128 contiguous bytes per
+      // angle (one wavefront); the table column of position 0 (class token) is the identity.
+      float rope_c[EPI == EPI_QKV_ROPE ? 32 : 1], rope_s[EPI == EPI_QKV_ROPE ? 32 : 1];
+      if constexpr (EPI == EPI_QKV_ROPE) {
+        if (tn * BN < args.rope_cols) {
+          const int pos = (row_ok ? m : 0) % args.tokens;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            rope_c[j] = __ldg(args.rope_cos + static_cast<size_t>(j) * args.tokens + pos);
+            rope_s[j] = __ldg(args.rope_sin + static_cast<size_t>(j) * args.tokens + pos);
+          }
+        }
+      }
+      if (!wait(&tfull[acc], acc_phase, kDevTimeoutTmemFull)) break;
+      tc_fence_after();
       const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const int n_tile = tn * BN;
       float rs = 1.f;
@@ -364,7 +386,11 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, PAIR>::THREADS, 1)
         // Tile columns hold [gate 64 | up 64] groups; the output h has N/2 columns.
         constexpr int OUTS = BN == 256 ? 64 : 32;  // output columns per warp
         const int cg0 = BN == 256 ? half * 128 : half * 32;
-        uint32_t packed[OUTS / 2];
+        const int col0 = (n_tile >> 1) + (BN == 256 ? half * 64 : half * 32);
+        // The staging buffer is free once this warp's previous TMA store has read it; each 32-column
+        // group of the output goes into it as soon as it is packed.
+        if (lane == 0) bulk_wait_read_all();
+        __syncwarp();
 #pragma unroll
         for (int sub = 0; sub < OUTS / 32; ++sub) {
           uint32_t rg[32], ru[32];
@@ -376,20 +402,18 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, PAIR>::THREADS, 1)
           float2 g[16], u[16];
           dequant32_x2(rg, rs, args.col_scale + n_tile + cg, args.bias + n_tile + cg, g);
           dequant32_x2(ru, rs, args.col_scale + n_tile + cu, args.bias + n_tile + cu, u);
+          uint32_t packed[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const float2 h = silu_mul2(g[j], u[j]);
-            packed[sub * 16 + j] = pack_half2(h.x, h.y);
+            packed[j] = pack_half2(h.x, h.y);
+          }
+          if constexpr (OUTS == 64) {
+            stage_half_row128(stg, lane, sub, packed);
+          } else {
+            stage_row64(stg, lane, packed);
           }
         }
-        const int col0 = (n_tile >> 1) + (BN == 256 ? half * 64 : half * 32);
-        // The staging buffer is free once this warp's previous TMA store has read it.
-        if (lane == 0) bulk_wait_read_all();
-        __syncwarp();
-        if constexpr (OUTS == 64)
-          stage_row128(stg, lane, packed);
-        else
-          stage_row64(stg, lane, packed);
         fence_async_smem();
         __syncwarp();
         if (lane == 0) {
@@ -404,7 +428,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, PAIR>::THREADS, 1)
         for (int ch = 0; ch < HALF / 64; ++ch) {
           const int c0 = half * HALF + ch * 64;  // tile column of this chunk
           const int n0 = n_tile + c0;
-          uint32_t packed[32];
+          // The staging buffer is free once this warp's previous TMA store has read it; each 32-column
+          // half of the chunk goes into it as soon as it is packed.
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
 #pragma unroll
           for (int sub = 0; sub < 2; ++sub) {
             uint32_t r[32];
@@ -429,16 +456,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, PAIR>::THREADS, 1)
             if constexpr (EPI == EPI_QKV_ROPE) {
               if (n0 < args.rope_cols) {
                 // Interleaved pairs (2i, 2i+1) of each 64-wide head rotate by the angle of pair i at this
-                // token's position; the table column of position 0 (class token) is the identity. The
-                // tables are angle-major [32, tokens], so the warp's 32 consecutive rows read 128
-                // contiguous bytes per angle (one wavefront) instead of 32 scattered 16-byte pieces.
-                const int pos = (row_ok ? m : 0) % args.tokens;
-                const float* cr = args.rope_cos + static_cast<size_t>(sub * 16) * args.tokens + pos;
-                const float* sr = args.rope_sin + static_cast<size_t>(sub * 16) * args.tokens + pos;
+                // token's position.
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
-                  const float cc = __ldg(cr + static_cast<size_t>(j) * args.tokens);
-                  const float ss = __ldg(sr + static_cast<size_t>(j) * args.tokens);
+                  const float cc = rope_c[sub * 16 + j], ss = rope_s[sub * 16 + j];
                   const float x0 = y[2 * j], x1 = y[2 * j + 1];
                   y[2 * j] = x0 * cc - x1 * ss;
                   y[2 * j + 1] = x0 * ss + x1 * cc;
@@ -449,12 +470,11 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, PAIR>::THREADS, 1)
 #pragma unroll
               for (int j = 0; j < 32; ++j) y[j] = gelu_tanh(y[j]);
             }
+            uint32_t packed[16];
 #pragma unroll
-            for (int j = 0; j < 32; j += 2) packed[sub * 16 + j / 2] = pack_half2(y[j], y[j + 1]);
+            for (int j = 0; j < 32; j += 2) packed[j / 2] = pack_half2(y[j], y[j + 1]);
+            stage_half_row128(stg, lane, sub, packed);
           }
-          if (lane == 0) bulk_wait_read_all();
-          __syncwarp();
-          stage_row128(stg, lane, packed);
           fence_async_smem();
           __syncwarp();
           if (lane == 0) {
