@@ -183,11 +183,13 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, PAIR>::THREADS, 1)
   const int unit = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);  // CTA or pair
   const int units = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
   // Waits on barriers the other CTA of a pair arrives on take cluster-scope acquire.
+  // Waiting threads suspend rather than poll (mbar_wait<true>), leaving issue slots to the MMA thread and
+  // the epilogue warps that share their schedulers.
   auto wait = [&](uint64_t* bar, uint32_t parity, int code) {
     if constexpr (PAIR)
-      return mbar_wait_cluster(bar, parity, abort_flag, args.err, code);
+      return mbar_wait_cluster<true>(bar, parity, abort_flag, args.err, code);
     else
-      return mbar_wait(bar, parity, abort_flag, args.err, code);
+      return mbar_wait<true>(bar, parity, abort_flag, args.err, code);
   };
 
   if (threadIdx.x == 0) {

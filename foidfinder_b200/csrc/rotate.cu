@@ -364,7 +364,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       if (lane == 0) issue(next, b ^ 1);
       ++issued;
     }
-    if (!mbar_wait(&bars[wid][b], static_cast<uint32_t>(k >> 1) & 1u, abort_v, err, kDevTimeoutRotate)) break;
+    if (!mbar_wait<true>(&bars[wid][b], static_cast<uint32_t>(k >> 1) & 1u, abort_v, err, kDevTimeoutRotate)) break;
     ++waited;
     rot_row<NCH, BLOCK, NORM, true>(buf(b), eps, row, valid_cols, out, row_scale, tbuf + wid * S::SW, lane,
                                     [&](int i, float (&g)[8], float (&bb)[8]) {
@@ -542,9 +542,13 @@ __global__ void __launch_bounds__((WPR >= 8 ? 1 : 8 / WPR) * WPR * 32)
     }
   }
 
-  const bool swap_halves = lane & 4;
+  // Transposes as in rot_row: writer lane l stores the low half of its 8 columns at +4 when bit 2 of l is
+  // set (the swap is in the addresses only), so a reader of element t finds column e at offset e ^ 4 when
+  // bit 2 of t is set.
+  const int half_sw = (lane & 4) ? 4 : 0;
   const int e = lane & 7, q = lane >> 3;
-  float* tp = sw + e + q * (QB + 8);  // transposed element t at tp[8 t]
+  float* const tp_a = sw + e + q * (QB + 8);        // transposed element t at tp[8 t], bit 2 of t clear
+  float* const tp_b = sw + (e ^ 4) + q * (QB + 8);  // bit 2 of t set
 #pragma unroll
   for (int c0 = 0; c0 < CPW; c0 += 2) {
     if (first + c0 >= nch) break;  // warp-uniform: the rest of this warp's chunks are past the row
@@ -566,15 +570,16 @@ __global__ void __launch_bounds__((WPR >= 8 ? 1 : 8 / WPR) * WPR * 32)
     for (int i = c0; i < c0 + 2; ++i) {
       const int c = (i - c0) * 256 + lane * 8;
       float* d = sw + c + 8 * (c / QB);
-      const float4 lo = make_float4(v[i][0].x, v[i][0].y, v[i][1].x, v[i][1].y);
-      const float4 hi = make_float4(v[i][2].x, v[i][2].y, v[i][3].x, v[i][3].y);
-      *reinterpret_cast<float4*>(d + (swap_halves ? 4 : 0)) = swap_halves ? hi : lo;
-      *reinterpret_cast<float4*>(d + (swap_halves ? 0 : 4)) = swap_halves ? lo : hi;
+      *reinterpret_cast<float4*>(d + half_sw) = make_float4(v[i][0].x, v[i][0].y, v[i][1].x, v[i][1].y);
+      *reinterpret_cast<float4*>(d + 4 - half_sw) = make_float4(v[i][2].x, v[i][2].y, v[i][3].x, v[i][3].y);
     }
     __syncwarp();
     float2 tv[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) tv[j] = make_float2(tp[16 * j], tp[16 * j + 8]);
+    for (int j = 0; j < 8; ++j) {
+      const float* tp = ((j >> 1) & 1) ? tp_b : tp_a;  // elements 2j, 2j + 1 share bit 2 (compile-time choice)
+      tv[j] = make_float2(tp[16 * j], tp[16 * j + 8]);
+    }
 #pragma unroll
     for (int j = 0; j < 8; ++j) tv[j] = make_float2(tv[j].x + tv[j].y, tv[j].x - tv[j].y);
 #pragma unroll
@@ -588,6 +593,7 @@ __global__ void __launch_bounds__((WPR >= 8 ? 1 : 8 / WPR) * WPR * 32)
         }
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
+      float* tp = ((j >> 1) & 1) ? tp_b : tp_a;
       tp[16 * j] = tv[j].x;
       tp[16 * j + 8] = tv[j].y;
     }
@@ -596,10 +602,8 @@ __global__ void __launch_bounds__((WPR >= 8 ? 1 : 8 / WPR) * WPR * 32)
     for (int i = c0; i < c0 + 2; ++i) {
       const int c = (i - c0) * 256 + lane * 8;
       const float* d = sw + c + 8 * (c / QB);
-      const float4 f0 = *reinterpret_cast<const float4*>(d + (swap_halves ? 4 : 0));
-      const float4 f1 = *reinterpret_cast<const float4*>(d + (swap_halves ? 0 : 4));
-      const float4 a = swap_halves ? f1 : f0;
-      const float4 b = swap_halves ? f0 : f1;
+      const float4 a = *reinterpret_cast<const float4*>(d + half_sw);
+      const float4 b = *reinterpret_cast<const float4*>(d + 4 - half_sw);
       v[i][0] = make_float2(a.x, a.y);
       v[i][1] = make_float2(a.z, a.w);
       v[i][2] = make_float2(b.x, b.y);
