@@ -179,6 +179,7 @@ int build_batch(ff_engine* e, int B, ff_engine::Batch** out) {
   int rc = FF_OK;
   {
     GemmProblem p{};
+    p.args.w_const = 1;  // the engine's weights stay constant while forwards run
     p.A = b->patches;
     p.W = e->w.patch_w;
     p.out = b->x;
@@ -195,6 +196,7 @@ int build_batch(ff_engine* e, int B, ff_engine::Batch** out) {
   }
   if (rc == FF_OK) {
     GemmProblem p{};
+    p.args.w_const = 1;  // the engine's weights stay constant while forwards run
     p.A = b->cls;
     p.W = e->w.head_w;
     p.out = b->logits;
@@ -213,6 +215,7 @@ int build_batch(ff_engine* e, int B, ff_engine::Batch** out) {
     // PixAI pool (reference.py:133-140): pool-normed tokens (+ pos) in o, keys|values in qkv, the attended
     // [B, dim] rows in h, the projected rows in cls (the tag head's input).
     GemmProblem p{};
+    p.args.w_const = 1;  // the engine's weights stay constant while forwards run
     p.A = b->o;
     p.W = e->w.pool_kv_w;
     p.out = b->qkv;
@@ -226,6 +229,7 @@ int build_batch(ff_engine* e, int B, ff_engine::Batch** out) {
     rc = gemm_prepare(p, &b->pool_kv);
     if (rc == FF_OK) {
       GemmProblem q{};
+      q.args.w_const = 1;
       q.A = b->h;
       q.W = e->w.pool_proj_w;
       q.out = b->cls;
@@ -251,6 +255,7 @@ int build_batch(ff_engine* e, int B, ff_engine::Batch** out) {
     const int rope_tokens = glob ? e->tokens : c.window * c.window;  // the RoPE table's rows
     auto prep = [&](GemmPlan* plan, const int8_t* W, const float* s, const float* bias, void* out, int N, int K, int epi) {
       GemmProblem p{};
+      p.args.w_const = 1;  // the engine's weights stay constant while forwards run
       p.A = b->a8;
       p.W = W;
       p.out = out;

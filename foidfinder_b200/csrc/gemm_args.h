@@ -34,6 +34,8 @@ struct GemmArgs {
   const float* pos_bias;   // EPI_STEM: [patches, N] = patch bias + position embedding
   int patches;          // EPI_STEM: patches per image
   int* err;             // device error word
+  int w_const;          // 1: no kernel writes W while a forward runs (the engine's weights), so the producer may
+                        // load W tiles before the wait for the previous kernel (programmatic dependent launch)
 };
 
 }  // namespace ff

@@ -223,7 +223,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, PAIR>::THREADS, 1)
   if constexpr (PAIR) cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  pdl_wait();  // the prologue above overlapped the previous kernel; from here on its outputs are visible
+  // The prologue above overlapped the previous kernel (programmatic dependent launch). Each role waits for
+  // that kernel's outputs (pdl_wait) only before its first access to them: with args.w_const the producer
+  // first loads the weight tiles of its first stages, which no kernel of the forward writes.
   pdl_trigger();
 
   if (warp == 0) {
@@ -235,15 +237,36 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, PAIR>::THREADS, 1)
 #pragma unroll
       for (int s = 0; s < STAGES; ++s) last_phase[s] = -1;
       constexpr int kElemsPerStage = F16IN ? C::BKB / 2 : C::BKB;
+      // W tiles of the first tile's first stages, ahead of the wait for the previous kernel (the stages
+      // are fresh, so no empty-wait; each full barrier expects the whole stage, A included).
+      const int pre = (!PAIR && args.w_const && unit < tiles) ? (args.num_kb < STAGES ? args.num_kb : STAGES) : 0;
+      if (!PAIR) {
+        for (int kb = 0; kb < pre; ++kb) {
+          mbar_arrive_expect_tx(&full[kb], C::STAGE_BYTES);
+          tma_load_2d(smem + kb * C::STAGE_BYTES + C::A_BYTES, &tmB, &full[kb], kb * kElemsPerStage,
+                      (unit % tiles_n) * BN);
+        }
+      }
+      pdl_wait();
       bool ok = true;
+      bool first = true;
       for (int t = unit; t < tiles && ok; t += units) {
         const int tm = t / tiles_n, tn = t % tiles_n;
         for (int kb = 0; kb < args.num_kb; ++kb) {
+          uint8_t* sa = smem + stage * C::STAGE_BYTES;
+          if (first && kb < pre) {  // W already on its way: only A
+            tma_load_2d(sa, &tmA, &full[stage], kb * kElemsPerStage, tm * C::BM);
+            last_phase[stage] = static_cast<int>(phase);
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            continue;
+          }
           if (!wait(&empty[stage], phase ^ 1u, kDevTimeoutSmemEmpty)) {
             ok = false;
             break;
           }
-          uint8_t* sa = smem + stage * C::STAGE_BYTES;
           if constexpr (PAIR) {
             // Both CTAs' copies of this stage complete on the even CTA's full barrier.
             if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
@@ -262,6 +285,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, PAIR>::THREADS, 1)
             phase ^= 1u;
           }
         }
+        first = false;
       }
       if (!ok && leader) {
         // Let every issued copy land before the CTA exits (bounded). In a pair the even CTA's full barrier
@@ -277,6 +301,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, PAIR>::THREADS, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (the even CTA of a pair)
+    pdl_wait();
     if (lane == 0 && leader) {
       constexpr uint32_t idesc = F16IN ? idesc_f16(128, BN) : idesc_s8(C::TILE_M, BN);
       auto commit = [&](uint64_t* bar) {  // local barrier
@@ -348,6 +373,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, PAIR>::THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue (warps 2..9)
+    pdl_wait();
     const int ew = warp - 2;
     const int q = warp & 3;         // TMEM sub-partition (lanes 32q..32q+31) this warp can read
     const int half = ew >> 2;       // which half of the tile's columns this warp owns
