@@ -15,6 +15,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cstring>
 #include <map>
 #include <mutex>
 #include <vector>
@@ -51,6 +52,10 @@ struct ff_engine {
   std::vector<ff_layer_weights> layers;
   int device = 0;
   int grid = 0, patches = 0, tokens = 0, k_pad = 0;
+  // Separable form of the (window) RoPE tables, when every entry checks out (rope_separable): [cos | sin],
+  // each [32, rope_grid]; nullptr keeps the QKV epilogue on the full tables.
+  float* rope_compact = nullptr;
+  int rope_grid = 0, rope_cls = 0, rope_swap = 0;
   std::map<int, Batch*> batches;
   std::mutex mu;
 };
@@ -68,6 +73,39 @@ struct DeviceScope {
 };
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// The full RoPE tables (angle-major [32, rows], rows = cls + G * G positions) as [32, G] tables of one grid
+// coordinate each: pairs 0..15 follow the row coordinate and 16..31 the column (or the reverse with swap),
+// as the EVA02 and PixAI axial tables are built. Accepted only if every entry of the full tables equals its
+// compact counterpart bit for bit (and the class token's column is the identity), so the QKV epilogue
+// computes exactly what it computes from the full tables. Returns false (no compact form) otherwise.
+bool rope_separable(const std::vector<float>& fc, const std::vector<float>& fs, int rows, int G, int cls, int swap,
+                    std::vector<float>* compact) {
+  if (G <= 0 || rows != cls + G * G) return false;
+  std::vector<float> cc(32 * G), cs(32 * G);
+  for (int j = 0; j < 32; ++j)
+    for (int a = 0; a < G; ++a) {
+      const bool row_coord = (j < 16) != (swap != 0);  // this pair follows the row coordinate
+      const int idx = row_coord ? a * G : a;
+      cc[j * G + a] = fc[static_cast<size_t>(j) * rows + cls + idx];
+      cs[j * G + a] = fs[static_cast<size_t>(j) * rows + cls + idx];
+    }
+  auto same = [](float a, float b) { return std::memcmp(&a, &b, sizeof(float)) == 0; };
+  for (int j = 0; j < 32; ++j) {
+    if (cls && (!same(fc[static_cast<size_t>(j) * rows], 1.f) || !same(fs[static_cast<size_t>(j) * rows], 0.f)))
+      return false;
+    for (int idx = 0; idx < G * G; ++idx) {
+      const int r = idx / G, c = idx % G;
+      const int a = ((j < 16) != (swap != 0)) ? r : c;
+      if (!same(fc[static_cast<size_t>(j) * rows + cls + idx], cc[j * G + a]) ||
+          !same(fs[static_cast<size_t>(j) * rows + cls + idx], cs[j * G + a]))
+        return false;
+    }
+  }
+  compact->assign(cc.begin(), cc.end());
+  compact->insert(compact->end(), cs.begin(), cs.end());
+  return true;
+}
 
 struct Layout {
   size_t images, patches, x, a8, rs, qkv, o, h, cls, logits, top_idx, top_val, pool, total;
@@ -272,6 +310,13 @@ int build_batch(ff_engine* e, int B, ff_engine::Batch** out) {
       p.args.rope_sin = rsin;
       p.args.rope_cols = epi == EPI_QKV_ROPE ? 2 * D : 0;
       p.args.tokens = rope_tokens;
+      if (e->rope_compact && !(pixai(c) && glob)) {  // the table rope_separable checked
+        p.args.rope_grid = e->rope_grid;
+        p.args.rope_cls = e->rope_cls;
+        p.args.rope_swap = e->rope_swap;
+        p.args.rope_cos_c = e->rope_compact;
+        p.args.rope_sin_c = e->rope_compact + 32 * e->rope_grid;
+      }
       return gemm_prepare(p, plan);
     };
     rc = prep(&b->qkv_p[i], lw.qkv_w, lw.qkv_s, lw.qkv_b, b->qkv, 3 * D, D, EPI_QKV_ROPE);
@@ -454,6 +499,29 @@ extern "C" int ff_engine_create(const ff_model_config* cfg, const ff_model_weigh
   e->patches = e->grid * e->grid;
   e->tokens = tokens_of(*cfg);
   e->k_pad = static_cast<int>(align_up(static_cast<size_t>(cfg->patch) * cfg->patch * 3, 64));
+  {
+    // Separable RoPE tables for the QKV epilogue (EVA02's table; PixAI's window table), checked entry by entry.
+    DeviceScope scope(device);
+    const int G = pixai(*cfg) ? cfg->window : e->grid, cls = pixai(*cfg) ? 0 : 1;
+    const int rows = cls + G * G;
+    std::vector<float> fc(static_cast<size_t>(32) * rows), fs(fc.size()), compact;
+    if (G > 0 && cudaMemcpy(fc.data(), w->rope_cos, fc.size() * 4, cudaMemcpyDeviceToHost) == cudaSuccess &&
+        cudaMemcpy(fs.data(), w->rope_sin, fs.size() * 4, cudaMemcpyDeviceToHost) == cudaSuccess) {
+      for (int swap = 0; swap < 2 && e->rope_compact == nullptr; ++swap)
+        if (rope_separable(fc, fs, rows, G, cls, swap, &compact) &&
+            cudaMalloc(&e->rope_compact, compact.size() * 4) == cudaSuccess) {
+          if (cudaMemcpy(e->rope_compact, compact.data(), compact.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess) {
+            e->rope_grid = G;
+            e->rope_cls = cls;
+            e->rope_swap = swap;
+          } else {
+            cudaFree(e->rope_compact);
+            e->rope_compact = nullptr;
+          }
+        }
+    }
+    cudaGetLastError();  // a table that is not separable (or a failed copy) only keeps the full tables
+  }
   *out = e;
   return FF_OK;
 }
@@ -586,6 +654,7 @@ extern "C" int ff_engine_destroy(ff_engine* e) {
       cudaFree(b->block);
       delete b;
     }
+    if (e->rope_compact) cudaFree(e->rope_compact);
   }
   delete e;
   return FF_OK;

@@ -30,6 +30,14 @@ struct GemmArgs {
   const float* rope_cos;   // EPI_QKV_ROPE: angle-major [32, tokens]
   const float* rope_sin;
   int rope_cols;        // EPI_QKV_ROPE: columns [0, rope_cols) are rotated (q and k)
+  // Separable RoPE (rope_grid > 0): the angle of pair i at position p depends on one grid coordinate of p,
+  // so the tables shrink to [32, rope_grid] (a few KB, resident in L1). idx = p - rope_cls (negative: the
+  // class token, identity); (r, c) = (idx / grid, idx % grid); pairs 0..15 take coordinate r and 16..31
+  // coordinate c, or the other way round with rope_swap. The engine builds these from the full tables
+  // only after checking that every full-table entry equals its compact one bit for bit.
+  int rope_grid, rope_cls, rope_swap;
+  const float* rope_cos_c;  // [32, rope_grid]
+  const float* rope_sin_c;
   int tokens;           // tokens per image (RoPE position = m % tokens; stem row remap)
   const float* pos_bias;   // EPI_STEM: [patches, N] = patch bias + position embedding
   int patches;          // EPI_STEM: patches per image

@@ -395,10 +395,36 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, PAIR>::THREADS, 1)
       if constexpr (EPI == EPI_QKV_ROPE) {
         if (tn * BN < args.rope_cols) {
           const int pos = (row_ok ? m : 0) % args.tokens;
+          if (args.rope_grid > 0) {
+            // Separable tables (L1-resident): two coordinates per row instead of a column of the full table.
+            const int idx = pos - args.rope_cls;
+            if (idx < 0) {  // class token: identity rotation, as the full table's first column
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            rope_c[j] = __ldg(args.rope_cos + static_cast<size_t>(j) * args.tokens + pos);
-            rope_s[j] = __ldg(args.rope_sin + static_cast<size_t>(j) * args.tokens + pos);
+              for (int j = 0; j < 32; ++j) {
+                rope_c[j] = 1.f;
+                rope_s[j] = 0.f;
+              }
+            } else {
+              const int G = args.rope_grid, r = idx / G, c = idx - r * G;
+              const int a0 = args.rope_swap ? c : r, a1 = args.rope_swap ? r : c;
+              const float* c0 = args.rope_cos_c + a0;
+              const float* s0 = args.rope_sin_c + a0;
+              const float* c1 = args.rope_cos_c + 16 * G + a1;
+              const float* s1 = args.rope_sin_c + 16 * G + a1;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                rope_c[j] = __ldg(c0 + j * G);
+                rope_s[j] = __ldg(s0 + j * G);
+                rope_c[16 + j] = __ldg(c1 + j * G);
+                rope_s[16 + j] = __ldg(s1 + j * G);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              rope_c[j] = __ldg(args.rope_cos + static_cast<size_t>(j) * args.tokens + pos);
+              rope_s[j] = __ldg(args.rope_sin + static_cast<size_t>(j) * args.tokens + pos);
+            }
           }
         }
       }
