@@ -446,12 +446,20 @@ __global__ void __launch_bounds__(TAILW ? fa::THREADS_TAIL : fa::THREADS, 1)
       };
       auto issue_pv = [&](int i, int j, int c, bool tail, int k0) {  // K steps k0 .. k0 + 3
         const uint32_t sv = smem_u32(smem + OFF_V + (c % STAGES) * TILE);
-        const int steps = tail ? kv_tail_n / 16 : 8;
+        const uint64_t vd = fa::sdesc_mn_sw128(sv + k0 * 2048);
+        const uint32_t d = tmem + t_o(i), a = tmem + t_s(i) + 8 * k0;
+        if (!tail) {  // straight-line issue: no branch between the MMAs
+          mma_f16_ts(d, a, vd, id_o, (j > 0 || k0 > 0) ? 1u : 0u);
 #pragma unroll
-        for (int k = k0; k < k0 + 4; ++k) {  // 16 keys per step: P columns 8k.., V rows 16k..
-          if (k < steps) {
-            const uint32_t acc = (j > 0 || k > 0) ? 1u : 0u;
-            mma_f16_ts(tmem + t_o(i), tmem + t_s(i) + 8 * k, fa::sdesc_mn_sw128(sv + k * 2048), id_o, acc);
+          for (int k = 1; k < 4; ++k) mma_f16_ts(d, a + 8 * k, vd + static_cast<uint64_t>(k * 128), id_o, 1u);
+        } else {
+          const int steps = kv_tail_n / 16;
+#pragma unroll
+          for (int k = k0; k < k0 + 4; ++k) {  // 16 keys per step: P columns 8k.., V rows 16k..
+            if (k < steps) {
+              const uint32_t acc = (j > 0 || k > 0) ? 1u : 0u;
+              mma_f16_ts(tmem + t_o(i), tmem + t_s(i) + 8 * k, fa::sdesc_mn_sw128(sv + k * 2048), id_o, acc);
+            }
           }
         }
       };
