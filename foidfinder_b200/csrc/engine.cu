@@ -53,7 +53,7 @@ struct ff_engine {
   int device = 0;
   int grid = 0, patches = 0, tokens = 0, k_pad = 0;
   // Separable form of the (window) RoPE tables, when every entry checks out (rope_separable): [cos | sin],
-  // each [32, rope_grid]; nullptr keeps the QKV epilogue on the full tables.
+  // each [32, rope_grid + 1]; nullptr keeps the QKV epilogue on the full tables.
   float* rope_compact = nullptr;
   int rope_grid = 0, rope_cls = 0, rope_swap = 0;
   std::map<int, Batch*> batches;
@@ -74,22 +74,27 @@ struct DeviceScope {
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// The full RoPE tables (angle-major [32, rows], rows = cls + G * G positions) as [32, G] tables of one grid
+// The full RoPE tables (angle-major [32, rows], rows = cls + G * G positions) as [32, G + 1] tables of one grid
 // coordinate each: pairs 0..15 follow the row coordinate and 16..31 the column (or the reverse with swap),
-// as the EVA02 and PixAI axial tables are built. Accepted only if every entry of the full tables equals its
-// compact counterpart bit for bit (and the class token's column is the identity), so the QKV epilogue
-// computes exactly what it computes from the full tables. Returns false (no compact form) otherwise.
+// as the EVA02 and PixAI axial tables are built; column G holds the class token's identity rotation.
+// Accepted only if every entry of the full tables equals its compact counterpart bit for bit (and the class
+// token's column is the identity), so the QKV epilogue computes exactly what it computes from the full
+// tables. Returns false (no compact form) otherwise.
 bool rope_separable(const std::vector<float>& fc, const std::vector<float>& fs, int rows, int G, int cls, int swap,
                     std::vector<float>* compact) {
   if (G <= 0 || rows != cls + G * G) return false;
-  std::vector<float> cc(32 * G), cs(32 * G);
-  for (int j = 0; j < 32; ++j)
+  const int W = G + 1;  // column G: the identity rotation of the class token
+  std::vector<float> cc(32 * W), cs(32 * W);
+  for (int j = 0; j < 32; ++j) {
     for (int a = 0; a < G; ++a) {
       const bool row_coord = (j < 16) != (swap != 0);  // this pair follows the row coordinate
       const int idx = row_coord ? a * G : a;
-      cc[j * G + a] = fc[static_cast<size_t>(j) * rows + cls + idx];
-      cs[j * G + a] = fs[static_cast<size_t>(j) * rows + cls + idx];
+      cc[j * W + a] = fc[static_cast<size_t>(j) * rows + cls + idx];
+      cs[j * W + a] = fs[static_cast<size_t>(j) * rows + cls + idx];
     }
+    cc[j * W + G] = 1.f;
+    cs[j * W + G] = 0.f;
+  }
   auto same = [](float a, float b) { return std::memcmp(&a, &b, sizeof(float)) == 0; };
   for (int j = 0; j < 32; ++j) {
     if (cls && (!same(fc[static_cast<size_t>(j) * rows], 1.f) || !same(fs[static_cast<size_t>(j) * rows], 0.f)))
@@ -97,8 +102,8 @@ bool rope_separable(const std::vector<float>& fc, const std::vector<float>& fs, 
     for (int idx = 0; idx < G * G; ++idx) {
       const int r = idx / G, c = idx % G;
       const int a = ((j < 16) != (swap != 0)) ? r : c;
-      if (!same(fc[static_cast<size_t>(j) * rows + cls + idx], cc[j * G + a]) ||
-          !same(fs[static_cast<size_t>(j) * rows + cls + idx], cs[j * G + a]))
+      if (!same(fc[static_cast<size_t>(j) * rows + cls + idx], cc[j * W + a]) ||
+          !same(fs[static_cast<size_t>(j) * rows + cls + idx], cs[j * W + a]))
         return false;
     }
   }
@@ -315,7 +320,7 @@ int build_batch(ff_engine* e, int B, ff_engine::Batch** out) {
         p.args.rope_cls = e->rope_cls;
         p.args.rope_swap = e->rope_swap;
         p.args.rope_cos_c = e->rope_compact;
-        p.args.rope_sin_c = e->rope_compact + 32 * e->rope_grid;
+        p.args.rope_sin_c = e->rope_compact + 32 * (e->rope_grid + 1);
       }
       return gemm_prepare(p, plan);
     };

@@ -36,7 +36,7 @@ struct GemmArgs {
   // coordinate c, or the other way round with rope_swap. The engine builds these from the full tables
   // only after checking that every full-table entry equals its compact one bit for bit.
   int rope_grid, rope_cls, rope_swap;
-  const float* rope_cos_c;  // [32, rope_grid]
+  const float* rope_cos_c;  // [32, rope_grid + 1]: column rope_grid is the identity (class token)
   const float* rope_sin_c;
   int tokens;           // tokens per image (RoPE position = m % tokens; stem row remap)
   const float* pos_bias;   // EPI_STEM: [patches, N] = patch bias + position embedding
