@@ -461,7 +461,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, PAIR>::THREADS, 1)
         // 64 fp16 output columns per chunk; the warp owns HALF columns. The residual epilogue adds the
         // fp16-rounded y to the fp16 stream with a TMA add-reduction (x = fp16(x + fp16(y)), the reference's
         // __hadd2 of the staged fp16 result, foidfinder/backends/cuda/csrc/gemm.cuh:163-169).
-#pragma unroll 1
+#pragma unroll  // unrolled: QKV + RoPE 0.229 -> 0.216 ms at bs64 (rolled, the RoPE branch stayed inside)
         for (int ch = 0; ch < HALF / 64; ++ch) {
           const int c0 = half * HALF + ch * 64;  // tile column of this chunk
           const int n0 = n_tile + c0;
