@@ -144,9 +144,14 @@ constexpr unsigned kPolyChunks = FF_ATTN_POLY_CHUNKS;
 // of that (image, head)'s items bring the same rows into L2 (a tensor-core tile for them
 // would run a whole 128-row query tile for one row; a separate launch re-read all keys and values from
 // HBM). Each quarter-warp (8 lanes x 8 dims = one 128-byte key/value row, coalesced) walks its share of
-// the keys with its own online softmax (running max m, sum l, o over its 8 dims per lane), UNR keys in
-// flight; the partial results are then merged through shared memory. Called by every thread of the tail
-// warps (t = 0 .. 32 kTailWarps - 1), which synchronise among themselves on named barrier 1.
+// the keys (quarter-warp w: keys w, w + 4 kTailWarps, ...) with its own online softmax (running max m, sum
+// l, o over its 8 dims per lane), UNR keys in flight; the partial results are then merged through shared
+// memory in a fixed order. UNR does not change the arithmetic, only how many rows are requested at once:
+//  - UNR = 2 when the tail warps run beside an item's softmax warps (4 measured 0.6% slower there);
+//  - UNR = 8 when they run in CTAs of their own (small batches, fewer items than SMs: there the tail rows
+//    of an item's CTA, ~15 us at UNR = 2 behind the other warps' issue, outlasted the item).
+// Called by every thread of the tail warps (t = 0 .. 32 kTailWarps - 1), which synchronise among
+// themselves on named barrier 1.
 namespace fa {
 constexpr int kTailRows = 4;
 constexpr int kTailWarps = (THREADS_TAIL - THREADS) / 32;
@@ -158,10 +163,10 @@ __device__ __forceinline__ void tail_bar() {
   asm volatile("bar.sync 1, %0;" ::"n"(kTailWarps * 32) : "memory");
 }
 
+template <int UNR>
 __device__ __forceinline__ void attention_tail_rows(const __half* __restrict__ qkv, __half* __restrict__ out, int T,
                                                  int T_main, int heads, float scale_log2, int img, int h, int t) {
   constexpr int NQ = kTailWarps * 4;  // quarter-warps (8 lanes each)
-  constexpr int UNR = 2;              // keys in flight per quarter-warp (4 measured 0.6% slower: code size)
   __shared__ float part_m[NQ], part_l[NQ];
   __shared__ float part_o[NQ][HD];
   const int dim = heads * HD, qw = t >> 3, ql = t & 7;
@@ -183,6 +188,31 @@ __device__ __forceinline__ void attention_tail_rows(const __half* __restrict__ q
     float m = -INFINITY, l = 0.f, o[8];
 #pragma unroll
     for (int d = 0; d < 8; ++d) o[d] = 0.f;
+    // One key of this quarter-warp's chain: its score, then the online-softmax update of m, l and o.
+    auto add_key = [&](const uint4& kr, const uint4& vr) {
+      const uint32_t kw[4] = {kr.x, kr.y, kr.z, kr.w};
+      float sc = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = unpack_half2(kw[e]);
+        sc = fmaf(q[2 * e], f.x, fmaf(q[2 * e + 1], f.y, sc));
+      }
+      sc += __shfl_xor_sync(qmask, sc, 1, 8);
+      sc += __shfl_xor_sync(qmask, sc, 2, 8);
+      sc += __shfl_xor_sync(qmask, sc, 4, 8);
+      const float m_new = fmaxf(m, sc);
+      const float corr = ex2_approx(m - m_new);  // 0 while m is still -inf
+      const float p = ex2_approx(sc - m_new);
+      m = m_new;
+      l = fmaf(l, corr, p);
+      const uint32_t vw[4] = {vr.x, vr.y, vr.z, vr.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = unpack_half2(vw[e]);
+        o[2 * e] = fmaf(p, f.x, o[2 * e] * corr);
+        o[2 * e + 1] = fmaf(p, f.y, o[2 * e + 1] * corr);
+      }
+    };
     for (int k0 = qw; k0 < T; k0 += NQ * UNR) {
       uint4 kr[UNR], vr[UNR];
 #pragma unroll
@@ -194,31 +224,16 @@ __device__ __forceinline__ void attention_tail_rows(const __half* __restrict__ q
           vr[i] = __ldg(reinterpret_cast<const uint4*>(base + 2 * dim) + ql);
         }
       }
+      if (UNR > 2 && k0 + (UNR - 1) * NQ < T) {
+        // every key of the step is valid: no branch between them, so their dot products and shuffles overlap
+        // (with the branches, the dedicated tail CTAs took ~23 us for one row of 1025 keys)
 #pragma unroll
-      for (int i = 0; i < UNR; ++i) {
-        const int key = k0 + i * NQ;
-        if (key >= T) break;  // uniform within the quarter-warp
-        const uint32_t kw[4] = {kr[i].x, kr[i].y, kr[i].z, kr[i].w};
-        float sc = 0.f;
+        for (int i = 0; i < UNR; ++i) add_key(kr[i], vr[i]);
+      } else {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = unpack_half2(kw[e]);
-          sc = fmaf(q[2 * e], f.x, fmaf(q[2 * e + 1], f.y, sc));
-        }
-        sc += __shfl_xor_sync(qmask, sc, 1, 8);
-        sc += __shfl_xor_sync(qmask, sc, 2, 8);
-        sc += __shfl_xor_sync(qmask, sc, 4, 8);
-        const float m_new = fmaxf(m, sc);
-        const float corr = ex2_approx(m - m_new);  // 0 while m is still -inf
-        const float p = ex2_approx(sc - m_new);
-        m = m_new;
-        l = l * corr + p;
-        const uint32_t vw[4] = {vr[i].x, vr[i].y, vr[i].z, vr[i].w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = unpack_half2(vw[e]);
-          o[2 * e] = fmaf(p, f.x, o[2 * e] * corr);
-          o[2 * e + 1] = fmaf(p, f.y, o[2 * e + 1] * corr);
+        for (int i = 0; i < UNR; ++i) {
+          if (k0 + i * NQ >= T) break;  // uniform within the quarter-warp
+          add_key(kr[i], vr[i]);
         }
       }
     }
@@ -305,8 +320,10 @@ __device__ __noinline__ void rescale_o(uint32_t to, float corr) {
 // storing, so the next item's first P V, which overwrites O, waits only for that read. Every barrier
 // phase is counted per CTA (items, tiles), not per item. An item whose second query tile is empty runs
 // that warpgroup's protocol without work (its S and P V are skipped, its barriers still advance).
-template <bool TAILW>
-__global__ void __launch_bounds__(TAILW ? fa::THREADS_TAIL : fa::THREADS, 1)
+// TAIL: 0 no tail rows; 1 tail rows on warps 10-11 of the item CTAs; 2 tail rows in CTAs of their own, the
+// launch's CTAs past the first `items` (one item per CTA: only when there are fewer items than SMs).
+template <int TAIL>
+__global__ void __launch_bounds__(TAIL ? fa::THREADS_TAIL : fa::THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __half* __restrict__ qkv,
                         __half* __restrict__ out, int T, int T_main, int heads, int num_seqs, float scale_log2,
                         int* err) {
@@ -342,6 +359,19 @@ __global__ void __launch_bounds__(TAILW ? fa::THREADS_TAIL : fa::THREADS, 1)
     img = r / heads;
     q0 = pair * 2 * BQ;
   };
+
+  if constexpr (TAIL == 2) {
+    if (static_cast<int>(blockIdx.x) >= items) {  // a tail-row CTA: no TMEM, none of the item pipeline's barriers
+      pdl_wait();
+      pdl_trigger();
+      if (warp < kTailWarps) {
+        const int tails = num_seqs * heads, stride = static_cast<int>(gridDim.x) - items;
+        for (int s = static_cast<int>(blockIdx.x) - items; s < tails; s += stride)
+          attention_tail_rows<8>(qkv, out, T, T_main, heads, scale_log2, s / heads, s % heads, threadIdx.x);
+      }
+      return;
+    }
+  }
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
@@ -566,14 +596,14 @@ __global__ void __launch_bounds__(TAILW ? fa::THREADS_TAIL : fa::THREADS, 1)
     }
   } else if (warp >= 10) {
     // ------------------------------------------------------------ tail query rows (warps 10, 11)
-    if constexpr (TAILW) {
+    if constexpr (TAIL == 1) {
       for (int it = blockIdx.x; it < items; it += gridDim.x) {
         // One item of each (image, head) carries its tail rows, chosen so that they spread evenly over
         // the CTAs (a CTA's items all have the same pair index when the grid is a multiple of n_pairs).
         if (it % n_pairs != (it / n_pairs) % n_pairs) continue;
         int img, h, q0;
         item_of(it, img, h, q0);
-        attention_tail_rows(qkv, out, T, T_main, heads, scale_log2, img, h, threadIdx.x - THREADS);
+        attention_tail_rows<2>(qkv, out, T, T_main, heads, scale_log2, img, h, threadIdx.x - THREADS);
       }
     }
   } else {
@@ -746,8 +776,9 @@ int attention_tc(const void* qkv, void* out, int num_seqs, int seq_len, int head
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !configured[dev]) {
-    if (cudaFuncSetAttribute(attention_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess ||
-        cudaFuncSetAttribute(attention_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess)
+    if (cudaFuncSetAttribute(attention_tc_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess ||
+        cudaFuncSetAttribute(attention_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess ||
+        cudaFuncSetAttribute(attention_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess)
       return check_launch("attention_tc: cudaFuncSetAttribute");
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
@@ -757,13 +788,21 @@ int attention_tc(const void* qkv, void* out, int num_seqs, int seq_len, int head
   FF_REQUIRE(items <= 0x7fffffff, "attention: %lld work items", items);
   const int grid = static_cast<int>(std::min<long long>(items, sm_count()));
   // Tail rows (EVA02's 1025th) run on two extra warps of the same launch; without them the kernel keeps
-  // 320 threads (the extra warps, idle, measured 2.6% slower on 1024-token sequences).
-  if (t_main < seq_len)
-    launch(attention_tc_kernel<true>, dim3(grid), dim3(THREADS_TAIL), SMEM, s, map, static_cast<const __half*>(qkv),
+  // 320 threads (the extra warps, idle, measured 2.6% slower on 1024-token sequences). With fewer items
+  // than SMs the tail rows run in CTAs of their own on the idle SMs instead (same arithmetic, more rows in
+  // flight; see attention_tail_rows), one (image, head) after another.
+  const long long tails = static_cast<long long>(num_seqs) * heads;
+  if (t_main < seq_len && items < sm_count()) {
+    const int tail_ctas = static_cast<int>(std::min<long long>(tails, sm_count() - items));
+    launch(attention_tc_kernel<2>, dim3(static_cast<int>(items) + tail_ctas), dim3(THREADS_TAIL), SMEM, s, map,
+           static_cast<const __half*>(qkv), static_cast<__half*>(out), seq_len, t_main, heads, num_seqs, scale_log2,
+           err);
+  } else if (t_main < seq_len)
+    launch(attention_tc_kernel<1>, dim3(grid), dim3(THREADS_TAIL), SMEM, s, map, static_cast<const __half*>(qkv),
                                                                static_cast<__half*>(out), seq_len, t_main, heads,
                                                                num_seqs, scale_log2, err);
   else
-    launch(attention_tc_kernel<false>, dim3(grid), dim3(THREADS), SMEM, s, map, static_cast<const __half*>(qkv),
+    launch(attention_tc_kernel<0>, dim3(grid), dim3(THREADS), SMEM, s, map, static_cast<const __half*>(qkv),
                                                            static_cast<__half*>(out), seq_len, t_main, heads,
                                                            num_seqs, scale_log2, err);
   return check_launch("attention_tc_kernel");

@@ -158,6 +158,22 @@ def test_attention_matches_oracle(cuda_device, no_device_error, seqs, T, heads, 
     torch.testing.assert_close(out.float().cpu(), ref, atol=4e-3, rtol=1e-2)
 
 
+@pytest.mark.parametrize(("T", "heads", "seqs"), [(1025, 16, 10), (1540, 4, 8)])
+def test_attention_tail_rows_batch_invariant(cuda_device, no_device_error, T, heads, seqs):
+    """A sequence alone (at most one work item per CTA: the tail rows' burst schedule) and the same
+    sequence among others (more items than CTAs: the steady schedule) give the same bits."""
+    from foidfinder_b200 import ops
+
+    g = torch.Generator().manual_seed(T + heads)
+    qkv = torch.randn(seqs * T, 3 * heads * 64, generator=g).half().to(cuda_device)
+    many = torch.empty(seqs * T, heads * 64, dtype=torch.float16, device=cuda_device)
+    one = torch.empty(T, heads * 64, dtype=torch.float16, device=cuda_device)
+    ops.attention(qkv, many, T, heads, scale=0.125)
+    ops.attention(qkv[:T].contiguous(), one, T, heads, scale=0.125)
+    torch.cuda.synchronize()
+    assert torch.equal(one, many[:T])
+
+
 def test_attention_rejects_rope_tables(cuda_device):
     """RoPE belongs to the QKV GEMM epilogue (as in the reference); the attention op refuses tables."""
     from foidfinder_b200 import ops
