@@ -326,7 +326,7 @@ template <int TAIL>
 __global__ void __launch_bounds__(TAIL ? fa::THREADS_TAIL : fa::THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __half* __restrict__ qkv,
                         __half* __restrict__ out, int T, int T_main, int heads, int num_seqs, float scale_log2,
-                        int* err) {
+                        int pair_items, int* err) {
   using namespace fa;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -347,17 +347,31 @@ __global__ void __launch_bounds__(TAIL ? fa::THREADS_TAIL : fa::THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int dim = heads * HD;
   const int n_pairs = (T_main + 2 * BQ - 1) / (2 * BQ);
-  const int items = num_seqs * heads * n_pairs;
+  // Items [0, pair_items) are pairs of query tiles; the pairs after them run as one item per query tile
+  // (TAIL == 2 only: a single round of items; the other instantiations take pairs only).
+  const int items = TAIL == 2 ? pair_items + 2 * (num_seqs * heads * n_pairs - pair_items) : num_seqs * heads * n_pairs;
   const int nkv = (T + BKV - 1) / BKV;
   // The last key tile may be ragged: its S and P V products only cover the first kv_tail_n keys
   // (a multiple of 16; keys past T inside them are masked in the softmax).
   const int kv_tail = T - (nkv - 1) * BKV;
   const int kv_tail_n = (kv_tail + 15) & ~15;
-  auto item_of = [&](int it, int& img, int& h, int& q0) {
-    const int pair = it % n_pairs, r = it / n_pairs;
+  // Item -> (image, head, first query row, whether a second query tile follows). `tail`: the item that
+  // carries its (image, head)'s tail rows on the steady schedule (one per (image, head), spread so that a
+  // CTA's items mostly share the pair index when the grid is a multiple of n_pairs).
+  auto item_of = [&](int it, int& img, int& h, int& q0, bool& two, bool& tail) {
+    int pi = it, tile = 0;
+    if constexpr (TAIL == 2) {
+      if (it >= pair_items) {
+        pi = pair_items + ((it - pair_items) >> 1);
+        tile = (it - pair_items) & 1;
+      }
+    }
+    const int pair = pi % n_pairs, r = pi / n_pairs;
     h = r % heads;
     img = r / heads;
-    q0 = pair * 2 * BQ;
+    q0 = pair * 2 * BQ + tile * BQ;
+    two = (TAIL != 2 || it < pair_items) && q0 + BQ < T_main;
+    tail = pair == r % n_pairs && tile == 0;
   };
 
   if constexpr (TAIL == 2) {
@@ -419,8 +433,8 @@ __global__ void __launch_bounds__(TAIL ? fa::THREADS_TAIL : fa::THREADS, 1)
       int kv_count = 0, n = 0;
       for (int it = blockIdx.x; it < items && ok; it += gridDim.x, ++n) {
         int img, h, q0;
-        item_of(it, img, h, q0);
-        const bool has1 = q0 + BQ < T_main;
+        bool has1, tail;
+        item_of(it, img, h, q0, has1, tail);
         const int qb = n & 1;
         if (n >= 2 && !mbar_wait(&q_empty[qb], static_cast<uint32_t>((n >> 1) - 1) & 1u, abort_flag, err,
                                  kDevTimeoutAttn)) {
@@ -503,10 +517,9 @@ __global__ void __launch_bounds__(TAIL ? fa::THREADS_TAIL : fa::THREADS, 1)
       bool ok = true;
       int kv_count = 0, tiles = 0, n = 0, it = blockIdx.x;
       int img, h, q0;
-      bool has1 = false;
+      bool has1 = false, tail;
       if (it < items) {
-        item_of(it, img, h, q0);
-        has1 = q0 + BQ < T_main;
+        item_of(it, img, h, q0, has1, tail);
         ok = mbar_wait(&q_full[0], 0u, abort_flag, err, kDevTimeoutAttn) && kv_wait(0);
         if (ok) {
           tc_fence_after();
@@ -524,8 +537,7 @@ __global__ void __launch_bounds__(TAIL ? fa::THREADS_TAIL : fa::THREADS, 1)
         bool has1_next = false;
         if (more) {
           int img2, h2, q02;
-          item_of(it_next, img2, h2, q02);
-          has1_next = q02 + BQ < T_main;
+          item_of(it_next, img2, h2, q02, has1_next, tail);
         }
         for (int j = 0; j < nkv; ++j, ++kv_count, ++tiles) {
           const bool last = j == nkv - 1;
@@ -598,11 +610,10 @@ __global__ void __launch_bounds__(TAIL ? fa::THREADS_TAIL : fa::THREADS, 1)
     // ------------------------------------------------------------ tail query rows (warps 10, 11)
     if constexpr (TAIL == 1) {
       for (int it = blockIdx.x; it < items; it += gridDim.x) {
-        // One item of each (image, head) carries its tail rows, chosen so that they spread evenly over
-        // the CTAs (a CTA's items all have the same pair index when the grid is a multiple of n_pairs).
-        if (it % n_pairs != (it / n_pairs) % n_pairs) continue;
         int img, h, q0;
-        item_of(it, img, h, q0);
+        bool two, tail;
+        item_of(it, img, h, q0, two, tail);
+        if (!tail) continue;
         attention_tail_rows<2>(qkv, out, T, T_main, heads, scale_log2, img, h, threadIdx.x - THREADS);
       }
     }
@@ -616,8 +627,9 @@ __global__ void __launch_bounds__(TAIL ? fa::THREADS_TAIL : fa::THREADS, 1)
     int tiles = 0, n = 0;
     for (int it = blockIdx.x; it < items && ok; it += gridDim.x, ++n) {
       int img, h, q0;
-      item_of(it, img, h, q0);
-      const bool active = g == 0 || q0 + BQ < T_main;  // warp-uniform
+      bool two, tail;
+      item_of(it, img, h, q0, two, tail);
+      const bool active = g == 0 || two;  // warp-uniform
       const int row = q0 + g * BQ + q * 32 + lane;
       float m_ref = -INFINITY;
       for (int j = 0; j < nkv; ++j, ++tiles) {
@@ -784,8 +796,17 @@ int attention_tc(const void* qkv, void* out, int num_seqs, int seq_len, int head
   }
   const float scale_log2 = scale * 1.4426950408889634f;
   const int t_main = seq_len - attention_tc_tail_rows(seq_len);
-  const long long items = static_cast<long long>(num_seqs) * heads * ((t_main + 2 * BQ - 1) / (2 * BQ));
-  FF_REQUIRE(items <= 0x7fffffff, "attention: %lld work items", items);
+  const long long pairs = static_cast<long long>(num_seqs) * heads * ((t_main + 2 * BQ - 1) / (2 * BQ));
+  FF_REQUIRE(pairs <= 0x3fffffff, "attention: %lld work items", pairs);
+  const long long sms = sm_count();
+  // Items are pairs of query tiles. With tail rows, when even single query tiles fill less than one round
+  // over the SMs (EVA02-L bs1: 64 pairs, 128 tiles), each tile is an item of its own: 18.9 vs 21.9 us per
+  // bs1 launch. (Single tiles for the pairs left over after full rounds, e.g. bs8's last 68 of 512,
+  // measured slower: 79.2 vs 73.3 us.) Only when every pair holds two tiles; a query tile gives the same
+  // bits either way.
+  const bool singles = t_main < seq_len && t_main % (2 * BQ) == 0 && 2 * pairs < sms;
+  const long long pair_items = singles ? 0 : pairs;
+  const long long items = pair_items + 2 * (pairs - pair_items);
   const int grid = static_cast<int>(std::min<long long>(items, sm_count()));
   // Tail rows (EVA02's 1025th) run on two extra warps of the same launch; without them the kernel keeps
   // 320 threads (the extra warps, idle, measured 2.6% slower on 1024-token sequences). With fewer items
@@ -796,15 +817,15 @@ int attention_tc(const void* qkv, void* out, int num_seqs, int seq_len, int head
     const int tail_ctas = static_cast<int>(std::min<long long>(tails, sm_count() - items));
     launch(attention_tc_kernel<2>, dim3(static_cast<int>(items) + tail_ctas), dim3(THREADS_TAIL), SMEM, s, map,
            static_cast<const __half*>(qkv), static_cast<__half*>(out), seq_len, t_main, heads, num_seqs, scale_log2,
-           err);
+           static_cast<int>(pair_items), err);
   } else if (t_main < seq_len)
     launch(attention_tc_kernel<1>, dim3(grid), dim3(THREADS_TAIL), SMEM, s, map, static_cast<const __half*>(qkv),
                                                                static_cast<__half*>(out), seq_len, t_main, heads,
-                                                               num_seqs, scale_log2, err);
+                                                               num_seqs, scale_log2, static_cast<int>(pair_items), err);
   else
     launch(attention_tc_kernel<0>, dim3(grid), dim3(THREADS), SMEM, s, map, static_cast<const __half*>(qkv),
                                                            static_cast<__half*>(out), seq_len, t_main, heads,
-                                                           num_seqs, scale_log2, err);
+                                                           num_seqs, scale_log2, static_cast<int>(pair_items), err);
   return check_launch("attention_tc_kernel");
 }
 

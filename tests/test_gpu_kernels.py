@@ -119,7 +119,13 @@ def _ref_attention(qkv, seqs, T, heads, scale, rope=None):
                                                           (2, 1025, 16, ("dominant", 64, 128)),
                                                           (1, 1025, 16, ("dominant", 320, 384)),
                                                           (1, 1025, 16, ("dominant", 512, 560)),
-                                                          (2, 1025, 8, "ramp")])
+                                                          (2, 1025, 8, "ramp"),
+                                                          # 512 pairs of query tiles, 3.5 rounds over the
+                                                          # SMs, tail rows on the items' own warps (the cases
+                                                          # above with fewer items put each query tile in
+                                                          # an item of its own and the tail rows in CTAs of
+                                                          # their own)
+                                                          (8, 1025, 16, False)])
 def test_attention_matches_oracle(cuda_device, no_device_error, seqs, T, heads, rope):
     from foidfinder_b200 import ops
 
