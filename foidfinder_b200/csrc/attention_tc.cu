@@ -148,8 +148,8 @@ constexpr unsigned kPolyChunks = FF_ATTN_POLY_CHUNKS;
 // l, o over its 8 dims per lane), UNR keys in flight; the partial results are then merged through shared
 // memory in a fixed order. UNR does not change the arithmetic, only how many rows are requested at once:
 //  - UNR = 2 when the tail warps run beside an item's softmax warps (4 measured 0.6% slower there);
-//  - UNR = 8 when they run in CTAs of their own (small batches, fewer items than SMs: there the tail rows
-//    of an item's CTA, ~15 us at UNR = 2 behind the other warps' issue, outlasted the item).
+//  - UNR = 8 when they run in CTAs of their own (small batches, fewer items than SMs: there, on an item's
+//    CTA at UNR = 2, they kept EVA02-L's bs1 launch at 36 us against 19 us for 1024 tokens).
 // Called by every thread of the tail warps (t = 0 .. 32 kTailWarps - 1), which synchronise among
 // themselves on named barrier 1.
 namespace fa {
@@ -349,7 +349,8 @@ __global__ void __launch_bounds__(TAIL ? fa::THREADS_TAIL : fa::THREADS, 1)
   const int n_pairs = (T_main + 2 * BQ - 1) / (2 * BQ);
   // Items [0, pair_items) are pairs of query tiles; the pairs after them run as one item per query tile
   // (TAIL == 2 only: a single round of items; the other instantiations take pairs only).
-  const int items = TAIL == 2 ? pair_items + 2 * (num_seqs * heads * n_pairs - pair_items) : num_seqs * heads * n_pairs;
+  const int items =
+      TAIL == 2 ? pair_items + 2 * (num_seqs * heads * n_pairs - pair_items) : num_seqs * heads * n_pairs;
   const int nkv = (T + BKV - 1) / BKV;
   // The last key tile may be ragged: its S and P V products only cover the first kv_tail_n keys
   // (a multiple of 16; keys past T inside them are masked in the softmax).
