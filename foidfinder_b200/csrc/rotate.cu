@@ -366,16 +366,19 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     }
     if (!mbar_wait<true>(&bars[wid][b], static_cast<uint32_t>(k >> 1) & 1u, abort_v, err, kDevTimeoutRotate)) break;
     ++waited;
+    // Chunk i's gamma/beta come from a TMEM load issued at chunk i - 1 (chunks are taken in order 0, 1, ...),
+    // so each load's latency overlaps the previous chunk's affine step instead of stalling it.
+    uint32_t gbr[16];
     rot_row<NCH, BLOCK, NORM, true>(buf(b), eps, row, valid_cols, out, row_scale, tbuf + wid * S::SW, lane,
                                     [&](int i, float (&g)[8], float (&bb)[8]) {
-                                      uint32_t r[16];
-                                      tmem_ld16(tmem + 16 * i, r);
+                                      if (i == 0) tmem_ld16(tmem, gbr);
                                       tmem_ld_wait();
 #pragma unroll
                                       for (int e = 0; e < 8; ++e) {
-                                        g[e] = __uint_as_float(r[e]);
-                                        bb[e] = __uint_as_float(r[8 + e]);
+                                        g[e] = __uint_as_float(gbr[e]);
+                                        bb[e] = __uint_as_float(gbr[8 + e]);
                                       }
+                                      if (i + 1 < NCH) tmem_ld16(tmem + 16 * (i + 1), gbr);
                                     });
     __syncwarp();
   }
